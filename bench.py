@@ -1,0 +1,414 @@
+#!/usr/bin/env python3
+"""Benchmark of the GDN-2 token-mixer hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the chunked forward core (kernels (1) chunk-intra +
+(2) chunk-inter with the fused SiLU-gated RMS-norm epilogue) over one batch
+of BASELINE config 2: hidden 2048 = 16 value heads x K = V = 128, B = 8,
+T = 4096, chunk 64, bf16 inputs / f32 state and accumulation.  Inputs are
+seeded synthetic tensors with the module's value laws (L2-normalised q/k,
+sigmoid gates, g = -A dt with A in [1,16], dt in [1e-3, 0.1]); they are
+1.2 GB per step, larger than the 126 MB L2, so no flush is needed.
+
+Printed (rank 0, one JSON line): tokens/s of the device-resident core
+(`value`), the same through the C ABI from pinned host buffers (`e2e`),
+the roofline of the dominant kernel, the decode step of BASELINE config 3
+(B = 256, one token, state [256,16,128,128] f32) as `decode`, the CPU
+baseline (numpy restatement of the crate's tensor path on the host cores)
+and SM clocks sampled during the timed region.
+
+Multi-GPU (torchrun, one rank per GPU): (batch x value-head) chains are
+independent, so each rank runs its own partition of config-2 chains
+(weak scaling, no collective in the timed region); the value is the sum of
+all ranks' tokens over the slowest rank's device time.
+"""
+import argparse
+import ctypes
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "burn-gdn2_b200"))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "src": "measured"}
+    except Exception:
+        return dict(PEAKS_FALLBACK, src="fallback")
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+CFG2 = dict(B=8, HV=16, H=16, T=4096, K=128, V=128, chunk=64)
+CFG3 = dict(B=256, HV=16, H=16, K=128, V=128)
+
+
+def core_bytes_per_token_head(K, V, esize):
+    """Algorithmic HBM bytes per token per value head of the chunk core:
+    q, k, b, v, w, gate read and out written at the input dtype, g in f32
+    (the state read/write once per (b, hv) is amortised and excluded)."""
+    return 3 * K * esize + 4 * K + 4 * V * esize
+
+
+def core_flops_per_token_head(K, V, C):
+    return (6 * C * C * K + 4 * C * C * V + 6 * C * K * V) / C
+
+
+def make_inputs(torch, B, HV, T, K, V, dtype, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def nrm(*s):
+        return torch.randn(*s, generator=g, device=device, dtype=torch.float32)
+
+    def uni(lo, hi, *s):
+        return torch.rand(*s, generator=g, device=device, dtype=torch.float32) * (hi - lo) + lo
+
+    q = nrm(B, T, HV, K)
+    q = q / q.norm(dim=-1, keepdim=True)
+    k = nrm(B, T, HV, K)
+    k = k / k.norm(dim=-1, keepdim=True)
+    A = torch.exp(uni(0.0, math.log(16.0), B, T, HV, K))
+    dt = torch.exp(uni(math.log(1e-3), math.log(0.1), B, T, HV, K))
+    gl = (-A * dt).contiguous()
+    b = torch.sigmoid(nrm(B, T, HV, K))
+    v = nrm(B, T, HV, V)
+    w = torch.sigmoid(nrm(B, T, HV, V))
+    gate = nrm(B, T, HV, V)
+    cast = lambda t: t.to(dtype).contiguous()
+    return dict(q=cast(q), k=cast(k), v=cast(v), g=gl, b=cast(b), w=cast(w), gate=cast(gate))
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import burn_gdn2 as bg
+    from burn_gdn2 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    esize = 2 if dtype == torch.bfloat16 else 4
+    c = CFG2
+    B, HV, T, K, V = c["B"], c["HV"], c["T"], c["K"], c["V"]
+    x = make_inputs(torch, B, HV, T, K, V, dtype, dev, seed=1000 + rank)
+    view = lambda t: t.permute(0, 2, 1, 3)  # [B,T,HV,D] storage -> [B,HV,T,D] view
+    state = torch.zeros(B, HV, K, V, dtype=torch.float32, device=dev)
+    out = torch.empty(B, T, HV, V, dtype=dtype, device=dev)
+    onw = torch.ones(V, dtype=torch.float32, device=dev)
+    a = ops.chunk_args(view(x["q"]), view(x["k"]), view(x["v"]), view(x["g"]), view(x["b"]), view(x["w"]), state,
+                       view(out), K ** -0.5, c["chunk"], num_heads=c["H"], gate=view(x["gate"]),
+                       o_norm_weight=onw, norm_eps=1e-5)
+    ws = ops.chunk_workspace(a, dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    wsp, wsn = ctypes.c_void_p(ws.data_ptr()), ws.numel()
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def step(e0=None, e1=None, e2=None):
+        state.zero_()
+        if e0 is not None:
+            e0.record(stream)
+        bg._lib.check(bg.LIB.gdn2_chunk_intra(ctypes.byref(a), wsp, wsn, sh))
+        if e1 is not None:
+            e1.record(stream)
+        bg._lib.check(bg.LIB.gdn2_chunk_inter(ctypes.byref(a), wsp, wsn, sh))
+        if e2 is not None:
+            e2.record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    evs = [(ev(), ev(), ev()) for _ in range(args.steps)]
+    t_start, t_end = ev(), ev()
+    t_start.record(stream)
+    for e in evs:
+        step(*e)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    barrier()
+    ms_local = t_start.elapsed_time(t_end) / args.steps
+    intra_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in evs) / args.steps
+    inter_ms = sum(e1.elapsed_time(e2) for _, e1, e2 in evs) / args.steps
+    ms = max_over_ranks(ms_local)
+    tokens = B * T
+    value = tokens * world / (ms / 1e3)
+
+    # ---- e2e through the C ABI from pinned host buffers ----
+    host = {n: t.cpu().pin_memory() for n, t in x.items()}
+    dbuf = {n: torch.empty_like(t) for n, t in x.items()}
+    hout = torch.empty(out.shape, dtype=dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = hout.numel() * hout.element_size()
+    a2 = ops.chunk_args(view(dbuf["q"]), view(dbuf["k"]), view(dbuf["v"]), view(dbuf["g"]), view(dbuf["b"]),
+                        view(dbuf["w"]), state, view(out), K ** -0.5, c["chunk"], num_heads=c["H"],
+                        gate=view(dbuf["gate"]), o_norm_weight=onw, norm_eps=1e-5)
+
+    def e2e_step():
+        for n in host:
+            dbuf[n].copy_(host[n], non_blocking=True)
+        state.zero_()
+        bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a2), wsp, wsn, sh))
+        hout.copy_(out, non_blocking=True)
+
+    e2e_steps = max(2, min(args.steps, 5))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    s0, s1 = ev(), ev()
+    s0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s0.elapsed_time(s1) / e2e_steps)
+    e2e_value = tokens * world / (e2e_ms / 1e3)
+    del host, dbuf
+
+    # ---- decode step, BASELINE config 3 (one token, B = 256) ----
+    decode = run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world)
+
+    # ---- roofline of the dominant kernel ----
+    peaks = load_peaks()
+    bpt = core_bytes_per_token_head(K, V, esize)
+    alg_bytes = bpt * tokens * HV
+    dom_name, dom_ms = ("chunk_inter", inter_ms) if inter_ms >= intra_ms else ("chunk_intra", intra_ms)
+    core_ms = intra_ms + inter_ms
+    achieved = alg_bytes / (core_ms / 1e3) / 1e9
+    flops = core_flops_per_token_head(K, V, c["chunk"]) * tokens * HV
+    launches_per_step = 3  # intra, inter, output stage
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "chunk-fwd tokens/s (H2048,T4096); decode tok/s @B256; % TC/HBM roofline",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": args.dtype, "data": "synthetic (seeded, module value laws)",
+            "config": {"workload": "BASELINE config 2 chunked forward core: B=8 (per rank), T=4096, HV=16, "
+                                   "K=V=128, chunk 64, fused gated RMS-norm epilogue",
+                       "global_batch": B * world, "seq_len": T, "parallelism": f"chains x{world} (no collective)",
+                       "l2": "inputs 1.2 GB/step > L2, no flush"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "roofline": {"bound": "hbm", "kernel": "chunk core (intra + inter + epilogue) per step",
+                         "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "peak_src": peaks["src"], "alg_bytes_per_step": alg_bytes,
+                         "tc_frac": flops / (core_ms / 1e3) / (peaks["bf16_tflops"] * 1e12)},
+            "kernels_ms": {"chunk_intra": intra_ms, "chunk_inter_plus_epilogue": inter_ms, "dominant": dom_name},
+            "decode": decode,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+    if world > 1:
+        dist.destroy_process_group()
+    return result
+
+
+def run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world):
+    c = CFG3
+    B, HV, H, K, V = c["B"], c["HV"], c["H"], c["K"], c["V"]
+    gen = torch.Generator(device=dev).manual_seed(7 + rank)
+    f = lambda *s: torch.randn(*s, generator=gen, device=dev, dtype=torch.float32)
+    S = f(B, HV, K, V) * 0.1
+    kd, vd = H * K, HV * V
+    qr, kr, vr = f(B, 1, kd), f(B, 1, kd), f(B, 1, vd)
+    g = -torch.rand(B, 1, kd, generator=gen, device=dev) * 0.5
+    b = torch.rand(B, 1, kd, generator=gen, device=dev)
+    w = torch.rand(B, 1, vd, generator=gen, device=dev)
+    gate = f(B, 1, vd)
+    cq, ck, cv = f(B, 3, kd), f(B, 3, kd), f(B, 3, vd)
+    cw = [torch.rand(n, 4, generator=gen, device=dev) - 0.5 for n in (kd, kd, vd)]
+    onw = torch.ones(V, device=dev)
+    out = torch.empty(B, 1, HV, V, device=dev)
+    to4 = lambda t, n, d: t.reshape(B, 1, n, d).permute(0, 2, 1, 3)
+    a = ops.recurrent_args(to4(qr, H, K), to4(kr, H, K), to4(vr, HV, V), to4(g, H, K), to4(b, H, K),
+                           to4(w, HV, V), S, out.permute(0, 2, 1, 3), K ** -0.5, num_heads=H, grouped=True,
+                           prologue=1, conv_w=cw, conv_in=(cq, ck, cv), conv_out=(cq, ck, cv),
+                           gate=to4(gate, HV, V), o_norm_weight=onw, norm_eps=1e-5)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    run = lambda: bg._lib.check(bg.LIB.gdn2_recurrent_fwd(ctypes.byref(a), sh))
+    for _ in range(max(3, args.warmup)):
+        run()
+    torch.cuda.synchronize()
+    steps = 128  # 128 decode steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    state_bytes = 2 * B * HV * K * V * 4
+    vec_bytes = B * 1 * (3 * kd + 4 * vd) * 4 + B * HV * V * 4 + 2 * B * 3 * (2 * kd + vd) * 4
+    peaks = load_peaks()
+    gbs = (state_bytes + vec_bytes) / (ms / 1e3) / 1e9
+    return {"value": B * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "workload": "BASELINE config 3 decode step: B=256 (per rank), HV=16, K=V=128, state f32 in place, "
+                        "fused short-conv + L2 prologue and gated RMS-norm epilogue",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "bytes_per_step": state_bytes + vec_bytes}}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: numpy restatement of the crate's tensor path (oracle)
+# ---------------------------------------------------------------------------
+def cpu_baseline(budget_s=12.0):
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import gdn2_oracle as O
+
+    c = CFG2
+    Bs, Ts = 1, 256
+    arr = O.make_core_inputs(Bs, c["HV"], Ts, c["K"], c["V"], seed=3, dtype=np.float32)
+    s0 = np.zeros((Bs, c["HV"], c["K"], c["V"]), np.float32)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        o, _ = O.chunk_wy_forward(arr["q"], arr["k"], arr["v"], arr["g"], arr["b"], arr["w"], s0,
+                                  c["K"] ** -0.5, c["chunk"])
+        O.rms_norm_gate_per_head(o.transpose(0, 2, 1, 3), arr["gate"], np.ones(c["V"], np.float32), 1e-5)
+        n += 1
+        el = time.perf_counter() - t0
+        if el > budget_s:
+            break
+    tok_s = n * Bs * Ts / el
+    cores = os.cpu_count()
+    return {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"numpy (OpenBLAS) restatement of chunk_wy_forward + rms_norm_gate, f32, B={Bs} T={Ts} "
+                      f"HV={c['HV']} K=V={c['K']} chunk 64, {n} reps in {el:.1f}s (same op sequence as the "
+                      f"crate's NdArray path; tokens/s scales linearly in B*T)"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    per = []
+    for _ in range(args.warmup):
+        cpu_baseline(budget_s=0.5)
+    for _ in range(args.steps):
+        per.append(cpu_baseline(budget_s=max(2.0, 20.0 / max(1, args.steps))))
+    value = sum(p["value"] for p in per) / len(per)
+    cb = dict(per[-1], value=value)
+    c = CFG2
+    return {"impl": "reference", "metric": "chunk-fwd tokens/s (H2048,T4096); decode tok/s @B256; % TC/HBM roofline",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": c["B"] * c["T"] / value * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, module value laws)",
+            "config": {"workload": "BASELINE config 2 chunked forward core (CPU sample, see cpu_baseline)",
+                       "global_batch": c["B"], "seq_len": c["T"], "parallelism": "host cores"},
+            "cpu_baseline": cb,
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        res = run_reference(args)
+    else:
+        res = run_ours(args)
+        if res is not None and int(os.environ.get("WORLD_SIZE", "1")) == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,218 @@
+"""Functional GDN-2 ops on CUDA tensors, each one C-ABI call into
+libgdn2_b200.so.  Names, argument order and return values mirror the
+reference crate (sehaxe/burn-gdn2 v0.5.1):
+
+  chunk_wy_forward        src/forward.rs:44-278
+  fused_recurrent_forward src/kernel/fused_recurrent.rs:11-56
+  fused_recurrent_gdn2    src/kernel/fused_recurrent.rs:65-108
+  short_conv_1d           src/short_conv.rs:22-65
+  l2_normalize_4d         src/l2norm.rs:13-16
+  rms_norm_gate_per_head  src/module.rs:501-517
+
+Every op requires CUDA tensors and raises if it gets anything else: there is
+no CPU or tensor-op fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import LIB, check
+
+SHORT_CONV_KERNEL = 4  # src/short_conv.rs:5
+SHORT_CONV_CACHE = 3  # src/short_conv.rs:7
+
+_DT = {torch.float32: _lib.GDN2_DTYPE_F32, torch.bfloat16: _lib.GDN2_DTYPE_BF16}
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("burn_gdn2 ops run on the B200 CUDA kernels only; got a CPU tensor")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt not in _DT:
+        raise TypeError(f"unsupported dtype {dt}; use float32 or bfloat16")
+    return _DT[dt]
+
+
+def view4(t: Optional[torch.Tensor]) -> _lib.View:
+    """gdn2_view of a 4-D tensor whose last dim is contiguous."""
+    if t is None:
+        return _lib.View()
+    assert t.dim() == 4, t.shape
+    if t.stride(3) != 1 and t.shape[3] > 1:
+        raise ValueError("last dim must be contiguous")
+    return _lib.View(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+
+def ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_handle(device=None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _last_contig(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    t = t.to(dtype)
+    if t.stride(-1) != 1 and t.shape[-1] > 1:
+        t = t.contiguous()
+    return t
+
+
+def _expand_k(t: torch.Tensor, K: int) -> torch.Tensor:
+    """g / b with a last dim of 1 broadcast over K (``k % g_dim``, src/forward.rs:149,173)."""
+    if t.shape[-1] == K:
+        return t
+    if t.shape[-1] != 1:
+        raise ValueError(f"last dim {t.shape[-1]} must be 1 or {K}")
+    return t.expand(*t.shape[:-1], K).contiguous()
+
+
+def chunk_args(q, k, v, g, b, w, state, out, scale, chunk_size, *, num_heads=None, grouped=False,
+               gate=None, o_norm_weight=None, norm_eps=1e-5) -> _lib.ChunkArgs:
+    """Fill gdn2_chunk_args.  q,k,g,b: [B,Hq,T,K]; v,w,out: [B,HV,T,V];
+    gate: [B,HV,T,V] view or None; state: [B,HV,K,V] f32 contiguous."""
+    B, Hq, T, K = q.shape
+    HV, V = v.shape[1], v.shape[3]
+    a = _lib.ChunkArgs()
+    a.dims = _lib.Dims(B, T, num_heads if num_heads else Hq, HV, K, V)
+    a.chunk_size = int(chunk_size)
+    a.dtype = dtype_code(q.dtype)
+    a.key_heads_grouped = int(grouped)
+    a.fuse_epilogue = int(gate is not None)
+    a.scale = float(scale)
+    a.norm_eps = float(norm_eps)
+    a.q, a.k, a.v, a.g, a.b, a.w = (view4(x) for x in (q, k, v, g, b, w))
+    a.gate = view4(gate)
+    a.o_norm_weight = None if o_norm_weight is None else o_norm_weight.data_ptr()
+    a.state = state.data_ptr()
+    a.out = view4(out)
+    return a
+
+
+def chunk_workspace(a: _lib.ChunkArgs, device) -> torch.Tensor:
+    nbytes = LIB.gdn2_chunk_fwd_workspace_bytes(ctypes.byref(a))
+    return torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+
+
+def chunk_wy_forward(q, k, v, g, b, w, state, scale, chunk_size) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Chunked WY forward (src/forward.rs:44-278) on kernels (1) + (2).
+
+    q,k,g,b: [B,HV,T,K] (g, b may have last dim 1); v,w: [B,HV,T,V];
+    state [B,HV,K,V].  Returns (out [B,HV,T,V] in q's dtype, new state f32).
+    """
+    _require_cuda(q, k, v, g, b, w, state)
+    dt = q.dtype if q.dtype in _DT else torch.float32
+    K = q.shape[3]
+    q, k, v, w = (_last_contig(x, dt) for x in (q, k, v, w))
+    b = _last_contig(_expand_k(b, K), dt)
+    g = _last_contig(_expand_k(g, K), torch.float32)
+    st = state.to(torch.float32).contiguous().clone()
+    B, HV, T, _ = q.shape
+    out = torch.empty(B, HV, T, v.shape[3], dtype=dt, device=q.device)
+    a = chunk_args(q, k, v, g, b, w, st, out, scale, chunk_size)
+    ws = chunk_workspace(a, q.device)
+    check(LIB.gdn2_chunk_fwd(ctypes.byref(a), ptr(ws), ws.numel(), stream_handle(q.device)))
+    return out, st
+
+
+def recurrent_args(q, k, v, g, b, w, state, out, scale, *, num_heads=None, grouped=False, prologue=0,
+                   conv_w=(None, None, None), conv_in=(None, None, None), conv_out=(None, None, None),
+                   gate=None, o_norm_weight=None, norm_eps=1e-5, dtype=None) -> _lib.RecurrentArgs:
+    B, Hq, T, K = q.shape
+    HV, V = v.shape[1], v.shape[3]
+    a = _lib.RecurrentArgs()
+    a.dims = _lib.Dims(B, T, num_heads if num_heads else Hq, HV, K, V)
+    a.dtype = dtype_code(dtype if dtype is not None else q.dtype)
+    a.key_heads_grouped = int(grouped)
+    a.prologue = int(prologue)
+    a.fuse_epilogue = int(gate is not None)
+    a.scale = float(scale)
+    a.norm_eps = float(norm_eps)
+    a.q, a.k, a.v, a.g, a.b, a.w = (view4(x) for x in (q, k, v, g, b, w))
+    a.conv_w_q, a.conv_w_k, a.conv_w_v = (None if x is None else x.data_ptr() for x in conv_w)
+    a.conv_q_in, a.conv_k_in, a.conv_v_in = (None if x is None else x.data_ptr() for x in conv_in)
+    a.conv_q_out, a.conv_k_out, a.conv_v_out = (None if x is None else x.data_ptr() for x in conv_out)
+    a.gate = view4(gate)
+    a.o_norm_weight = None if o_norm_weight is None else o_norm_weight.data_ptr()
+    a.state = state.data_ptr()
+    a.out = view4(out)
+    return a
+
+
+def fused_recurrent_forward(q, k, v, g, b, w, state, scale) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Token-by-token scan (src/kernel/fused_recurrent.rs:11-56) on kernel (3):
+    one launch, state on chip for all T tokens.  Returns (out [B,HV,T,V], state)."""
+    _require_cuda(q, k, v, g, b, w, state)
+    dt = q.dtype if q.dtype in _DT else torch.float32
+    K = q.shape[3]
+    q, k, v, w = (_last_contig(x, dt) for x in (q, k, v, w))
+    b = _last_contig(_expand_k(b, K), dt)
+    g = _last_contig(_expand_k(g, K), torch.float32)
+    st = state.to(torch.float32).contiguous().clone()
+    B, HV, T, _ = q.shape
+    out = torch.empty(B, HV, T, v.shape[3], dtype=dt, device=q.device)
+    a = recurrent_args(q, k, v, g, b, w, st, out, scale)
+    check(LIB.gdn2_recurrent_fwd(ctypes.byref(a), stream_handle(q.device)))
+    return out, st
+
+
+def fused_recurrent_gdn2(q, k, v, g, b, w, state: Optional[torch.Tensor], scale, update_state: bool):
+    """Dispatcher of src/kernel/fused_recurrent.rs:65-108.
+
+    update_state: run the scan (any T; T == 1 is the decode step) and return
+    (out [B,HV,T,V], new state).  Otherwise the read-only branch
+    (:101-104): out = scale * q S, permuted to [B,T,HV,V], state unchanged.
+    """
+    B, HV, T, K = q.shape
+    V = v.shape[3]
+    s = state if state is not None else torch.zeros(B, HV, K, V, device=q.device, dtype=torch.float32)
+    if update_state:
+        return fused_recurrent_forward(q, k, v, g, b, w, s, scale)
+    out = (q.float() @ s * scale).permute(0, 2, 1, 3)
+    return out, s
+
+
+def short_conv_1d(x, weight, cache=None):
+    """Causal depthwise conv (kernel 4) + SiLU (src/short_conv.rs:22-65).
+    x [B,T,C]; weight [C,4]; cache [B,3,C] or None.  Returns (y, new_cache f32)."""
+    _require_cuda(x, weight, cache)
+    dt = x.dtype if x.dtype in _DT else torch.float32
+    x = x.to(dt).contiguous()
+    Bn, T, C = x.shape
+    y = torch.empty_like(x)
+    w32 = weight.to(torch.float32).contiguous()
+    cin = None if cache is None else cache.to(torch.float32).contiguous()
+    cout = torch.empty(Bn, SHORT_CONV_CACHE, C, dtype=torch.float32, device=x.device)
+    check(LIB.gdn2_short_conv(Bn, T, C, dtype_code(dt), ptr(x), ptr(w32), ptr(cin), ptr(cout), ptr(y),
+                              stream_handle(x.device)))
+    return y, cout
+
+
+def l2_normalize_4d(x, eps=1e-6):
+    """x / sqrt(sum_K x^2 + eps) (src/l2norm.rs:13-16)."""
+    xf = x.float()
+    return (xf / torch.sqrt((xf * xf).sum(-1, keepdim=True) + eps)).to(x.dtype)
+
+
+def rms_norm_gate_per_head(x, gate, weight, eps):
+    """x / sqrt(mean_V x^2 + eps) * weight * silu(gate) (src/module.rs:501-517).
+    x, gate: [B,T,HV,V] (any strides with V contiguous); weight [V]."""
+    _require_cuda(x, gate, weight)
+    dt = x.dtype if x.dtype in _DT else torch.float32
+    x = _last_contig(x, dt)
+    gate = _last_contig(gate, dt)
+    B, T, HV, V = x.shape
+    out = torch.empty(B, T, HV, V, dtype=dt, device=x.device)
+    dims = _lib.Dims(B, T, HV, HV, 1, V)
+    w32 = weight.to(torch.float32).contiguous()
+    perm = lambda t: t.permute(0, 2, 1, 3)  # [B,HV,T,V] views
+    check(LIB.gdn2_rms_norm_gate(ctypes.byref(dims), dtype_code(dt), view4(perm(x)), view4(perm(gate)), ptr(w32),
+                                 float(eps), view4(perm(out)), stream_handle(x.device)))
+    return out

@@ -1,0 +1,197 @@
+// C ABI of libgdn2_b200.so (declared in include/gdn2.h): argument checks,
+// error reporting and the launch sequences of the three kernels.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "chunk.cuh"
+#include "common.cuh"
+
+namespace gdn2 {
+
+static thread_local char g_err[512] = "";
+static thread_local int g_cuda_err = 0;
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return GDN2_OK;
+  g_cuda_err = (int)e;
+  return set_error(GDN2_ECUDA, "%s: %s (%d)", where, cudaGetErrorString(e), (int)e);
+}
+
+int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream);
+int launch_short_conv(int B, int Tn, int C, int dtype, const void* x, const float* w, const float* cin, float* cout,
+                      void* y, cudaStream_t st);
+int launch_rms_norm_gate(const gdn2_dims& d, int dtype, const gdn2_view& o, const gdn2_view& gate, const float* w,
+                         float eps, const gdn2_view& out, cudaStream_t st);
+
+static int check_dims(const gdn2_dims& d, const char* fn) {
+  if (d.batch <= 0 || d.seq_len <= 0 || d.num_heads <= 0 || d.num_v_heads <= 0 || d.head_k_dim <= 0 ||
+      d.head_v_dim <= 0)
+    return set_error(GDN2_EINVAL, "%s: all dims must be > 0 (B=%d T=%d H=%d HV=%d K=%d V=%d)", fn, d.batch,
+                     d.seq_len, d.num_heads, d.num_v_heads, d.head_k_dim, d.head_v_dim);
+  if (d.num_v_heads % d.num_heads)
+    return set_error(GDN2_EINVAL, "%s: num_v_heads=%d must be a multiple of num_heads=%d", fn, d.num_v_heads,
+                     d.num_heads);
+  return GDN2_OK;
+}
+
+static int prep_chunk(const gdn2_chunk_args* a, void* ws, size_t wsb, ChunkParams& p, const char* fn) {
+  if (!a) return set_error(GDN2_EINVAL, "%s: null args", fn);
+  int rc = check_dims(a->dims, fn);
+  if (rc) return rc;
+  const gdn2_dims& d = a->dims;
+  if (a->dtype != GDN2_DTYPE_F32 && a->dtype != GDN2_DTYPE_BF16)
+    return set_error(GDN2_EINVAL, "%s: unknown dtype %d", fn, a->dtype);
+  if (a->chunk_size <= 0) return set_error(GDN2_EINVAL, "%s: chunk_size must be > 0, got %d", fn, a->chunk_size);
+  if (!a->q.data || !a->k.data || !a->v.data || !a->g.data || !a->b.data || !a->w.data || !a->state ||
+      !a->out.data)
+    return set_error(GDN2_EINVAL, "%s: null tensor pointer", fn);
+  if (a->fuse_epilogue && (!a->gate.data || !a->o_norm_weight))
+    return set_error(GDN2_EINVAL, "%s: fuse_epilogue needs gate and o_norm_weight", fn);
+  if (((uintptr_t)a->state & 15u) != 0) return set_error(GDN2_EINVAL, "%s: state must be 16-byte aligned", fn);
+  if (d.head_v_dim % 4) return set_error(GDN2_EUNSUPPORTED, "%s: head_v_dim=%d not a multiple of 4", fn, d.head_v_dim);
+  const int C = a->chunk_size < CP ? a->chunk_size : CP;
+  const ChunkWorkspace L = chunk_workspace_layout(d.batch, d.num_v_heads, d.seq_len, d.head_k_dim, d.head_v_dim, C);
+  if (!ws) return set_error(GDN2_EINVAL, "%s: null workspace", fn);
+  if (wsb < L.total * sizeof(float))
+    return set_error(GDN2_EWORKSPACE, "%s: workspace %zu bytes < required %zu", fn, wsb, L.total * sizeof(float));
+  if (((uintptr_t)ws & 255u) != 0) return set_error(GDN2_EINVAL, "%s: workspace must be 256-byte aligned", fn);
+  p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.K = d.head_k_dim; p.V = d.head_v_dim;
+  p.C = C;
+  p.NC = (d.seq_len + C - 1) / C;
+  p.rep = a->key_heads_grouped ? d.num_v_heads / d.num_heads : 1;
+  p.fuse_epilogue = a->fuse_epilogue;
+  p.scale = a->scale; p.eps = a->norm_eps;
+  p.q = make_dview(a->q); p.k = make_dview(a->k); p.v = make_dview(a->v);
+  p.g = make_dview(a->g); p.b = make_dview(a->b); p.w = make_dview(a->w);
+  p.gate = make_dview(a->gate); p.out = make_dview(a->out);
+  p.onw = a->o_norm_weight;
+  p.state = a->state;
+  float* base = static_cast<float*>(ws);
+  p.ws_aqk = base + L.aqk; p.ws_w = base + L.w; p.ws_u = base + L.u;
+  p.ws_qg = base + L.qg; p.ws_kd = base + L.kd; p.ws_gl = base + L.gl; p.ws_o = base + L.o;
+  return GDN2_OK;
+}
+
+}  // namespace gdn2
+
+using namespace gdn2;
+
+extern "C" {
+
+const char* gdn2_last_error(void) { return g_err; }
+int gdn2_last_cuda_error(void) { return g_cuda_err; }
+int gdn2_abi_version(void) { return GDN2_ABI_VERSION; }
+
+size_t gdn2_chunk_fwd_workspace_bytes(const gdn2_chunk_args* a) {
+  if (!a || a->chunk_size <= 0 || a->dims.batch <= 0 || a->dims.seq_len <= 0) return 0;
+  const int C = a->chunk_size < CP ? a->chunk_size : CP;
+  return chunk_workspace_layout(a->dims.batch, a->dims.num_v_heads, a->dims.seq_len, a->dims.head_k_dim,
+                                a->dims.head_v_dim, C)
+             .total *
+         sizeof(float);
+}
+
+int gdn2_chunk_intra(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream) {
+  ChunkParams p;
+  int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_intra");
+  if (rc) return rc;
+  return launch_intra_simt(p, a->dtype, (cudaStream_t)stream);
+}
+
+int gdn2_chunk_inter(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream) {
+  ChunkParams p;
+  int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_inter");
+  if (rc) return rc;
+  rc = launch_inter_simt(p, (cudaStream_t)stream);
+  if (rc) return rc;
+  return launch_chunk_out(p, a->dtype, (cudaStream_t)stream);
+}
+
+int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream) {
+  ChunkParams p;
+  int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_fwd");
+  if (rc) return rc;
+  rc = launch_intra_simt(p, a->dtype, (cudaStream_t)stream);
+  if (rc) return rc;
+  rc = launch_inter_simt(p, (cudaStream_t)stream);
+  if (rc) return rc;
+  return launch_chunk_out(p, a->dtype, (cudaStream_t)stream);
+}
+
+int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, void* stream) {
+  if (!a) return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: null args");
+  return launch_recurrent(a, (cudaStream_t)stream);
+}
+
+int gdn2_short_conv(int32_t batch, int32_t seq_len, int32_t channels, int32_t dtype, const void* x,
+                    const float* weight, const float* cache_in, float* cache_out, void* y, void* stream) {
+  if (batch <= 0 || seq_len <= 0 || channels <= 0) return set_error(GDN2_EINVAL, "gdn2_short_conv: dims must be > 0");
+  if (dtype != GDN2_DTYPE_F32 && dtype != GDN2_DTYPE_BF16)
+    return set_error(GDN2_EINVAL, "gdn2_short_conv: unknown dtype %d", dtype);
+  if (!x || !weight || !y) return set_error(GDN2_EINVAL, "gdn2_short_conv: null pointer");
+  return launch_short_conv(batch, seq_len, channels, dtype, x, weight, cache_in, cache_out, y, (cudaStream_t)stream);
+}
+
+int gdn2_rms_norm_gate(const gdn2_dims* dims, int32_t dtype, gdn2_view o, gdn2_view gate, const float* weight,
+                       float eps, gdn2_view out, void* stream) {
+  if (!dims) return set_error(GDN2_EINVAL, "gdn2_rms_norm_gate: null dims");
+  int rc = check_dims(*dims, "gdn2_rms_norm_gate");
+  if (rc) return rc;
+  if (dtype != GDN2_DTYPE_F32 && dtype != GDN2_DTYPE_BF16)
+    return set_error(GDN2_EINVAL, "gdn2_rms_norm_gate: unknown dtype %d", dtype);
+  if (!o.data || !gate.data || !weight || !out.data) return set_error(GDN2_EINVAL, "gdn2_rms_norm_gate: null pointer");
+  return launch_rms_norm_gate(*dims, dtype, o, gate, weight, eps, out, (cudaStream_t)stream);
+}
+
+int gdn2_config_validate(const gdn2_config* c, char* msg, size_t msg_len) {
+  int rc = GDN2_OK;
+  if (!c) {
+    rc = set_error(GDN2_EINVAL, "null config");
+  } else if (c->hidden_size <= 0) {
+    rc = set_error(GDN2_EINVAL, "hidden_size must be > 0, got %lld", (long long)c->hidden_size);
+  } else if (c->num_heads <= 0) {
+    rc = set_error(GDN2_EINVAL, "num_heads must be > 0, got %lld", (long long)c->num_heads);
+  } else if (c->head_dim <= 0) {
+    rc = set_error(GDN2_EINVAL, "head_dim must be > 0, got %lld", (long long)c->head_dim);
+  } else {
+    const float prod = (float)c->head_dim * c->expand_v;
+    if (!(c->expand_v > 0.0f && prod - floorf(prod) == 0.0f)) {
+      rc = set_error(GDN2_EINVAL,
+                     "expand_v=%g must produce an integer head_v_dim when multiplied by head_dim=%lld (got %g)",
+                     (double)c->expand_v, (long long)c->head_dim, (double)prod);
+    } else if (c->num_v_heads == 0) {
+      rc = set_error(GDN2_EINVAL, "num_v_heads must be > 0, got %lld", (long long)c->num_v_heads);
+    } else if (c->num_v_heads > 0 && c->num_v_heads < c->num_heads) {
+      rc = set_error(GDN2_EINVAL,
+                     "num_v_heads=%lld < num_heads=%lld is not supported; use num_v_heads >= num_heads (GVA "
+                     "repeats key-side heads)",
+                     (long long)c->num_v_heads, (long long)c->num_heads);
+    } else if (c->num_v_heads > 0 && c->num_v_heads % c->num_heads != 0) {
+      rc = set_error(GDN2_EINVAL, "num_v_heads=%lld must be divisible by num_heads=%lld", (long long)c->num_v_heads,
+                     (long long)c->num_heads);
+    } else if (c->chunk_size <= 0) {
+      rc = set_error(GDN2_EINVAL, "chunk_size must be > 0, got %lld", (long long)c->chunk_size);
+    } else if (!(c->norm_eps > 0.0)) {
+      rc = set_error(GDN2_EINVAL, "norm_eps must be > 0, got %g", c->norm_eps);
+    }
+  }
+  if (msg && msg_len) {
+    if (rc)
+      snprintf(msg, msg_len, "%s", g_err);
+    else
+      msg[0] = 0;
+  }
+  return rc;
+}
+
+}  // extern "C"

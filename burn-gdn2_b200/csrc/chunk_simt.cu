@@ -1,0 +1,396 @@
+// Kernels (1) + (2), f32 CUDA-core path: chunk-intra and chunk-inter.
+//
+// This is the exact-f32 path of the chunked forward (src/forward.rs:44-278)
+// and the fallback-free general path for every shape the tensor-core path
+// does not take (chunk sizes other than 64, head dims that are not a
+// multiple of 64).  It follows the reference's tile-local log-space scheme:
+// decay factors are taken relative to the start of each 16-row tile, so no
+// exp() argument exceeds 16 tokens of decay.
+//
+// Workspace (f32), per chunk n = (b*HV + hv)*NC + c, rows padded to CP = 64:
+//   Aqk [CP][CP]  scale * causal (q E)(k/E)^T e_block     (forward.rs:159-187)
+//   W   [CP][K]   (I + Akk)^-1 (b k gamma)                 (forward.rs:189-261)
+//   U   [CP][V]   (I + Akk)^-1 (w v)
+//   Qg  [CP][K]   scale * q gamma                          (forward.rs:266-267)
+//   Kd  [CP][K]   k exp(G_last - G)                        (forward.rs:271-274)
+//   gl  [K]       gamma_last
+//   O   [B,HV,T,V] raw core output (before the epilogue kernel)
+#include "chunk.cuh"
+
+namespace gdn2 {
+
+constexpr int SIMT_THREADS = 256;
+
+// ---------------------------------------------------------------------------
+// chunk-intra: one CTA per (chunk, hv, b)
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(SIMT_THREADS) k_intra_simt(const ChunkParams p) {
+  extern __shared__ float sm[];
+  float* sQs = sm;                  // [KS][CP]  q E
+  float* sKx = sQs + KS * CP;       // [KS][CP]  k / E
+  float* sBs = sKx + KS * CP;       // [KS][CP]  b k E
+  float* seb = sBs + KS * CP;       // [4][4][KS] exp(min(Gb_p - Gb_q, 0))
+  float* sTot = seb + 16 * KS;      // [4][KS] tile sums of g
+  float* sGl = sTot + 4 * KS;       // [KS] G at the last valid row
+  float* sA = sGl + KS;             // [CP][CP+1] Akk
+
+  const int c = blockIdx.x, hv = blockIdx.y, bb = blockIdx.z;
+  const int kh = hv / p.rep;
+  const int t0 = c * p.C;
+  const int cv = min(p.C, p.T - t0);
+  const int K = p.K, V = p.V;
+  const int64_t n = ((int64_t)bb * p.HV + hv) * p.NC + c;
+  float* gAqk = p.ws_aqk + n * CP * CP;
+  float* gW = p.ws_w + n * CP * K;
+  float* gU = p.ws_u + n * CP * V;
+  float* gQg = p.ws_qg + n * CP * K;
+  float* gKd = p.ws_kd + n * CP * K;
+  float* gGl = p.ws_gl + n * K;
+
+  const int tid = threadIdx.x;
+  const int kk = tid % KS, tp = tid / KS;  // channel within slice, 16-row tile
+  const int ti = tid / 16, tj = tid % 16;
+  const int r0 = 4 * ti, s0 = 4 * tj;
+  const bool blk = s0 <= r0 + 3;
+  const int lt = (cv - 1) >> 4, lr = (cv - 1) & 15;  // tile / row of the last valid token
+
+  float aq[4][4], ak[4][4];
+  #pragma unroll
+  for (int i = 0; i < 4; ++i)
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) aq[i][j] = ak[i][j] = 0.f;
+
+  for (int k0 = 0; k0 < K; k0 += KS) {
+    const int kc = k0 + kk;
+    const bool kval = kc < K;
+    float gl[16];
+    float run = 0.f, glast_loc = 0.f;
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int r = tp * 16 + i;
+      const float gv = (kval && r < cv) ? vload<float>(p.g, bb, kh, t0 + r, kc) : 0.f;
+      run += gv;
+      gl[i] = run;
+      if (i == lr) glast_loc = run;
+    }
+    sTot[tp * KS + kk] = run;
+    __syncthreads();
+    float gbp[4];
+    gbp[0] = 0.f;
+    #pragma unroll
+    for (int pp = 1; pp < 4; ++pp) gbp[pp] = gbp[pp - 1] + sTot[(pp - 1) * KS + kk];
+    const float gb = gbp[tp];
+    if (tp == lt) sGl[kk] = gb + glast_loc;
+    #pragma unroll
+    for (int qq = 0; qq < 4; ++qq)
+      if (qq <= tp) seb[(tp * 4 + qq) * KS + kk] = expf(fminf(gb - gbp[qq], 0.f));
+    __syncthreads();
+    const float Glast = sGl[kk];
+    if (tp == 0 && kval) gGl[kc] = expf(Glast);
+    #pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      const int r = tp * 16 + i;
+      const bool rv = kval && r < cv;
+      const float qv = rv ? vload<T>(p.q, bb, kh, t0 + r, kc) : 0.f;
+      const float kv = rv ? vload<T>(p.k, bb, kh, t0 + r, kc) : 0.f;
+      const float bv = rv ? vload<T>(p.b, bb, kh, t0 + r, kc) : 0.f;
+      const float E = expf(gl[i]);
+      const float G = gb + gl[i];
+      const float gam = expf(G);
+      sQs[kk * CP + r] = qv * E;
+      sKx[kk * CP + r] = kv / E;
+      sBs[kk * CP + r] = bv * kv * E;
+      if (kval) {
+        gW[r * K + kc] = bv * kv * gam;
+        gQg[r * K + kc] = qv * gam * p.scale;
+        gKd[r * K + kc] = kv * expf(Glast - G);
+      }
+    }
+    __syncthreads();
+    if (blk) {
+      const float* eb = seb + ((r0 >> 4) * 4 + (s0 >> 4)) * KS;
+      #pragma unroll 4
+      for (int j = 0; j < KS; ++j) {
+        const float4 a = *reinterpret_cast<const float4*>(sQs + j * CP + r0);
+        const float4 bq = *reinterpret_cast<const float4*>(sBs + j * CP + r0);
+        const float4 kx = *reinterpret_cast<const float4*>(sKx + j * CP + s0);
+        const float e = eb[j];
+        const float av[4] = {a.x * e, a.y * e, a.z * e, a.w * e};
+        const float bv[4] = {bq.x * e, bq.y * e, bq.z * e, bq.w * e};
+        const float kvv[4] = {kx.x, kx.y, kx.z, kx.w};
+        #pragma unroll
+        for (int i = 0; i < 4; ++i)
+          #pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            aq[i][jj] += av[i] * kvv[jj];
+            ak[i][jj] += bv[i] * kvv[jj];
+          }
+      }
+    }
+    __syncthreads();
+  }
+
+  #pragma unroll
+  for (int i = 0; i < 4; ++i)
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = r0 + i, s = s0 + j;
+      gAqk[r * CP + s] = (blk && s <= r) ? aq[i][j] * p.scale : 0.f;
+      sA[r * (CP + 1) + s] = (blk && s < r) ? ak[i][j] : 0.f;
+    }
+  for (int idx = tid; idx < CP * V; idx += SIMT_THREADS) {
+    const int r = idx / V, col = idx % V;
+    gU[idx] = r < cv ? vload<T>(p.w, bb, hv, t0 + r, col) * vload<T>(p.v, bb, hv, t0 + r, col) : 0.f;
+  }
+  __syncthreads();
+
+  // (I + Akk) X = RHS by forward substitution, one column per thread.
+  for (int j = tid; j < K + V; j += SIMT_THREADS) {
+    float* base = j < K ? gW + j : gU + (j - K);
+    const int stride = j < K ? K : V;
+    float x[CP];
+    #pragma unroll
+    for (int r = 0; r < CP; ++r) x[r] = base[r * stride];
+    #pragma unroll
+    for (int r = 1; r < CP; ++r) {
+      float acc = x[r];
+      #pragma unroll
+      for (int s = 0; s < r; ++s) acc -= sA[r * (CP + 1) + s] * x[s];
+      x[r] = acc;
+    }
+    #pragma unroll
+    for (int r = 0; r < CP; ++r) base[r * stride] = x[r];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// chunk-inter: one CTA per (value tile, hv, b), sequential over chunks
+// ---------------------------------------------------------------------------
+template <int VT>
+__global__ void __launch_bounds__(SIMT_THREADS) k_inter_simt(const ChunkParams p) {
+  constexpr int CQ = VT / 4;              // float4 column groups
+  constexpr int RT = CP * VT / (SIMT_THREADS * 4);  // rows per thread
+  extern __shared__ float sm[];
+  const int Kp = (p.K + KS - 1) / KS * KS;
+  float* sS = sm;                          // [Kp][VT]
+  float* sW = sS + Kp * VT;                // [CP][KS+1]
+  float* sQ = sW + CP * (KS + 1);          // [CP][KS+1]
+  float* sAq = sQ + CP * (KS + 1);         // [CP][CP+1]
+  float* svn = sAq + CP * (CP + 1);        // [CP][VT]
+
+  const int vt = blockIdx.x, hv = blockIdx.y, bb = blockIdx.z;
+  const int K = p.K, V = p.V;
+  const int col0 = vt * VT;
+  const int tid = threadIdx.x;
+  const int cq = tid % CQ, rb = tid / CQ;
+  const int c4 = col0 + cq * 4;
+  const bool cval = c4 < V;  // V % 4 == 0, so a float4 group is all-in or all-out
+  float* st = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V;
+
+  for (int idx = tid; idx < Kp * CQ; idx += SIMT_THREADS) {
+    const int k = idx / CQ, q4 = idx % CQ;
+    const int col = col0 + q4 * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (k < K && col < V) v = *reinterpret_cast<const float4*>(st + (int64_t)k * V + col);
+    *reinterpret_cast<float4*>(sS + k * VT + q4 * 4) = v;
+  }
+  __syncthreads();
+
+  for (int c = 0; c < p.NC; ++c) {
+    const int t0 = c * p.C;
+    const int cv = min(p.C, p.T - t0);
+    const int64_t n = ((int64_t)bb * p.HV + hv) * p.NC + c;
+    const float* gAqk = p.ws_aqk + n * CP * CP;
+    const float* gW = p.ws_w + n * CP * K;
+    const float* gU = p.ws_u + n * CP * V;
+    const float* gQg = p.ws_qg + n * CP * K;
+    const float* gKd = p.ws_kd + n * CP * K;
+    const float* gGl = p.ws_gl + n * K;
+
+    for (int idx = tid; idx < CP * CP; idx += SIMT_THREADS) sAq[(idx / CP) * (CP + 1) + idx % CP] = gAqk[idx];
+
+    float avn[RT][4], ao[RT][4];
+    #pragma unroll
+    for (int i = 0; i < RT; ++i)
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) avn[i][j] = ao[i][j] = 0.f;
+
+    for (int k0 = 0; k0 < K; k0 += KS) {
+      for (int idx = tid; idx < CP * KS; idx += SIMT_THREADS) {
+        const int r = idx / KS, j = idx % KS;
+        const bool ok = k0 + j < K;
+        sW[r * (KS + 1) + j] = ok ? gW[r * K + k0 + j] : 0.f;
+        sQ[r * (KS + 1) + j] = ok ? gQg[r * K + k0 + j] : 0.f;
+      }
+      __syncthreads();
+      #pragma unroll 4
+      for (int j = 0; j < KS; ++j) {
+        const float4 s4 = *reinterpret_cast<const float4*>(sS + (k0 + j) * VT + cq * 4);
+        #pragma unroll
+        for (int i = 0; i < RT; ++i) {
+          const float wv = sW[(rb * RT + i) * (KS + 1) + j];
+          const float qv = sQ[(rb * RT + i) * (KS + 1) + j];
+          avn[i][0] += wv * s4.x; avn[i][1] += wv * s4.y; avn[i][2] += wv * s4.z; avn[i][3] += wv * s4.w;
+          ao[i][0] += qv * s4.x; ao[i][1] += qv * s4.y; ao[i][2] += qv * s4.z; ao[i][3] += qv * s4.w;
+        }
+      }
+      __syncthreads();
+    }
+    // v_new = U - W S
+    #pragma unroll
+    for (int i = 0; i < RT; ++i) {
+      const int r = rb * RT + i;
+      float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (cval) u = *reinterpret_cast<const float4*>(gU + r * V + c4);
+      *reinterpret_cast<float4*>(svn + r * VT + cq * 4) =
+          make_float4(u.x - avn[i][0], u.y - avn[i][1], u.z - avn[i][2], u.w - avn[i][3]);
+    }
+    __syncthreads();
+    // o = Aqk v_new + scale q gamma S
+    for (int s = 0; s < CP; ++s) {
+      const float4 v4 = *reinterpret_cast<const float4*>(svn + s * VT + cq * 4);
+      #pragma unroll
+      for (int i = 0; i < RT; ++i) {
+        const float a = sAq[(rb * RT + i) * (CP + 1) + s];
+        ao[i][0] += a * v4.x; ao[i][1] += a * v4.y; ao[i][2] += a * v4.z; ao[i][3] += a * v4.w;
+      }
+    }
+    if (cval) {
+      #pragma unroll
+      for (int i = 0; i < RT; ++i) {
+        const int r = rb * RT + i;
+        if (r < cv)
+          *reinterpret_cast<float4*>(p.ws_o + (((int64_t)bb * p.HV + hv) * p.T + t0 + r) * V + c4) =
+              make_float4(ao[i][0], ao[i][1], ao[i][2], ao[i][3]);
+      }
+    }
+    // S <- diag(gamma_last) S + Kd^T v_new
+    for (int k0 = 0; k0 < K; k0 += KS) {
+      for (int idx = tid; idx < CP * KS; idx += SIMT_THREADS) {
+        const int r = idx / KS, j = idx % KS;
+        sW[r * (KS + 1) + j] = (k0 + j < K) ? gKd[r * K + k0 + j] : 0.f;
+      }
+      __syncthreads();
+      float acc[RT][4];
+      #pragma unroll
+      for (int i = 0; i < RT; ++i)
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+      #pragma unroll 4
+      for (int r = 0; r < CP; ++r) {
+        const float4 v4 = *reinterpret_cast<const float4*>(svn + r * VT + cq * 4);
+        #pragma unroll
+        for (int i = 0; i < RT; ++i) {
+          const float kd = sW[r * (KS + 1) + rb * RT + i];
+          acc[i][0] += kd * v4.x; acc[i][1] += kd * v4.y; acc[i][2] += kd * v4.z; acc[i][3] += kd * v4.w;
+        }
+      }
+      #pragma unroll
+      for (int i = 0; i < RT; ++i) {
+        const int k = k0 + rb * RT + i;
+        if (k < K) {
+          const float gk = gGl[k];
+          float4* sp = reinterpret_cast<float4*>(sS + k * VT + cq * 4);
+          float4 s4 = *sp;
+          s4.x = gk * s4.x + acc[i][0]; s4.y = gk * s4.y + acc[i][1];
+          s4.z = gk * s4.z + acc[i][2]; s4.w = gk * s4.w + acc[i][3];
+          *sp = s4;
+        }
+      }
+      __syncthreads();
+    }
+  }
+
+  for (int idx = tid; idx < K * CQ; idx += SIMT_THREADS) {
+    const int k = idx / CQ, q4 = idx % CQ;
+    const int col = col0 + q4 * 4;
+    if (col < V) *reinterpret_cast<float4*>(st + (int64_t)k * V + col) = *reinterpret_cast<const float4*>(sS + k * VT + q4 * 4);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// output stage: out = rms_norm_gate(O) or out = O (dtype conversion)
+// one warp per (b, hv, t) row
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) k_chunk_out(const ChunkParams p) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t nrows = (int64_t)p.B * p.HV * p.T;
+  if (row >= nrows) return;
+  const int t = (int)(row % p.T);
+  const int hv = (int)((row / p.T) % p.HV);
+  const int bb = (int)(row / ((int64_t)p.T * p.HV));
+  const float* o = p.ws_o + row * p.V;
+  float ss = 0.f;
+  for (int c = lane; c < p.V; c += 32) ss += o[c] * o[c];
+  #pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rms = sqrtf(ss / (float)p.V + p.eps);
+  for (int c = lane; c < p.V; c += 32) {
+    float y = o[c];
+    if (p.fuse_epilogue) y = y / rms * p.onw[c] * silu_f(vload<T>(p.gate, bb, hv, t, c));
+    vstore<T>(p.out, bb, hv, t, c, y);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host launchers
+// ---------------------------------------------------------------------------
+size_t simt_smem_intra() { return sizeof(float) * (3 * KS * CP + 16 * KS + 4 * KS + KS + CP * (CP + 1)); }
+
+template <int VT>
+static size_t smem_inter(int K) {
+  const int Kp = (K + KS - 1) / KS * KS;
+  return sizeof(float) * ((size_t)Kp * VT + 2 * CP * (KS + 1) + CP * (CP + 1) + CP * VT);
+}
+
+static int set_smem(const void* fn, size_t bytes) {
+  if (bytes <= 48 * 1024) return GDN2_OK;
+  return check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
+                    "smem attribute");
+}
+
+int launch_intra_simt(const ChunkParams& p, int dtype, cudaStream_t st) {
+  const size_t smem = simt_smem_intra();
+  dim3 grid(p.NC, p.HV, p.B);
+  if (dtype == GDN2_DTYPE_BF16) {
+    int rc = set_smem((const void*)k_intra_simt<__nv_bfloat16>, smem);
+    if (rc) return rc;
+    k_intra_simt<__nv_bfloat16><<<grid, SIMT_THREADS, smem, st>>>(p);
+  } else {
+    int rc = set_smem((const void*)k_intra_simt<float>, smem);
+    if (rc) return rc;
+    k_intra_simt<float><<<grid, SIMT_THREADS, smem, st>>>(p);
+  }
+  return check_cuda(cudaGetLastError(), "chunk intra launch");
+}
+
+template <int VT>
+static int launch_inter_vt(const ChunkParams& p, cudaStream_t st) {
+  const size_t smem = smem_inter<VT>(p.K);
+  int rc = set_smem((const void*)k_inter_simt<VT>, smem);
+  if (rc) return rc;
+  dim3 grid((p.V + VT - 1) / VT, p.HV, p.B);
+  k_inter_simt<VT><<<grid, SIMT_THREADS, smem, st>>>(p);
+  return check_cuda(cudaGetLastError(), "chunk inter launch");
+}
+
+int launch_inter_simt(const ChunkParams& p, cudaStream_t st) {
+  if (p.V <= 16) return launch_inter_vt<16>(p, st);
+  if (p.V <= 64 && p.V % 32 != 0) return launch_inter_vt<16>(p, st);
+  return launch_inter_vt<32>(p, st);
+}
+
+int launch_chunk_out(const ChunkParams& p, int dtype, cudaStream_t st) {
+  const int64_t nrows = (int64_t)p.B * p.HV * p.T;
+  dim3 grid((unsigned)((nrows + 7) / 8));
+  if (dtype == GDN2_DTYPE_BF16)
+    k_chunk_out<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+  else
+    k_chunk_out<float><<<grid, 256, 0, st>>>(p);
+  return check_cuda(cudaGetLastError(), "chunk output launch");
+}
+
+}  // namespace gdn2

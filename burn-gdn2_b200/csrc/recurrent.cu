@@ -1,0 +1,358 @@
+// Kernel (3): fused-recurrent GDN-2 forward / decode step.
+//
+// Replaces gdn2_step_kernel + cuda::fused_step
+// (src/kernel/fused_recurrent_cube.rs:15-57, :108-172) and the tensor-op
+// token loop fused_recurrent_forward (src/kernel/fused_recurrent.rs:11-56).
+//
+// One CTA owns the state slice S[b, hv, :, col0:col0+VT] for the whole
+// call: it is read from HBM once (128-bit loads, one float4 column group per
+// thread, rows strided by RPP), kept in registers across all T tokens and
+// written back once, in place.  Per token (src/kernel/fused_recurrent.rs:36-49):
+//     S <- S diag(e^g);  v_new = w v - (b k)^T S;  S <- S + k v_new^T;
+//     o = scale q^T S
+// is evaluated with a single pass over the registers:
+//     erased = sum_k (b k e^g)_k S[k,:],   qs = sum_k (q e^g)_k S[k,:]
+//     v_new  = w v - erased,              o  = scale (qs + (q.k) v_new)
+//     S      = e^g S + k v_new^T
+// The optional prologue applies the kernel-4 causal short conv + SiLU with
+// the [B,3,C] caches (src/short_conv.rs:22-65) and the per-head L2 norm
+// (src/l2norm.rs:13-16) to the raw projections; the optional epilogue is the
+// SiLU-gated RMS norm (src/module.rs:501-517).
+//
+// Value columns may be split over `vsplit` CTAs.  When several CTAs share a
+// key head's conv cache (GVA, or a V split) and the cache is updated in
+// place, or when a split row needs the RMS epilogue, the sharing CTAs form a
+// thread-block cluster: cache writes wait behind a cluster barrier and the
+// RMS partial sums travel through distributed shared memory.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace gdn2 {
+
+constexpr int REC_THREADS = 256;
+constexpr int REC_MAXP = 16;  // float4 state registers per thread (64 floats)
+
+struct RecParams {
+  int B, T, Hq, HV, K, V;
+  int rep;  // value heads per q/k/g/b head in the views (1 = per value head)
+  int vsplit, VT, CPR, RPP, npass;
+  int prologue, fuse_epilogue;
+  int cluster_x, cluster_y;
+  int conv_sync;  // cluster barrier before in-place conv cache writes
+  float scale, eps;
+  DView q, k, v, g, b, w, gate, out;
+  const float *cwq, *cwk, *cwv;
+  const float *cq_in, *ck_in, *cv_in;
+  float *cq_out, *ck_out, *cv_out;
+  const float* onw;
+  float* state;
+};
+
+// x_pad[j] of src/short_conv.rs:30-55 for one channel: j < 3 comes from the
+// cache (or replicates token 0 when there is none), j >= 3 is token j-3.
+template <typename T>
+__device__ __forceinline__ float conv_pad(const DView& x, const float* cache, int C, int bb, int head, int kk,
+                                          int ch, int j) {
+  if (j >= 3) return vload<T>(x, bb, head, j - 3, kk);
+  if (cache) return cache[((int64_t)bb * 3 + j) * C + ch];
+  return vload<T>(x, bb, head, 0, kk);
+}
+
+template <typename T>
+__device__ __forceinline__ float conv_act(const DView& x, const float* w, const float* cache, int C, int bb, int head,
+                                          int kk, int ch, int t) {
+  float acc = 0.f;
+  #pragma unroll
+  for (int i = 0; i < 4; ++i) acc += conv_pad<T>(x, cache, C, bb, head, kk, ch, t + i) * w[(int64_t)ch * 4 + i];
+  return silu_f(acc);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(REC_THREADS) k_recurrent(const RecParams p) {
+  extern __shared__ float smem[];
+  const int K = p.K, VT = p.VT, RPP = p.RPP;
+  float* sq = smem;
+  float* sk = sq + K;
+  float* seg = sk + K;
+  float* sbk = seg + K;
+  float* sqg = sbk + K;
+  float* svv = sqg + K;
+  float* svn = svv + VT;
+  float* so = svn + VT;
+  float* red = so + VT;             // 2 * RPP * VT
+  float* misc = red + 2 * RPP * VT;  // 32 (block_sum) + 16 (cluster slots)
+
+  const int vs = blockIdx.x, hv = blockIdx.y, bb = blockIdx.z;
+  const int kh = hv / p.rep;
+  const int col0 = vs * VT;
+  const int tid = threadIdx.x;
+  const int cgi = tid % p.CPR, r0 = tid / p.CPR;
+  const bool active = r0 < RPP;
+  const int Cq = p.Hq * K;   // q/k conv channels
+  const int Cv = p.HV * p.V; // v conv channels
+
+  float* st = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * p.V + col0 + cgi * 4;
+  float4 s[REC_MAXP];
+  #pragma unroll
+  for (int i = 0; i < REC_MAXP; ++i) {
+    const int kk = r0 + i * RPP;
+    if (active && i < p.npass && kk < K)
+      s[i] = *reinterpret_cast<const float4*>(st + (int64_t)kk * p.V);
+    else
+      s[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
+  for (int t = 0; t < p.T; ++t) {
+    // ---- prologue: q, k (conv + SiLU + L2 as requested) ----
+    float ssq = 0.f, ssk = 0.f;
+    for (int kk = tid; kk < K; kk += REC_THREADS) {
+      float qv, kv;
+      if (p.prologue == 1) {
+        const int ch = kh * K + kk;
+        qv = conv_act<T>(p.q, p.cwq, p.cq_in, Cq, bb, kh, kk, ch, t);
+        kv = conv_act<T>(p.k, p.cwk, p.ck_in, Cq, bb, kh, kk, ch, t);
+      } else {
+        qv = vload<T>(p.q, bb, kh, t, kk);
+        kv = vload<T>(p.k, bb, kh, t, kk);
+        if (p.prologue == 2) {
+          qv = silu_f(qv);
+          kv = silu_f(kv);
+        }
+      }
+      sq[kk] = qv;
+      sk[kk] = kv;
+      ssq += qv * qv;
+      ssk += kv * kv;
+    }
+    float nq = 1.f, nk = 1.f;
+    if (p.prologue != 0) {
+      nq = sqrtf(block_sum<REC_THREADS>(ssq, misc) + 1e-6f);
+      nk = sqrtf(block_sum<REC_THREADS>(ssk, misc) + 1e-6f);
+    }
+    float pqk = 0.f;
+    for (int kk = tid; kk < K; kk += REC_THREADS) {
+      const float qv = sq[kk] / nq, kv = sk[kk] / nk;
+      const float e = expf(vload<float>(p.g, bb, kh, t, kk));
+      const float bv = vload<T>(p.b, bb, kh, t, kk);
+      sk[kk] = kv;
+      seg[kk] = e;
+      sbk[kk] = bv * kv * e;
+      sqg[kk] = qv * e;
+      pqk += qv * kv;
+    }
+    for (int c = tid; c < VT; c += REC_THREADS) {
+      const int col = col0 + c;
+      float vv;
+      if (p.prologue == 1) {
+        vv = conv_act<T>(p.v, p.cwv, p.cv_in, Cv, bb, hv, col, hv * p.V + col, t);
+      } else {
+        vv = vload<T>(p.v, bb, hv, t, col);
+        if (p.prologue == 2) vv = silu_f(vv);
+      }
+      svv[c] = vload<T>(p.w, bb, hv, t, col) * vv;
+    }
+    const float qk = block_sum<REC_THREADS>(pqk, misc);  // also publishes seg/sbk/sqg/svv
+
+    // ---- one pass over the register-resident state ----
+    float4 pe = make_float4(0.f, 0.f, 0.f, 0.f), pq = pe;
+    #pragma unroll
+    for (int i = 0; i < REC_MAXP; ++i) {
+      const int kk = r0 + i * RPP;
+      if (active && i < p.npass && kk < K) {
+        const float a = sbk[kk], c = sqg[kk];
+        pe.x += a * s[i].x; pe.y += a * s[i].y; pe.z += a * s[i].z; pe.w += a * s[i].w;
+        pq.x += c * s[i].x; pq.y += c * s[i].y; pq.z += c * s[i].z; pq.w += c * s[i].w;
+      }
+    }
+    if (active) {
+      *reinterpret_cast<float4*>(red + r0 * VT + cgi * 4) = pe;
+      *reinterpret_cast<float4*>(red + (RPP + r0) * VT + cgi * 4) = pq;
+    }
+    __syncthreads();
+    for (int c = tid; c < VT; c += REC_THREADS) {
+      float e = 0.f, qs = 0.f;
+      for (int r = 0; r < RPP; ++r) {
+        e += red[r * VT + c];
+        qs += red[(RPP + r) * VT + c];
+      }
+      const float vn = svv[c] - e;
+      svn[c] = vn;
+      so[c] = p.scale * (qs + qk * vn);
+    }
+    __syncthreads();
+    if (active) {
+      const float4 vn = *reinterpret_cast<const float4*>(svn + cgi * 4);
+      #pragma unroll
+      for (int i = 0; i < REC_MAXP; ++i) {
+        const int kk = r0 + i * RPP;
+        if (i < p.npass && kk < K) {
+          const float e = seg[kk], kv = sk[kk];
+          s[i].x = e * s[i].x + kv * vn.x;
+          s[i].y = e * s[i].y + kv * vn.y;
+          s[i].z = e * s[i].z + kv * vn.z;
+          s[i].w = e * s[i].w + kv * vn.w;
+        }
+      }
+    }
+
+    // ---- epilogue ----
+    if (p.fuse_epilogue) {
+      float ss = 0.f;
+      for (int c = tid; c < VT; c += REC_THREADS) ss += so[c] * so[c];
+      float tot = block_sum<REC_THREADS>(ss, misc);
+      if (p.cluster_x > 1) {
+        cg::cluster_group cl = cg::this_cluster();
+        const dim3 ci = cl.block_index();
+        float* slot = misc + 32 + (t & 1) * 8;
+        if (tid == 0) {
+          for (int x = 0; x < p.cluster_x; ++x) {
+            const unsigned rank = x + ci.y * p.cluster_x;
+            float* peer = cl.map_shared_rank(slot, rank);
+            peer[ci.x] = tot;
+          }
+        }
+        cl.sync();
+        tot = 0.f;
+        for (int x = 0; x < p.cluster_x; ++x) tot += slot[x];
+      }
+      const float rms = sqrtf(tot / (float)p.V + p.eps);
+      for (int c = tid; c < VT; c += REC_THREADS) {
+        const int col = col0 + c;
+        const float gt = vload<T>(p.gate, bb, hv, t, col);
+        vstore<T>(p.out, bb, hv, t, col, so[c] / rms * p.onw[col] * silu_f(gt));
+      }
+    } else {
+      for (int c = tid; c < VT; c += REC_THREADS) vstore<T>(p.out, bb, hv, t, col0 + c, so[c]);
+    }
+    __syncthreads();  // so / svn / sk reused by the next token
+  }
+
+  #pragma unroll
+  for (int i = 0; i < REC_MAXP; ++i) {
+    const int kk = r0 + i * RPP;
+    if (active && i < p.npass && kk < K) *reinterpret_cast<float4*>(st + (int64_t)kk * p.V) = s[i];
+  }
+
+  // ---- new conv caches: rows T..T+2 of the padded sequence ----
+  if (p.prologue == 1) {
+    if (p.conv_sync) cg::this_cluster().sync();
+    if (vs == 0 && hv % p.rep == 0) {
+      for (int kk = tid; kk < K; kk += REC_THREADS) {
+        const int ch = kh * K + kk;
+        float xq[3], xk[3];
+        #pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          xq[j] = conv_pad<T>(p.q, p.cq_in, Cq, bb, kh, kk, ch, p.T + j);
+          xk[j] = conv_pad<T>(p.k, p.ck_in, Cq, bb, kh, kk, ch, p.T + j);
+        }
+        #pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          p.cq_out[((int64_t)bb * 3 + j) * Cq + ch] = xq[j];
+          p.ck_out[((int64_t)bb * 3 + j) * Cq + ch] = xk[j];
+        }
+      }
+    }
+    for (int c = tid; c < VT; c += REC_THREADS) {
+      const int col = col0 + c, ch = hv * p.V + col;
+      float xv[3];
+      #pragma unroll
+      for (int j = 0; j < 3; ++j) xv[j] = conv_pad<T>(p.v, p.cv_in, Cv, bb, hv, col, ch, p.T + j);
+      #pragma unroll
+      for (int j = 0; j < 3; ++j) p.cv_out[((int64_t)bb * 3 + j) * Cv + ch] = xv[j];
+    }
+  }
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream) {
+  const gdn2_dims& d = a->dims;
+  if (d.batch <= 0 || d.seq_len <= 0 || d.num_heads <= 0 || d.num_v_heads <= 0 || d.head_k_dim <= 0 ||
+      d.head_v_dim <= 0)
+    return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: all dims must be > 0");
+  if (d.num_v_heads % d.num_heads)
+    return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: num_v_heads %d not a multiple of num_heads %d",
+                     d.num_v_heads, d.num_heads);
+  if (a->dtype != GDN2_DTYPE_F32 && a->dtype != GDN2_DTYPE_BF16)
+    return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: unknown dtype %d", a->dtype);
+  if (a->prologue < 0 || a->prologue > 2) return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: bad prologue");
+  if (!a->q.data || !a->k.data || !a->v.data || !a->g.data || !a->b.data || !a->w.data || !a->state ||
+      !a->out.data)
+    return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: null tensor pointer");
+  if (a->fuse_epilogue && (!a->gate.data || !a->o_norm_weight))
+    return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: epilogue needs gate and o_norm_weight");
+  if (a->prologue == 1 && (!a->conv_w_q || !a->conv_w_k || !a->conv_w_v || !a->conv_q_out || !a->conv_k_out ||
+                           !a->conv_v_out))
+    return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: conv prologue needs weights and output caches");
+  if (!aligned16(a->state)) return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: state must be 16-byte aligned");
+
+  const int K = d.head_k_dim, V = d.head_v_dim;
+  const int rep = a->key_heads_grouped ? d.num_v_heads / d.num_heads : 1;
+  if (V % 4) return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: head_v_dim %d not a multiple of 4", V);
+  int vsplit = 1;
+  while ((int64_t)K * (V / vsplit) > (int64_t)REC_THREADS * 4 * REC_MAXP && (V % (8 * vsplit)) == 0) vsplit *= 2;
+  const int VT = V / vsplit;
+  const int CPR = VT / 4;
+  if (CPR > REC_THREADS) return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: head_v_dim %d too large", V);
+  const int RPP = REC_THREADS / CPR;
+  const int npass = (K + RPP - 1) / RPP;
+  if (npass > REC_MAXP)
+    return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: head %dx%d exceeds the register-resident state", K, V);
+
+  RecParams p;
+  p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.K = K; p.V = V;
+  p.Hq = a->key_heads_grouped ? d.num_heads : d.num_v_heads;
+  p.rep = rep;
+  p.vsplit = vsplit; p.VT = VT; p.CPR = CPR; p.RPP = RPP; p.npass = npass;
+  p.prologue = a->prologue; p.fuse_epilogue = a->fuse_epilogue;
+  p.scale = a->scale; p.eps = a->norm_eps;
+  p.q = make_dview(a->q); p.k = make_dview(a->k); p.v = make_dview(a->v);
+  p.g = make_dview(a->g); p.b = make_dview(a->b); p.w = make_dview(a->w);
+  p.gate = make_dview(a->gate); p.out = make_dview(a->out);
+  p.cwq = a->conv_w_q; p.cwk = a->conv_w_k; p.cwv = a->conv_w_v;
+  p.cq_in = a->conv_q_in; p.ck_in = a->conv_k_in; p.cv_in = a->conv_v_in;
+  p.cq_out = a->conv_q_out; p.ck_out = a->conv_k_out; p.cv_out = a->conv_v_out;
+  p.onw = a->o_norm_weight;
+  p.state = a->state;
+
+  // CTAs that read a key head's conv cache which is overwritten in place
+  // must finish reading before the owner writes: put them in one cluster.
+  const bool shared_inplace = a->prologue == 1 &&
+                              ((a->conv_q_in && a->conv_q_in == a->conv_q_out) ||
+                               (a->conv_k_in && a->conv_k_in == a->conv_k_out));
+  p.cluster_x = (vsplit > 1 && (a->fuse_epilogue || shared_inplace)) ? vsplit : 1;
+  p.cluster_y = (shared_inplace && rep > 1) ? rep : 1;
+  p.conv_sync = shared_inplace && p.cluster_x * p.cluster_y > 1;
+  if (p.cluster_x * p.cluster_y > 8)
+    return set_error(GDN2_EUNSUPPORTED,
+                     "gdn2_recurrent_fwd: %d CTAs share one conv cache updated in place (max 8); pass separate "
+                     "conv_*_out buffers",
+                     p.cluster_x * p.cluster_y);
+
+  const size_t smem = sizeof(float) * (5 * (size_t)K + 3 * (size_t)VT + 2 * (size_t)RPP * VT + 48);
+  void (*fn)(const RecParams) = a->dtype == GDN2_DTYPE_BF16 ? k_recurrent<__nv_bfloat16> : k_recurrent<float>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_fwd: smem attribute");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(vsplit, d.num_v_heads, d.batch);
+  cfg.blockDim = dim3(REC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (p.cluster_x * p.cluster_y > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.cluster_x;
+    attr[0].val.clusterDim.y = p.cluster_y;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return check_cuda(cudaLaunchKernelEx(&cfg, fn, p), "gdn2_recurrent_fwd launch");
+}
+
+}  // namespace gdn2

@@ -1,0 +1,202 @@
+/*
+ * gdn2.h — C ABI of the B200 (sm_100a) GDN-2 token-mixer hot path.
+ *
+ * Drop-in boundary for sehaxe/burn-gdn2 v0.5.1: the crate's host code
+ * (Rust) binds these `extern "C"` symbols in place of its cubecl kernels
+ * and tensor-op loops.  Plain pointers, sizes and strides only; no CUDA or
+ * torch types (a `void* stream` is a `cudaStream_t`).
+ *
+ * Conventions
+ *  - Every entry point returns 0 (GDN2_OK) or a positive gdn2_status.  It
+ *    never aborts and never falls back to another implementation; a config
+ *    the kernels do not implement returns GDN2_EUNSUPPORTED.  The message
+ *    of the last failure on the calling thread is gdn2_last_error().
+ *  - Device pointers are caller-owned.  Launches are asynchronous on the
+ *    given stream.  Calls on different streams are independent; the only
+ *    hidden state is a lazily built per-device attribute cache.
+ *  - Tensors are passed as gdn2_view: a 4-D view [d0][d1][d2][d3] whose
+ *    last dim is contiguous and whose first three dims have arbitrary
+ *    element strides, so the reference's permuted [B,T,H,K] -> [B,H,T,K]
+ *    projections (src/module.rs:395-398) need no copy.
+ *  - g (log decay) and the recurrent state are always f32; q k v b w gate
+ *    out use `dtype` (f32 or bf16); accumulation is f32.
+ */
+#ifndef GDN2_H
+#define GDN2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN2_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GDN2_API __attribute__((visibility("default")))
+#else
+#define GDN2_API
+#endif
+
+typedef enum gdn2_status {
+  GDN2_OK = 0,
+  GDN2_EINVAL = 1,        /* null pointer, bad shape / stride / alignment */
+  GDN2_EUNSUPPORTED = 2,  /* valid but not implemented (reported, never downgraded) */
+  GDN2_ECUDA = 3,         /* CUDA runtime error, see gdn2_last_cuda_error() */
+  GDN2_EWORKSPACE = 4     /* workspace smaller than *_workspace_bytes() */
+} gdn2_status;
+
+typedef enum gdn2_dtype { GDN2_DTYPE_F32 = 0, GDN2_DTYPE_BF16 = 1 } gdn2_dtype;
+
+/* 4-D view [d0][d1][d2][d3], d3 contiguous; strides in elements. */
+typedef struct gdn2_view {
+  void* data;
+  int64_t stride0, stride1, stride2;
+} gdn2_view;
+
+/* Sizes of one layer call.  H key heads, HV value heads (HV % H == 0). */
+typedef struct gdn2_dims {
+  int32_t batch;       /* B */
+  int32_t seq_len;     /* T */
+  int32_t num_heads;   /* H  */
+  int32_t num_v_heads; /* HV */
+  int32_t head_k_dim;  /* K */
+  int32_t head_v_dim;  /* V */
+} gdn2_dims;
+
+/* ------------------------------------------------------------------------
+ * Chunked forward: kernels (1) chunk-intra and (2) chunk-inter + epilogue.
+ * Replaces chunk_wy_forward (src/forward.rs:44-278, called from
+ * src/module.rs:269-285 and :354-365) and the unwired cubecl pair
+ * cuda::fused_chunk_forward (src/kernel/chunk_cube.rs:781-952).
+ *
+ *   q, k, b : [B, Hq, T, K] views   (dtype)       Hq = H if key_heads_grouped else HV
+ *   g       : [B, Hq, T, K] view    (f32)
+ *   v, w    : [B, HV, T, V] views   (dtype)
+ *   gate    : [B, HV, T, V] view    (dtype; the module's [B,T,HV,V] storage)
+ *   state   : [B, HV, K, V] f32 contiguous, read then overwritten in place
+ *   out     : [B, HV, T, V] view    (dtype)
+ * key_heads_grouped = 1: value head hv reads key-side head hv / (HV/H)
+ * (no materialised GVA repeat).  = 0: the caller passes per-value-head
+ * tensors (e.g. the reference's own repeat, src/module.rs:457-468).
+ * fuse_epilogue = 1: out = rms_norm_gate_per_head(o, gate, o_norm_weight,
+ * norm_eps) (src/module.rs:501-517); = 0: out = o.
+ * chunk_size: any value >= 1 (the tuned path is 64).
+ * ---------------------------------------------------------------------- */
+typedef struct gdn2_chunk_args {
+  gdn2_dims dims;
+  int32_t chunk_size;
+  int32_t dtype;
+  int32_t key_heads_grouped;
+  int32_t fuse_epilogue;
+  float scale;
+  float norm_eps;
+  gdn2_view q, k, v, g, b, w;
+  gdn2_view gate;
+  const float* o_norm_weight; /* [V] */
+  float* state;
+  gdn2_view out;
+} gdn2_chunk_args;
+
+/* Bytes of device workspace gdn2_chunk_fwd / _intra / _inter need. */
+GDN2_API size_t gdn2_chunk_fwd_workspace_bytes(const gdn2_chunk_args* args);
+
+/* Full chunked forward (intra, inter, epilogue) on `stream`. */
+GDN2_API int gdn2_chunk_fwd(const gdn2_chunk_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Diagnostics / profiling: the two phases separately.  gdn2_chunk_intra
+ * fills the workspace with the per-chunk WY factors; gdn2_chunk_inter
+ * consumes them, runs the cross-chunk recurrence and writes out + state.
+ * Replaces gdn2_chunk_intra_kernel (src/kernel/chunk_cube.rs:27-295, host
+ * :817-887) and gdn2_chunk_inter_kernel (:300-610, host :889-917). */
+GDN2_API int gdn2_chunk_intra(const gdn2_chunk_args* args, void* workspace, size_t workspace_bytes, void* stream);
+GDN2_API int gdn2_chunk_inter(const gdn2_chunk_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused recurrent forward: kernel (3).  T >= 1 tokens in one launch with
+ * the state held on chip; T == 1 is the decode step.  Replaces
+ * fused_recurrent_forward (src/kernel/fused_recurrent.rs:11-56), the decode
+ * dispatch fused_recurrent_gdn2 (:65-108) and cuda::fused_step /
+ * gdn2_step_kernel (src/kernel/fused_recurrent_cube.rs:15-57, :108-172).
+ *
+ * prologue = 0: q,k,v are final activations (q,k L2-normalised).
+ * prologue = 1: q,k,v are the raw projections ([B,T,C] storage viewed as
+ *   [B,Hq,T,K] / [B,HV,T,V]); the kernel applies the kernel-4 causal short
+ *   conv + SiLU (src/short_conv.rs:22-65) with the [B,3,C] f32 caches
+ *   (conv_*_in NULL = replicate the first token, :42-54) and writes the new
+ *   caches to conv_*_out (may alias conv_*_in), then L2-normalises q and k
+ *   per head with eps 1e-6 inside the sqrt (src/l2norm.rs:13-16).
+ * prologue = 2: SiLU + L2 only (use_short_conv = false, src/module.rs:415).
+ * g, b, w are always final (g = log decay, f32).
+ * ---------------------------------------------------------------------- */
+typedef struct gdn2_recurrent_args {
+  gdn2_dims dims;
+  int32_t dtype;
+  int32_t key_heads_grouped;
+  int32_t prologue;
+  int32_t fuse_epilogue;
+  float scale;
+  float norm_eps;
+  gdn2_view q, k, v, g, b, w;
+  const float* conv_w_q; /* [Hq*K, 4] */
+  const float* conv_w_k; /* [Hq*K, 4] */
+  const float* conv_w_v; /* [HV*V, 4] */
+  const float* conv_q_in;
+  const float* conv_k_in;
+  const float* conv_v_in;
+  float* conv_q_out;
+  float* conv_k_out;
+  float* conv_v_out;
+  gdn2_view gate;
+  const float* o_norm_weight;
+  float* state; /* [B,HV,K,V] f32, updated in place */
+  gdn2_view out;
+} gdn2_recurrent_args;
+
+GDN2_API int gdn2_recurrent_fwd(const gdn2_recurrent_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Standalone pieces of the layer around the core.
+ * ---------------------------------------------------------------------- */
+/* short_conv_1d (src/short_conv.rs:22-65): y = silu(causal conv4(x)).
+ * x, y: [B,T,C] contiguous (dtype); weight [C,4] f32; cache_in [B,3,C] f32
+ * or NULL (replicate first token); cache_out [B,3,C] f32 or NULL. */
+GDN2_API int gdn2_short_conv(int32_t batch, int32_t seq_len, int32_t channels, int32_t dtype, const void* x,
+                    const float* weight, const float* cache_in, float* cache_out, void* y, void* stream);
+
+/* rms_norm_gate_per_head (src/module.rs:501-517) on [B,HV,T,V] views. */
+GDN2_API int gdn2_rms_norm_gate(const gdn2_dims* dims, int32_t dtype, gdn2_view o, gdn2_view gate,
+                       const float* weight, float eps, gdn2_view out, void* stream);
+
+/* Mirror of Gdn2Config (src/config.rs:24-58) and its validate()
+ * (src/config.rs:71-111).  num_v_heads < 0 means None; min_decay < 0
+ * means None; mode 0 = FusedRecurrent, 1 = Chunk. */
+typedef struct gdn2_config {
+  int64_t hidden_size;
+  int64_t num_heads;
+  int64_t head_dim;
+  float expand_v;
+  int64_t num_v_heads;
+  int32_t use_short_conv;
+  int32_t allow_neg_eigval;
+  double norm_eps;
+  int32_t mode;
+  int64_t chunk_size;
+  double min_decay;
+} gdn2_config;
+
+/* Returns GDN2_OK or GDN2_EINVAL with the reference's panic message in
+ * msg (and in gdn2_last_error()). */
+GDN2_API int gdn2_config_validate(const gdn2_config* cfg, char* msg, size_t msg_len);
+
+/* Error / version queries. */
+GDN2_API const char* gdn2_last_error(void);
+GDN2_API int gdn2_last_cuda_error(void);
+GDN2_API int gdn2_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN2_H */

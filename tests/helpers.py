@@ -1,0 +1,48 @@
+"""Shared test helpers: tolerances of the north star and golden loading."""
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+# f32: rel 1e-3 / abs 1e-4 (elementwise |a-b| <= 1e-4 + 1e-3 |b|)
+F32_TOL = dict(rtol=1e-3, atol=1e-4)
+# bf16 inputs with f32 accumulation: rel 2e-2; the absolute floor is 2e-2 of
+# the reference's RMS so that entries crossing zero are judged on scale.
+BF16_RTOL = 2e-2
+
+
+def max_violation(a, b, rtol, atol):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.max(np.abs(a - b) - (atol + rtol * np.abs(b)))) if a.size else -1.0
+
+
+def assert_close(a, b, rtol, atol, what=""):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    assert a.shape == b.shape, (what, a.shape, b.shape)
+    assert np.all(np.isfinite(a)), f"{what}: non-finite values"
+    err = np.abs(a - b)
+    lim = atol + rtol * np.abs(b)
+    bad = err > lim
+    if bad.any():
+        i = np.unravel_index(np.argmax(err - lim), err.shape)
+        raise AssertionError(f"{what}: {int(bad.sum())}/{a.size} outside tol; worst at {i}: got {a[i]:.6g} "
+                             f"want {b[i]:.6g} (|d|={err[i]:.3g}, lim={lim[i]:.3g}); max|d|={err.max():.3g}")
+
+
+def assert_close_bf16(a, b, what=""):
+    b64 = np.asarray(b, dtype=np.float64)
+    rms = float(np.sqrt(np.mean(b64 * b64))) if b64.size else 0.0
+    assert_close(a, b, BF16_RTOL, BF16_RTOL * rms, what)
+
+
+def load_golden(name):
+    z = np.load(os.path.join(GOLDEN, name))
+    cfg = dict(hidden_size=int(z["D"]), num_heads=int(z["H"]), head_dim=int(z["HK"]), num_v_heads=int(z["HV"]),
+               expand_v=float(z["EXPAND_V"]), use_short_conv=bool(z["USE_SHORT_CONV"]),
+               allow_neg_eigval=bool(z["ALLOW_NEG_EIGVAL"]), norm_eps=float(z["EPS"]))
+    weights = {k: z[k] for k in z.files if not k.startswith(("x_", "y_")) and z[k].ndim > 0}
+    cases = [(z[f"x_{i:03d}"], z[f"y_{i:03d}"]) for i in range(int(z["n_cases"]))]
+    return cfg, weights, cases

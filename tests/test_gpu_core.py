@@ -1,0 +1,213 @@
+"""GPU parity of the core kernels against the CPU oracle (float64), through
+the C ABI (burn_gdn2.ops -> libgdn2_b200.so).
+
+Tolerances (north star): f32 inputs rel 1e-3 / abs 1e-4; bf16 inputs with
+f32 accumulation rel 2e-2 (absolute floor 2e-2 x RMS of the reference).
+bf16 cases feed the oracle the same bf16-rounded inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import gdn2_oracle as O
+from helpers import F32_TOL, assert_close, assert_close_bf16
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _to_dev(arrs, dtype):
+    return {k: torch.tensor(v, dtype=torch.float32 if k == "g" else dtype, device=DEV) for k, v in arrs.items()}
+
+
+def _oracle_inputs(dev_arrs):
+    return {k: v.detach().float().cpu().numpy().astype(np.float64) for k, v in dev_arrs.items()}
+
+
+def _check(got, want, dtype, what):
+    if dtype == torch.float32:
+        assert_close(got, want, what=what, **F32_TOL)
+    else:
+        assert_close_bf16(got, want, what=what)
+
+
+CORE_SHAPES = [
+    # B, HV, T, K, V
+    (2, 3, 96, 8, 8),
+    (2, 3, 130, 16, 8),
+    (1, 4, 70, 16, 24),
+    (1, 2, 200, 64, 64),
+    (1, 2, 129, 128, 128),
+    (1, 2, 100, 128, 256),
+]
+
+
+@pytest.mark.parametrize("shape", CORE_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fused_recurrent_matches_oracle(shape, dtype):
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = shape
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=11, dtype=np.float32)
+    d = _to_dev({k: arrs[k] for k in "qkvgbw"}, dtype)
+    s0 = np.random.default_rng(12).standard_normal((B, HV, K, V)).astype(np.float32)
+    o, s = bg.fused_recurrent_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"],
+                                      torch.tensor(s0, device=DEV), K ** -0.5)
+    ref = _oracle_inputs(d)
+    o_ref, s_ref = O.fused_recurrent_forward(ref["q"], ref["k"], ref["v"], ref["g"], ref["b"], ref["w"],
+                                             s0.astype(np.float64), K ** -0.5)
+    _check(o.float().cpu().numpy(), o_ref, dtype, "out")
+    _check(s.cpu().numpy(), s_ref, torch.float32 if dtype == torch.float32 else dtype, "state")
+
+
+@pytest.mark.parametrize("shape", CORE_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("chunk", [64, 16])
+def test_chunk_matches_oracle(shape, dtype, chunk):
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = shape
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=21, dtype=np.float32)
+    d = _to_dev({k: arrs[k] for k in "qkvgbw"}, dtype)
+    s0 = np.random.default_rng(22).standard_normal((B, HV, K, V)).astype(np.float32)
+    o, s = bg.chunk_wy_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"],
+                               torch.tensor(s0, device=DEV), K ** -0.5, chunk)
+    ref = _oracle_inputs(d)
+    o_ref, s_ref = O.chunk_wy_forward(ref["q"], ref["k"], ref["v"], ref["g"], ref["b"], ref["w"],
+                                      s0.astype(np.float64), K ** -0.5, chunk)
+    _check(o.float().cpu().numpy(), o_ref, dtype, "out")
+    _check(s.cpu().numpy(), s_ref, dtype, "state")
+
+
+@pytest.mark.parametrize("decay", [(-0.3, -0.02), (-5.0, -0.5)])
+@pytest.mark.parametrize("chunk", [16, 64, 4, 30])
+def test_stable_chunk_gpu(decay, chunk):
+    """tests/stable_chunk.rs:11-72 on the GPU: scalar-broadcast g and b
+    ([B,H,T,1]), chunk sizes 16 and 64 (plus 4 and 30), scale 1, 1e-3."""
+    import burn_gdn2 as bg
+
+    rng = np.random.default_rng(31)
+    B, H, T, K, V = 2, 3, 96, 8, 8
+    q = rng.standard_normal((B, H, T, K))
+    kr = rng.standard_normal((B, H, T, K))
+    k = kr / np.sqrt((kr * kr).sum(-1, keepdims=True))
+    v = rng.standard_normal((B, H, T, V))
+    g = rng.uniform(decay[0], decay[1], (B, H, T, 1))
+    b = rng.uniform(0.0, 1.0, (B, H, T, 1))
+    w = rng.standard_normal((B, H, T, V))
+    t = lambda x: torch.tensor(x, dtype=torch.float32, device=DEV)
+    s0 = np.zeros((B, H, K, V))
+    o_ref, s_ref = O.fused_recurrent_forward(q, k, v, g, b, w, s0, 1.0)
+    o, s = bg.chunk_wy_forward(t(q), t(k), t(v), t(g), t(b), t(w), t(s0), 1.0, chunk)
+    assert np.abs(o.cpu().numpy() - o_ref).max() < 1e-3
+    assert np.abs(s.cpu().numpy() - s_ref).max() < 1e-3
+    o2, s2 = bg.fused_recurrent_forward(t(q), t(k), t(v), t(g), t(b), t(w), t(s0), 1.0)
+    assert np.abs(o2.cpu().numpy() - o_ref).max() < 1e-3
+
+
+def test_chunk_real_decay_t130_gpu():
+    """tests/test_chunk.rs:200-256: T=130 (partial chunk), per-channel decay
+    U(-0.15,-0.01), K=16, V=8, random S0, scale 0.125; 1e-4."""
+    import burn_gdn2 as bg
+
+    rng = np.random.default_rng(41)
+    B, H, T, K, V = 2, 3, 130, 16, 8
+    g = rng.uniform(-0.15, -0.01, (B, H, T, K))
+    q = rng.standard_normal((B, H, T, K))
+    kr = rng.standard_normal((B, H, T, K))
+    k = kr / np.sqrt((kr ** 2).sum(-1, keepdims=True))
+    v = rng.standard_normal((B, H, T, V))
+    e = rng.uniform(0.0, 1.0, (B, H, T, K))
+    w = rng.standard_normal((B, H, T, V))
+    s0 = rng.standard_normal((B, H, K, V))
+    t = lambda x: torch.tensor(x, dtype=torch.float32, device=DEV)
+    o_ref, s_ref = O.fused_recurrent_forward(q, k, v, g, e, w, s0, 0.125)
+    o, s = bg.chunk_wy_forward(t(q), t(k), t(v), t(g), t(e), t(w), t(s0), 0.125, 64)
+    assert np.abs(o.cpu().numpy() - o_ref).max() < 1e-4
+    assert np.abs(s.cpu().numpy() - s_ref).max() < 1e-4
+
+
+def test_decode_steps_equal_chunked_forward():
+    """North star: token-by-token decode reproduces one chunked forward
+    (f32, rel 1e-3 / abs 1e-4), here at K = V = 128 over 3 chunks."""
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = 2, 4, 150, 128, 128
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=51, dtype=np.float32)
+    d = _to_dev({k: arrs[k] for k in "qkvgbw"}, torch.float32)
+    s0 = torch.zeros(B, HV, K, V, device=DEV)
+    oc, sc = bg.chunk_wy_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], s0, K ** -0.5, 64)
+    st = s0.clone()
+    outs = []
+    for t in range(T):
+        sl = {k: v[:, :, t:t + 1] for k, v in d.items()}
+        o, st = bg.fused_recurrent_forward(sl["q"], sl["k"], sl["v"], sl["g"], sl["b"], sl["w"], st, K ** -0.5)
+        outs.append(o)
+    od = torch.cat(outs, 2)
+    assert_close(od.cpu().numpy(), oc.cpu().numpy(), what="out", **F32_TOL)
+    assert_close(st.cpu().numpy(), sc.cpu().numpy(), what="state", **F32_TOL)
+
+
+def test_chunk_intra_inter_split_equals_fused_call():
+    """gdn2_chunk_intra + gdn2_chunk_inter == gdn2_chunk_fwd, bit for bit."""
+    import ctypes
+    import burn_gdn2 as bg
+    from burn_gdn2 import ops
+
+    B, HV, T, K, V = 1, 2, 200, 64, 64
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=61, dtype=np.float32)
+    d = _to_dev({k: arrs[k] for k in "qkvgbw"}, torch.float32)
+    res = []
+    for split in (False, True):
+        st = torch.zeros(B, HV, K, V, device=DEV)
+        out = torch.empty(B, HV, T, V, device=DEV)
+        a = ops.chunk_args(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], st, out, K ** -0.5, 64)
+        ws = ops.chunk_workspace(a, DEV)
+        s = ops.stream_handle()
+        if split:
+            bg._lib.check(bg.LIB.gdn2_chunk_intra(ctypes.byref(a), ops.ptr(ws), ws.numel(), s))
+            bg._lib.check(bg.LIB.gdn2_chunk_inter(ctypes.byref(a), ops.ptr(ws), ws.numel(), s))
+        else:
+            bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a), ops.ptr(ws), ws.numel(), s))
+        torch.cuda.synchronize()
+        res.append((out.cpu(), st.cpu()))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+
+
+def test_chunk_full_size_matches_recurrent_bf16():
+    """BASELINE config 2 shape per head (K = V = 128, T = 4096, chunk 64) at
+    B*HV = 4: the chunked kernels and the token scan kernel agree (a
+    size-independent property; the oracle would take minutes here)."""
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = 1, 4, 4096, 128, 128
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=71, dtype=np.float32)
+    d = _to_dev({k: arrs[k] for k in "qkvgbw"}, torch.bfloat16)
+    s0 = torch.zeros(B, HV, K, V, device=DEV)
+    oc, sc = bg.chunk_wy_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], s0, K ** -0.5, 64)
+    orr, sr = bg.fused_recurrent_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], s0, K ** -0.5)
+    assert_close_bf16(oc.float().cpu().numpy(), orr.float().cpu().numpy(), what="out")
+    assert_close(sc.cpu().numpy(), sr.cpu().numpy(), rtol=1e-3, atol=1e-3, what="state")
+
+
+def test_short_conv_and_rms_norm_gate_kernels():
+    import burn_gdn2 as bg
+
+    rng = np.random.default_rng(81)
+    x = rng.standard_normal((2, 9, 40)).astype(np.float32)
+    wc = rng.uniform(-0.5, 0.5, (40, 4)).astype(np.float32)
+    cache = rng.standard_normal((2, 3, 40)).astype(np.float32)
+    t = lambda a: torch.tensor(a, device=DEV)
+    for c in (None, cache):
+        y, nc = bg.short_conv_1d(t(x), t(wc), None if c is None else t(c))
+        yr, ncr = O.short_conv_1d(x.astype(np.float64), wc.astype(np.float64),
+                                  None if c is None else c.astype(np.float64))
+        assert_close(y.cpu().numpy(), yr, what="conv", **F32_TOL)
+        assert_close(nc.cpu().numpy(), ncr, what="cache", **F32_TOL)
+    o = rng.standard_normal((2, 5, 3, 24)).astype(np.float32)
+    gate = rng.standard_normal((2, 5, 3, 24)).astype(np.float32)
+    wn = rng.uniform(0.5, 1.5, 24).astype(np.float32)
+    y = bg.rms_norm_gate_per_head(t(o), t(gate), t(wn), 1e-5)
+    yr = O.rms_norm_gate_per_head(o.astype(np.float64), gate.astype(np.float64), wn.astype(np.float64), 1e-5)
+    assert_close(y.cpu().numpy(), yr, what="rms", **F32_TOL)
