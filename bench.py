@@ -92,49 +92,53 @@ def make_inputs(torch, B, HV, T, K, V, dtype, device, seed):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled through NVML
+    every ~5 ms on a background thread during the timed region (the same
+    counters `nvidia-smi --query-gpu=clocks.sm,clocks_event_reasons.*`
+    reports; read-only)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
-        self.path = None
+        self.samples = []
+        self._stop = threading.Event()
+        self._th = None
 
     def start(self):
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self._mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
+            return
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, rs))
+                except Exception:
+                    pass
+                time.sleep(0.005)
+
+        self._th = threading.Thread(target=loop, daemon=True)
+        self._th.start()
 
     def stop(self):
-        if self.proc is None:
+        if self._th is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
+        self._stop.set()
+        self._th.join()
+        if not self.samples:
             return None
-        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
-        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+        sm = sorted(s for s, _ in self.samples)
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self._mx, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------

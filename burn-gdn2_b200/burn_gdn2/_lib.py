@@ -67,7 +67,7 @@ class Config(ctypes.Structure):
 EXPORTS = (
     "gdn2_chunk_fwd_workspace_bytes", "gdn2_chunk_fwd", "gdn2_chunk_intra", "gdn2_chunk_inter",
     "gdn2_recurrent_fwd", "gdn2_short_conv", "gdn2_rms_norm_gate", "gdn2_config_validate",
-    "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version",
+    "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
 )
 
 
@@ -94,10 +94,19 @@ def _load():
     lib.gdn2_last_error.restype = ctypes.c_char_p
     lib.gdn2_last_cuda_error.restype = ctypes.c_int
     lib.gdn2_abi_version.restype = ctypes.c_int
+    lib.gdn2_read_device_errors.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
+    lib.gdn2_read_device_errors.restype = ctypes.c_int
     return lib
 
 
 LIB = _load()
+
+
+def read_device_errors() -> int:
+    """Device error bits since the last call (bit 0: a bounded wait gave up)."""
+    v = ctypes.c_uint32(0)
+    check(LIB.gdn2_read_device_errors(ctypes.byref(v)))
+    return int(v.value)
 
 
 def check(status):

@@ -28,6 +28,7 @@ int check_cuda(cudaError_t e, const char* where) {
 }
 
 int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream);
+unsigned read_device_errors_recurrent();
 int launch_short_conv(int B, int Tn, int C, int dtype, const void* x, const float* w, const float* cin, float* cout,
                       void* y, cudaStream_t st);
 int launch_rms_norm_gate(const gdn2_dims& d, int dtype, const gdn2_view& o, const gdn2_view& gate, const float* w,
@@ -91,6 +92,14 @@ extern "C" {
 const char* gdn2_last_error(void) { return g_err; }
 int gdn2_last_cuda_error(void) { return g_cuda_err; }
 int gdn2_abi_version(void) { return GDN2_ABI_VERSION; }
+
+int gdn2_read_device_errors(uint32_t* flags) {
+  if (!flags) return set_error(GDN2_EINVAL, "gdn2_read_device_errors: null flags");
+  int rc = check_cuda(cudaDeviceSynchronize(), "gdn2_read_device_errors");
+  if (rc) return rc;
+  *flags = read_device_errors_recurrent();
+  return GDN2_OK;
+}
 
 size_t gdn2_chunk_fwd_workspace_bytes(const gdn2_chunk_args* a) {
   if (!a || a->chunk_size <= 0 || a->dims.batch <= 0 || a->dims.seq_len <= 0) return 0;

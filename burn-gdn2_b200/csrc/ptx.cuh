@@ -1,0 +1,87 @@
+// Inline-PTX helpers for sm_100a: mbarriers, bulk (TMA) copies, fences and
+// the bounded waits every kernel uses (a wait that gives up records a
+// device error bit instead of spinning forever).
+#pragma once
+
+#include <stdint.h>
+
+namespace gdn2 {
+
+// Device error bits, read and cleared by gdn2_read_device_errors().
+enum : unsigned {
+  DEVERR_MBAR_TIMEOUT = 1u,  // a bounded mbarrier wait gave up
+};
+// One copy per translation unit (no relocatable device code); each unit
+// that launches kernels exposes a host reader (see gdn2_read_device_errors).
+static __device__ unsigned g_device_errors = 0;
+
+#define GDN2_DEVICE_ERROR_READER(fn)                                   \
+  unsigned fn() {                                                      \
+    unsigned v = 0, z = 0;                                             \
+    if (cudaMemcpyFromSymbol(&v, g_device_errors, sizeof(v)) != cudaSuccess) return 0; \
+    cudaMemcpyToSymbol(g_device_errors, &z, sizeof(z));                \
+    return v;                                                          \
+  }
+
+// Iterations of try_wait (each suspends for a hardware-chosen time slice)
+// before a wait is declared lost: about a second on B200.
+constexpr unsigned MBAR_SPIN_LIMIT = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  uint64_t st;
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 %0, [%1], %2;"
+               : "=l"(st)
+               : "r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+  (void)st;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  uint64_t st;
+  asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];" : "=l"(st) : "r"(smem_u32(bar)) : "memory");
+  (void)st;
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`.  Returns false (and records
+// DEVERR_MBAR_TIMEOUT) if the phase never completed.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
+  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicOr(&g_device_errors, DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sdst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace gdn2

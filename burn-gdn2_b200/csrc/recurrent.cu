@@ -5,12 +5,15 @@
 // token loop fused_recurrent_forward (src/kernel/fused_recurrent.rs:11-56).
 //
 // One CTA owns the state slice S[b, hv, :, col0:col0+VT] for the whole
-// call: it is read from HBM once (128-bit loads, one float4 column group per
-// thread, rows strided by RPP), kept in registers across all T tokens and
-// written back once, in place.  Per token (src/kernel/fused_recurrent.rs:36-49):
+// call: it is brought from HBM into shared memory once by bulk (TMA) copies
+// issued at kernel entry, so the load overlaps the prologue; it stays on
+// chip across all T tokens and the last token's update writes it back in
+// place with coalesced 128-bit stores.  Small slices (<= 32 KB) let five
+// CTAs share an SM, which keeps ~160 KB of state loads in flight per SM.
+// Per token (src/kernel/fused_recurrent.rs:36-49):
 //     S <- S diag(e^g);  v_new = w v - (b k)^T S;  S <- S + k v_new^T;
 //     o = scale q^T S
-// is evaluated with a single pass over the registers:
+// is evaluated with one reduction pass and one update pass over the slice:
 //     erased = sum_k (b k e^g)_k S[k,:],   qs = sum_k (q e^g)_k S[k,:]
 //     v_new  = w v - erased,              o  = scale (qs + (q.k) v_new)
 //     S      = e^g S + k v_new^T
@@ -27,13 +30,14 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace gdn2 {
 
 constexpr int REC_THREADS = 256;
-constexpr int REC_MAXP = 16;  // float4 state registers per thread (64 floats)
+constexpr int REC_SLICE_BYTES = 32 * 1024;  // target state bytes per CTA
 
 struct RecParams {
   int B, T, Hq, HV, K, V;
@@ -71,10 +75,12 @@ __device__ __forceinline__ float conv_act(const DView& x, const float* w, const 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(REC_THREADS) k_recurrent(const RecParams p) {
-  extern __shared__ float smem[];
+__global__ void __launch_bounds__(REC_THREADS, 4) k_recurrent(const RecParams p) {
+  extern __shared__ __align__(128) unsigned char smraw[];
   const int K = p.K, VT = p.VT, RPP = p.RPP;
-  float* sq = smem;
+  float* sS = reinterpret_cast<float*>(smraw);  // [K][VT] state slice
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sS + K * VT);
+  float* sq = reinterpret_cast<float*>(bar + 2);
   float* sk = sq + K;
   float* seg = sk + K;
   float* sbk = seg + K;
@@ -94,16 +100,24 @@ __global__ void __launch_bounds__(REC_THREADS) k_recurrent(const RecParams p) {
   const int Cq = p.Hq * K;   // q/k conv channels
   const int Cv = p.HV * p.V; // v conv channels
 
-  float* st = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * p.V + col0 + cgi * 4;
-  float4 s[REC_MAXP];
-  #pragma unroll
-  for (int i = 0; i < REC_MAXP; ++i) {
-    const int kk = r0 + i * RPP;
-    if (active && i < p.npass && kk < K)
-      s[i] = *reinterpret_cast<const float4*>(st + (int64_t)kk * p.V);
-    else
-      s[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // ---- state slice HBM -> smem with bulk (TMA) copies, overlapped with the prologue ----
+  float* st = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * p.V + col0;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
   }
+  __syncthreads();
+  if (tid < 32) {
+    if (tid == 0) mbar_arrive_expect_tx(bar, (unsigned)(K * VT * sizeof(float)));
+    __syncwarp();
+    if (VT == p.V) {
+      if (tid == 0) bulk_g2s(sS, st, (unsigned)(K * VT * sizeof(float)), bar);
+    } else {
+      for (int kk = tid; kk < K; kk += 32)
+        bulk_g2s(sS + kk * VT, st + (int64_t)kk * p.V, (unsigned)(VT * sizeof(float)), bar);
+    }
+  }
+  bool have_state = false;
 
   for (int t = 0; t < p.T; ++t) {
     // ---- prologue: q, k (conv + SiLU + L2 as requested) ----
@@ -155,19 +169,25 @@ __global__ void __launch_bounds__(REC_THREADS) k_recurrent(const RecParams p) {
       svv[c] = vload<T>(p.w, bb, hv, t, col) * vv;
     }
     const float qk = block_sum<REC_THREADS>(pqk, misc);  // also publishes seg/sbk/sqg/svv
-
-    // ---- one pass over the register-resident state ----
-    float4 pe = make_float4(0.f, 0.f, 0.f, 0.f), pq = pe;
-    #pragma unroll
-    for (int i = 0; i < REC_MAXP; ++i) {
-      const int kk = r0 + i * RPP;
-      if (active && i < p.npass && kk < K) {
-        const float a = sbk[kk], c = sqg[kk];
-        pe.x += a * s[i].x; pe.y += a * s[i].y; pe.z += a * s[i].z; pe.w += a * s[i].w;
-        pq.x += c * s[i].x; pq.y += c * s[i].y; pq.z += c * s[i].z; pq.w += c * s[i].w;
-      }
+    if (!have_state) {
+      // A wait that gives up has recorded a device error; the CTA still runs
+      // every barrier so cluster peers are never left waiting.
+      mbar_wait_bounded(bar, 0);
+      have_state = true;
     }
+
+    // ---- one pass over the smem-resident state ----
+    float4 pe = make_float4(0.f, 0.f, 0.f, 0.f), pq = pe;
     if (active) {
+      for (int i = 0; i < p.npass; ++i) {
+        const int kk = r0 + i * RPP;
+        if (kk < K) {
+          const float4 s = *reinterpret_cast<const float4*>(sS + kk * VT + cgi * 4);
+          const float a = sbk[kk], c = sqg[kk];
+          pe.x += a * s.x; pe.y += a * s.y; pe.z += a * s.z; pe.w += a * s.w;
+          pq.x += c * s.x; pq.y += c * s.y; pq.z += c * s.z; pq.w += c * s.w;
+        }
+      }
       *reinterpret_cast<float4*>(red + r0 * VT + cgi * 4) = pe;
       *reinterpret_cast<float4*>(red + (RPP + r0) * VT + cgi * 4) = pq;
     }
@@ -185,15 +205,21 @@ __global__ void __launch_bounds__(REC_THREADS) k_recurrent(const RecParams p) {
     __syncthreads();
     if (active) {
       const float4 vn = *reinterpret_cast<const float4*>(svn + cgi * 4);
-      #pragma unroll
-      for (int i = 0; i < REC_MAXP; ++i) {
+      const bool last = t == p.T - 1;
+      for (int i = 0; i < p.npass; ++i) {
         const int kk = r0 + i * RPP;
-        if (i < p.npass && kk < K) {
+        if (kk < K) {
+          float4* sp = reinterpret_cast<float4*>(sS + kk * VT + cgi * 4);
+          float4 s = *sp;
           const float e = seg[kk], kv = sk[kk];
-          s[i].x = e * s[i].x + kv * vn.x;
-          s[i].y = e * s[i].y + kv * vn.y;
-          s[i].z = e * s[i].z + kv * vn.z;
-          s[i].w = e * s[i].w + kv * vn.w;
+          s.x = e * s.x + kv * vn.x;
+          s.y = e * s.y + kv * vn.y;
+          s.z = e * s.z + kv * vn.z;
+          s.w = e * s.w + kv * vn.w;
+          if (last)
+            *reinterpret_cast<float4*>(st + (int64_t)kk * p.V + cgi * 4) = s;  // in place, coalesced
+          else
+            *sp = s;
         }
       }
     }
@@ -227,13 +253,7 @@ __global__ void __launch_bounds__(REC_THREADS) k_recurrent(const RecParams p) {
     } else {
       for (int c = tid; c < VT; c += REC_THREADS) vstore<T>(p.out, bb, hv, t, col0 + c, so[c]);
     }
-    __syncthreads();  // so / svn / sk reused by the next token
-  }
-
-  #pragma unroll
-  for (int i = 0; i < REC_MAXP; ++i) {
-    const int kk = r0 + i * RPP;
-    if (active && i < p.npass && kk < K) *reinterpret_cast<float4*>(st + (int64_t)kk * p.V) = s[i];
+    __syncthreads();  // so / svn / sk / sS reused by the next token
   }
 
   // ---- new conv caches: rows T..T+2 of the padded sequence ----
@@ -266,6 +286,299 @@ __global__ void __launch_bounds__(REC_THREADS) k_recurrent(const RecParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode step (T == 1): persistent, double-buffered.
+//
+// A work item is one (batch, key-side head); the CTA handles all `rep` value
+// heads of that key head and all `vsplit` column slices of each, so every
+// conv cache is read and rewritten by exactly one CTA (in place is safe) and
+// the q/k prologue runs once per key head.  The state slices of the CTA's
+// successive (item, value head, slice) steps stream through two shared
+// memory buffers: the bulk copy of step n+1 is issued before step n waits
+// for its own, and the prologue inputs of the next item / value head are
+// loaded into registers while the current one computes.  Each updated row
+// goes straight back to HBM with 128-bit stores.
+// ---------------------------------------------------------------------------
+struct DecTaps {
+  float qx[4], kx[4], g, b;     // item level (thread = key channel)
+  float vx[4], w, gate;         // value-head level (thread = value channel)
+};
+
+template <typename T>
+__device__ __forceinline__ void dec_load_qk(const RecParams& p, int item, DecTaps& r) {
+  const int tid = threadIdx.x;
+  if (tid >= p.K) return;
+  const int bb = item / p.Hq, kh = item % p.Hq;
+  const int Cq = p.Hq * p.K, ch = kh * p.K + tid;
+  if (p.prologue == 1) {
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      r.qx[j] = conv_pad<T>(p.q, p.cq_in, Cq, bb, kh, tid, ch, j);
+      r.kx[j] = conv_pad<T>(p.k, p.ck_in, Cq, bb, kh, tid, ch, j);
+    }
+  } else {
+    r.qx[3] = vload<T>(p.q, bb, kh, 0, tid);
+    r.kx[3] = vload<T>(p.k, bb, kh, 0, tid);
+  }
+  r.g = vload<float>(p.g, bb, kh, 0, tid);
+  r.b = vload<T>(p.b, bb, kh, 0, tid);
+}
+
+template <typename T>
+__device__ __forceinline__ void dec_load_v(const RecParams& p, int bb, int hv, DecTaps& r) {
+  const int tid = threadIdx.x;
+  if (tid >= p.V) return;
+  const int Cv = p.HV * p.V, ch = hv * p.V + tid;
+  if (p.prologue == 1) {
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) r.vx[j] = conv_pad<T>(p.v, p.cv_in, Cv, bb, hv, tid, ch, j);
+  } else {
+    r.vx[3] = vload<T>(p.v, bb, hv, 0, tid);
+  }
+  r.w = vload<T>(p.w, bb, hv, 0, tid);
+  r.gate = p.fuse_epilogue ? vload<T>(p.gate, bb, hv, 0, tid) : 0.f;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(REC_THREADS, 2) k_decode(const RecParams p) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  const int K = p.K, V = p.V, VT = p.VT, RPP = p.RPP;
+  float* sS0 = reinterpret_cast<float*>(smraw);
+  float* sS1 = sS0 + K * VT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sS1 + K * VT);
+  float* sk = reinterpret_cast<float*>(bars + 2);
+  float* seg = sk + K;
+  float* sbk = seg + K;
+  float* sqg = sbk + K;
+  float* svv = sqg + K;   // [V]
+  float* so = svv + V;    // [V]
+  float* svn = so + V;    // [VT]
+  float* red = svn + VT;  // 2 * RPP * VT
+  float* misc = red + 2 * RPP * VT;
+
+  const int tid = threadIdx.x;
+  const int cgi = tid % p.CPR, r0 = tid / p.CPR;
+  const bool active = r0 < RPP;
+  const int n_items = p.B * p.Hq;
+  const int nsub = p.rep * p.vsplit;
+  const int Cq = p.Hq * K, Cv = p.HV * V;
+  if ((int)blockIdx.x >= n_items) return;
+
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // bulk copy of the state slice of step (item, sub) into buffer `buf`
+  auto issue = [&](int item, int sub, int buf) {
+    if (tid >= 32) return;
+    const int bb = item / p.Hq, kh = item % p.Hq;
+    const int hv = kh * p.rep + sub / p.vsplit, vs = sub % p.vsplit;
+    const float* src = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V + vs * VT;
+    float* dst = buf ? sS1 : sS0;
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bars[buf], (unsigned)(K * VT * sizeof(float)));
+    }
+    __syncwarp();
+    if (VT == V) {
+      if (tid == 0) bulk_g2s(dst, src, (unsigned)(K * VT * sizeof(float)), &bars[buf]);
+    } else {
+      for (int kk = tid; kk < K; kk += 32)
+        bulk_g2s(dst + kk * VT, src + (int64_t)kk * V, (unsigned)(VT * sizeof(float)), &bars[buf]);
+    }
+  };
+
+  DecTaps r;
+  unsigned phase[2] = {0u, 0u};
+  int buf = 0;
+  issue(blockIdx.x, 0, 0);
+  dec_load_qk<T>(p, blockIdx.x, r);
+  dec_load_v<T>(p, blockIdx.x / p.Hq, (blockIdx.x % p.Hq) * p.rep, r);
+
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const int bb = item / p.Hq, kh = item % p.Hq;
+    const int next_item = item + gridDim.x;
+
+    // ---- q/k prologue (once per key head) ----
+    float qv = 0.f, kv = 0.f;
+    if (tid < K) {
+      if (p.prologue == 1) {
+        const float* wq = p.cwq + (int64_t)(kh * K + tid) * 4;
+        const float* wk = p.cwk + (int64_t)(kh * K + tid) * 4;
+        float aq = 0.f, ak = 0.f;
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          aq += r.qx[j] * wq[j];
+          ak += r.kx[j] * wk[j];
+        }
+        qv = silu_f(aq);
+        kv = silu_f(ak);
+        #pragma unroll
+        for (int j = 0; j < 3; ++j) {  // new caches: x_pad rows 1..3 (in place)
+          p.cq_out[((int64_t)bb * 3 + j) * Cq + kh * K + tid] = r.qx[j + 1];
+          p.ck_out[((int64_t)bb * 3 + j) * Cq + kh * K + tid] = r.kx[j + 1];
+        }
+      } else {
+        qv = r.qx[3];
+        kv = r.kx[3];
+        if (p.prologue == 2) {
+          qv = silu_f(qv);
+          kv = silu_f(kv);
+        }
+      }
+    }
+    const float gv = r.g, bv = r.b;
+    float nq = 1.f, nk = 1.f;
+    if (p.prologue != 0) {
+      nq = sqrtf(block_sum<REC_THREADS>(qv * qv, misc) + 1e-6f);
+      nk = sqrtf(block_sum<REC_THREADS>(kv * kv, misc) + 1e-6f);
+    }
+    float pqk = 0.f;
+    if (tid < K) {
+      qv /= nq;
+      kv /= nk;
+      const float e = expf(gv);
+      sk[tid] = kv;
+      seg[tid] = e;
+      sbk[tid] = bv * kv * e;
+      sqg[tid] = qv * e;
+      pqk = qv * kv;
+    }
+    const float qk = block_sum<REC_THREADS>(pqk, misc);
+    if (next_item < n_items) dec_load_qk<T>(p, next_item, r);  // prefetch, lands during the passes
+
+    for (int j = 0; j < p.rep; ++j) {
+      const int hv = kh * p.rep + j;
+      // ---- v prologue (once per value head) ----
+      const float gate_reg = r.gate;
+      if (tid < V) {
+        float vv;
+        if (p.prologue == 1) {
+          const float* wv = p.cwv + (int64_t)(hv * V + tid) * 4;
+          float av = 0.f;
+          #pragma unroll
+          for (int jj = 0; jj < 4; ++jj) av += r.vx[jj] * wv[jj];
+          vv = silu_f(av);
+          #pragma unroll
+          for (int jj = 0; jj < 3; ++jj) p.cv_out[((int64_t)bb * 3 + jj) * Cv + hv * V + tid] = r.vx[jj + 1];
+        } else {
+          vv = r.vx[3];
+          if (p.prologue == 2) vv = silu_f(vv);
+        }
+        svv[tid] = r.w * vv;
+      }
+      // prefetch the next value head's inputs
+      if (j + 1 < p.rep)
+        dec_load_v<T>(p, bb, hv + 1, r);
+      else if (next_item < n_items)
+        dec_load_v<T>(p, next_item / p.Hq, (next_item % p.Hq) * p.rep, r);
+      __syncthreads();
+
+      for (int vs = 0; vs < p.vsplit; ++vs) {
+        const int sub = j * p.vsplit + vs;
+        if (sub + 1 < nsub)
+          issue(item, sub + 1, buf ^ 1);
+        else if (next_item < n_items)
+          issue(next_item, 0, buf ^ 1);
+        mbar_wait_bounded(&bars[buf], phase[buf]);
+        phase[buf] ^= 1u;
+        const float* sS = buf ? sS1 : sS0;
+        const int col0 = vs * VT;
+
+        float4 pe = make_float4(0.f, 0.f, 0.f, 0.f), pq = pe;
+        if (active) {
+          for (int i = 0; i < p.npass; ++i) {
+            const int kk = r0 + i * RPP;
+            if (kk < K) {
+              const float4 s = *reinterpret_cast<const float4*>(sS + kk * VT + cgi * 4);
+              const float a = sbk[kk], c = sqg[kk];
+              pe.x += a * s.x; pe.y += a * s.y; pe.z += a * s.z; pe.w += a * s.w;
+              pq.x += c * s.x; pq.y += c * s.y; pq.z += c * s.z; pq.w += c * s.w;
+            }
+          }
+          *reinterpret_cast<float4*>(red + r0 * VT + cgi * 4) = pe;
+          *reinterpret_cast<float4*>(red + (RPP + r0) * VT + cgi * 4) = pq;
+        }
+        __syncthreads();
+        for (int c = tid; c < VT; c += REC_THREADS) {
+          float e = 0.f, qs = 0.f;
+          for (int rr = 0; rr < RPP; ++rr) {
+            e += red[rr * VT + c];
+            qs += red[(RPP + rr) * VT + c];
+          }
+          const float vn = svv[col0 + c] - e;
+          svn[c] = vn;
+          so[col0 + c] = p.scale * (qs + qk * vn);
+        }
+        __syncthreads();
+        if (active) {
+          const float4 vn = *reinterpret_cast<const float4*>(svn + cgi * 4);
+          float* dst = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V + col0 + cgi * 4;
+          for (int i = 0; i < p.npass; ++i) {
+            const int kk = r0 + i * RPP;
+            if (kk < K) {
+              float4 s = *reinterpret_cast<const float4*>(sS + kk * VT + cgi * 4);
+              const float e = seg[kk], kq = sk[kk];
+              s.x = e * s.x + kq * vn.x;
+              s.y = e * s.y + kq * vn.y;
+              s.z = e * s.z + kq * vn.z;
+              s.w = e * s.w + kq * vn.w;
+              *reinterpret_cast<float4*>(dst + (int64_t)kk * V) = s;
+            }
+          }
+        }
+        __syncthreads();  // buffer and svn free for the next step
+        buf ^= 1;
+      }
+
+      // ---- epilogue over the whole value head ----
+      if (p.fuse_epilogue) {
+        const float o = tid < V ? so[tid] : 0.f;
+        const float tot = block_sum<REC_THREADS>(o * o, misc);
+        const float rms = sqrtf(tot / (float)V + p.eps);
+        if (tid < V) vstore<T>(p.out, bb, hv, 0, tid, o / rms * p.onw[tid] * silu_f(gate_reg));
+      } else if (tid < V) {
+        vstore<T>(p.out, bb, hv, 0, tid, so[tid]);
+      }
+      __syncthreads();
+    }
+  }
+}
+
+static int launch_decode(const RecParams& p0, int dtype, cudaStream_t stream) {
+  RecParams p = p0;
+  const int K = p.K, V = p.V;
+  // slices of <= 32 KB so two CTAs (four buffers) share an SM
+  int vsplit = 1;
+  while ((int64_t)K * (V / vsplit) * 4 > REC_SLICE_BYTES && (V % (8 * vsplit)) == 0 && V / vsplit > 32) vsplit *= 2;
+  p.vsplit = vsplit;
+  p.VT = V / vsplit;
+  p.CPR = p.VT / 4;
+  p.RPP = REC_THREADS / p.CPR;
+  p.npass = (K + p.RPP - 1) / p.RPP;
+  const size_t smem = sizeof(float) * (2 * (size_t)K * p.VT + 4 + 4 * (size_t)K + 2 * (size_t)V + p.VT +
+                                       2 * (size_t)p.RPP * p.VT + 48);
+  if (smem > 220 * 1024) return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: decode slice does not fit");
+  void (*fn)(const RecParams) = dtype == GDN2_DTYPE_BF16 ? k_decode<__nv_bfloat16> : k_decode<float>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_fwd: smem attribute");
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, REC_THREADS, smem);
+  if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_fwd: occupancy");
+  const int n_items = p.B * p.Hq;
+  int grid = sms * (per_sm > 0 ? per_sm : 1);
+  if (grid > n_items) grid = n_items;
+  fn<<<grid, REC_THREADS, smem, stream>>>(p);
+  return check_cuda(cudaGetLastError(), "gdn2_recurrent_fwd decode launch");
+}
+
+GDN2_DEVICE_ERROR_READER(read_device_errors_recurrent)
+
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream) {
@@ -293,15 +606,12 @@ int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream) {
   const int rep = a->key_heads_grouped ? d.num_v_heads / d.num_heads : 1;
   if (V % 4) return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: head_v_dim %d not a multiple of 4", V);
   int vsplit = 1;
-  while ((int64_t)K * (V / vsplit) > (int64_t)REC_THREADS * 4 * REC_MAXP && (V % (8 * vsplit)) == 0) vsplit *= 2;
+  while ((int64_t)K * (V / vsplit) * 4 > REC_SLICE_BYTES && (V % (8 * vsplit)) == 0 && V / vsplit > 32) vsplit *= 2;
   const int VT = V / vsplit;
   const int CPR = VT / 4;
   if (CPR > REC_THREADS) return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: head_v_dim %d too large", V);
   const int RPP = REC_THREADS / CPR;
   const int npass = (K + RPP - 1) / RPP;
-  if (npass > REC_MAXP)
-    return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: head %dx%d exceeds the register-resident state", K, V);
-
   RecParams p;
   p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.K = K; p.V = V;
   p.Hq = a->key_heads_grouped ? d.num_heads : d.num_v_heads;
@@ -318,6 +628,8 @@ int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream) {
   p.onw = a->o_norm_weight;
   p.state = a->state;
 
+  if (d.seq_len == 1 && K <= REC_THREADS && V <= REC_THREADS) return launch_decode(p, a->dtype, stream);
+
   // CTAs that read a key head's conv cache which is overwritten in place
   // must finish reading before the owner writes: put them in one cluster.
   const bool shared_inplace = a->prologue == 1 &&
@@ -332,7 +644,9 @@ int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream) {
                      "conv_*_out buffers",
                      p.cluster_x * p.cluster_y);
 
-  const size_t smem = sizeof(float) * (5 * (size_t)K + 3 * (size_t)VT + 2 * (size_t)RPP * VT + 48);
+  const size_t smem = sizeof(float) * ((size_t)K * VT + 4 + 5 * (size_t)K + 3 * (size_t)VT + 2 * (size_t)RPP * VT + 48);
+  if (smem > 220 * 1024)
+    return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: state slice %dx%d does not fit shared memory", K, VT);
   void (*fn)(const RecParams) = a->dtype == GDN2_DTYPE_BF16 ? k_recurrent<__nv_bfloat16> : k_recurrent<float>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

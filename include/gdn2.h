@@ -190,6 +190,12 @@ typedef struct gdn2_config {
  * msg (and in gdn2_last_error()). */
 GDN2_API int gdn2_config_validate(const gdn2_config* cfg, char* msg, size_t msg_len);
 
+/* Device-side error bits accumulated since the last call (and cleared):
+ * bit 0 = a bounded wait inside a kernel gave up (a bulk copy that never
+ * completed); the kernel finished without hanging but its results are
+ * invalid.  Synchronises the current device. */
+GDN2_API int gdn2_read_device_errors(uint32_t* flags);
+
 /* Error / version queries. */
 GDN2_API const char* gdn2_last_error(void);
 GDN2_API int gdn2_last_cuda_error(void);

@@ -38,6 +38,18 @@ def assert_close_bf16(a, b, what=""):
     assert_close(a, b, BF16_RTOL, BF16_RTOL * rms, what)
 
 
+def assert_close_normwise(a, b, rtol, what=""):
+    """Whole-layer bf16 criterion: relative Frobenius error <= rtol and no
+    element off by more than 2.5 rtol of the reference's max magnitude."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    assert a.shape == b.shape and np.all(np.isfinite(a)), what
+    rel = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+    assert rel <= rtol, f"{what}: relative Frobenius error {rel:.3g} > {rtol}"
+    worst = np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
+    assert worst <= 2.5 * rtol, f"{what}: max |d| / max |ref| = {worst:.3g}"
+
+
 def load_golden(name):
     z = np.load(os.path.join(GOLDEN, name))
     cfg = dict(hidden_size=int(z["D"]), num_heads=int(z["H"]), head_dim=int(z["HK"]), num_v_heads=int(z["HV"]),

@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import gdn2_oracle as O
-from helpers import F32_TOL, assert_close, assert_close_bf16, load_golden
+from helpers import BF16_RTOL, F32_TOL, assert_close, assert_close_normwise, load_golden
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -121,7 +121,10 @@ def test_gva_decode_inplace_cluster():
 @pytest.mark.parametrize("mode", ["FusedRecurrent", "Chunk"])
 def test_layer_bf16_vs_oracle(mode):
     """bf16 weights/activations with f32 accumulation vs the f64 oracle on
-    the same bf16-rounded weights (rel 2e-2)."""
+    the same bf16-rounded weights: rel 2e-2 normwise.  Every projection and
+    activation of the layer is stored in bf16 (one rounding each), so an
+    elementwise bound is only meaningful on the core kernels, which
+    test_gpu_core checks elementwise."""
     import burn_gdn2 as bg
 
     cfgd = dict(hidden_size=128, num_heads=2, head_dim=64)
@@ -133,4 +136,27 @@ def test_layer_bf16_vs_oracle(mode):
     want = O.Gdn2Layer(ocfg, Wb, np.float64).forward_train(xb.astype(np.float64))
     m = _module(cfgd, W, getattr(bg.Gdn2Mode, mode), dtype=torch.bfloat16)
     got = m.forward_train(torch.tensor(xb, device=DEV, dtype=torch.bfloat16))
-    assert_close_bf16(got.float().cpu().numpy(), want, what="bf16 layer")
+    assert_close_normwise(got.float().cpu().numpy(), want, BF16_RTOL, what="bf16 layer")
+
+
+@pytest.mark.parametrize("gva_mode", ["grouped", "reference"])
+def test_multi_token_inplace_cluster_path(gva_mode):
+    """T = 5 continuation with state (in-place conv caches shared by 2 value
+    heads x 2 column slices: the cluster path of the multi-token kernel),
+    K = 128, V = 256, after a 70-token chunked prefill; vs the oracle."""
+    import burn_gdn2 as bg
+
+    cfgd = dict(hidden_size=128, num_heads=2, head_dim=128, num_v_heads=4, expand_v=2.0)
+    ocfg = O.Gdn2Config(mode="chunk", **cfgd)
+    W = O.init_weights(ocfg, seed=13)
+    layer = O.Gdn2Layer(ocfg, W, np.float64, gva=gva_mode)
+    x = np.random.default_rng(14).standard_normal((2, 75, 128)).astype(np.float32)
+    m = _module(cfgd, W, bg.Gdn2Mode.Chunk, gva_mode=gva_mode)
+    _, st = m.forward(torch.tensor(x[:, :70], device=DEV), None, True)
+    _, ost = layer.forward(x[:, :70].astype(np.float64), None, True)
+    y, st = m.forward(torch.tensor(x[:, 70:], device=DEV), st, True)
+    yo, ost = layer.forward(x[:, 70:].astype(np.float64), ost, True)
+    assert_close(y.cpu().numpy(), yo, what="continuation", **F32_TOL)
+    assert_close(st.recurrent.cpu().numpy(), ost.recurrent, what="state", **F32_TOL)
+    for n in ("conv_q", "conv_k", "conv_v"):
+        assert_close(getattr(st, n).cpu().numpy(), getattr(ost, n), what=n, **F32_TOL)
