@@ -84,4 +84,14 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, unsigned 
       : "memory");
 }
 
+// Ampere-style per-thread async copy, 16 bytes, L2 only (.cg).
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 }  // namespace gdn2

@@ -287,21 +287,32 @@ __global__ void __launch_bounds__(REC_THREADS, 4) k_recurrent(const RecParams p)
 }
 
 // ---------------------------------------------------------------------------
-// Decode step (T == 1): persistent, double-buffered.
+// Decode step (T == 1): persistent, double-buffered, barrier-free main loop.
 //
 // A work item is one (batch, key-side head); the CTA handles all `rep` value
-// heads of that key head and all `vsplit` column slices of each, so every
-// conv cache is read and rewritten by exactly one CTA (in place is safe) and
-// the q/k prologue runs once per key head.  The state slices of the CTA's
-// successive (item, value head, slice) steps stream through two shared
-// memory buffers: the bulk copy of step n+1 is issued before step n waits
-// for its own, and the prologue inputs of the next item / value head are
-// loaded into registers while the current one computes.  Each updated row
-// goes straight back to HBM with 128-bit stores.
+// heads of that key head and all 64-column slices of each, so every conv
+// cache is read and rewritten by exactly one CTA (in place is safe) and the
+// q/k prologue runs once per key head.
+//
+// Each of the 4 warps owns 16 columns of the current slice over all K rows
+// and streams them through two private shared-memory buffers with per-lane
+// 16-byte cp.async copies: the copy of step n+1 is issued before step n is
+// consumed, and since lane (rg = lane / 4, cg = lane % 4) reads back exactly
+// the rows rg, rg+8, ... and columns 4cg..4cg+3 it copied, no barrier is
+// needed between copy and use.  A quarter-warp touches two dense 64-byte
+// rows, so the 16-float rows need no padding to be bank-conflict free.  The
+// K reductions are warp shuffles and updated rows go straight back to HBM
+// (64 contiguous bytes per row per warp).  Block barriers remain only in the
+// per-item prologue (L2 norms) and the per-value-head RMS epilogue.
 // ---------------------------------------------------------------------------
+constexpr int DEC_THREADS = 128;
+constexpr int DEC_VT = 64;  // columns per slice (4 warps x 16)
+
+constexpr int DEC_VCH = 2;  // value channels per thread (V <= 256)
+
 struct DecTaps {
-  float qx[4], kx[4], g, b;     // item level (thread = key channel)
-  float vx[4], w, gate;         // value-head level (thread = value channel)
+  float qx[4], kx[4], wq[4], wk[4], g, b;                          // item: thread = key channel
+  float vx[DEC_VCH][4], wv[DEC_VCH][4], w[DEC_VCH], gate[DEC_VCH];  // value head: thread = channel(s)
 };
 
 template <typename T>
@@ -315,6 +326,8 @@ __device__ __forceinline__ void dec_load_qk(const RecParams& p, int item, DecTap
     for (int j = 0; j < 4; ++j) {
       r.qx[j] = conv_pad<T>(p.q, p.cq_in, Cq, bb, kh, tid, ch, j);
       r.kx[j] = conv_pad<T>(p.k, p.ck_in, Cq, bb, kh, tid, ch, j);
+      r.wq[j] = p.cwq[(int64_t)ch * 4 + j];
+      r.wk[j] = p.cwk[(int64_t)ch * 4 + j];
     }
   } else {
     r.qx[3] = vload<T>(p.q, bb, kh, 0, tid);
@@ -326,73 +339,59 @@ __device__ __forceinline__ void dec_load_qk(const RecParams& p, int item, DecTap
 
 template <typename T>
 __device__ __forceinline__ void dec_load_v(const RecParams& p, int bb, int hv, DecTaps& r) {
-  const int tid = threadIdx.x;
-  if (tid >= p.V) return;
-  const int Cv = p.HV * p.V, ch = hv * p.V + tid;
-  if (p.prologue == 1) {
-    #pragma unroll
-    for (int j = 0; j < 4; ++j) r.vx[j] = conv_pad<T>(p.v, p.cv_in, Cv, bb, hv, tid, ch, j);
-  } else {
-    r.vx[3] = vload<T>(p.v, bb, hv, 0, tid);
+  const int Cv = p.HV * p.V;
+  #pragma unroll
+  for (int u = 0; u < DEC_VCH; ++u) {
+    const int c = threadIdx.x + u * DEC_THREADS;
+    if (c >= p.V) break;
+    const int ch = hv * p.V + c;
+    if (p.prologue == 1) {
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        r.vx[u][j] = conv_pad<T>(p.v, p.cv_in, Cv, bb, hv, c, ch, j);
+        r.wv[u][j] = p.cwv[(int64_t)ch * 4 + j];
+      }
+    } else {
+      r.vx[u][3] = vload<T>(p.v, bb, hv, 0, c);
+    }
+    r.w[u] = vload<T>(p.w, bb, hv, 0, c);
+    r.gate[u] = p.fuse_epilogue ? vload<T>(p.gate, bb, hv, 0, c) : 0.f;
   }
-  r.w = vload<T>(p.w, bb, hv, 0, tid);
-  r.gate = p.fuse_epilogue ? vload<T>(p.gate, bb, hv, 0, tid) : 0.f;
 }
 
 template <typename T>
-__global__ void __launch_bounds__(REC_THREADS, 2) k_decode(const RecParams p) {
+__global__ void __launch_bounds__(DEC_THREADS) k_decode(const RecParams p) {
   extern __shared__ __align__(128) unsigned char smraw[];
-  const int K = p.K, V = p.V, VT = p.VT, RPP = p.RPP;
-  float* sS0 = reinterpret_cast<float*>(smraw);
-  float* sS1 = sS0 + K * VT;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sS1 + K * VT);
-  float* sk = reinterpret_cast<float*>(bars + 2);
+  const int K = p.K, V = p.V;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rg = lane >> 2, cg = lane & 3;
+  float* wbuf = reinterpret_cast<float*>(smraw) + warp * 2 * K * 16;  // this warp's 2 x [K][16]
+  float* sk = reinterpret_cast<float*>(smraw) + 4 * 2 * K * 16;
   float* seg = sk + K;
   float* sbk = seg + K;
   float* sqg = sbk + K;
-  float* svv = sqg + K;   // [V]
-  float* so = svv + V;    // [V]
-  float* svn = so + V;    // [VT]
-  float* red = svn + VT;  // 2 * RPP * VT
-  float* misc = red + 2 * RPP * VT;
+  float* svv = sqg + K;  // [V]
+  float* so = svv + V;   // [V]
+  float* misc = so + V;  // 32
 
-  const int tid = threadIdx.x;
-  const int cgi = tid % p.CPR, r0 = tid / p.CPR;
-  const bool active = r0 < RPP;
   const int n_items = p.B * p.Hq;
-  const int nsub = p.rep * p.vsplit;
+  const int vsplit = V / DEC_VT;
+  const int nsub = p.rep * vsplit;
   const int Cq = p.Hq * K, Cv = p.HV * V;
+  const int wc = warp * 16 + cg * 4;  // this lane's column inside a slice
   if ((int)blockIdx.x >= n_items) return;
 
-  if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  // bulk copy of the state slice of step (item, sub) into buffer `buf`
-  auto issue = [&](int item, int sub, int buf) {
-    if (tid >= 32) return;
+  // async copy of this lane's part of step (item, sub) into buffer b
+  auto issue = [&](int item, int sub, int b) {
     const int bb = item / p.Hq, kh = item % p.Hq;
-    const int hv = kh * p.rep + sub / p.vsplit, vs = sub % p.vsplit;
-    const float* src = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V + vs * VT;
-    float* dst = buf ? sS1 : sS0;
-    if (tid == 0) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bars[buf], (unsigned)(K * VT * sizeof(float)));
-    }
-    __syncwarp();
-    if (VT == V) {
-      if (tid == 0) bulk_g2s(dst, src, (unsigned)(K * VT * sizeof(float)), &bars[buf]);
-    } else {
-      for (int kk = tid; kk < K; kk += 32)
-        bulk_g2s(dst + kk * VT, src + (int64_t)kk * V, (unsigned)(VT * sizeof(float)), &bars[buf]);
-    }
+    const int hv = kh * p.rep + sub / vsplit, vs = sub % vsplit;
+    const float* src = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V + vs * DEC_VT + wc;
+    float* dst = wbuf + b * K * 16 + cg * 4;
+    for (int kk = rg; kk < K; kk += 8) cp_async16(dst + kk * 16, src + (int64_t)kk * V);
+    cp_async_commit();
   };
 
   DecTaps r;
-  unsigned phase[2] = {0u, 0u};
   int buf = 0;
   issue(blockIdx.x, 0, 0);
   dec_load_qk<T>(p, blockIdx.x, r);
@@ -406,18 +405,16 @@ __global__ void __launch_bounds__(REC_THREADS, 2) k_decode(const RecParams p) {
     float qv = 0.f, kv = 0.f;
     if (tid < K) {
       if (p.prologue == 1) {
-        const float* wq = p.cwq + (int64_t)(kh * K + tid) * 4;
-        const float* wk = p.cwk + (int64_t)(kh * K + tid) * 4;
         float aq = 0.f, ak = 0.f;
         #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          aq += r.qx[j] * wq[j];
-          ak += r.kx[j] * wk[j];
+          aq += r.qx[j] * r.wq[j];
+          ak += r.kx[j] * r.wk[j];
         }
         qv = silu_f(aq);
         kv = silu_f(ak);
         #pragma unroll
-        for (int j = 0; j < 3; ++j) {  // new caches: x_pad rows 1..3 (in place)
+        for (int j = 0; j < 3; ++j) {  // new caches = x_pad rows 1..3, in place
           p.cq_out[((int64_t)bb * 3 + j) * Cq + kh * K + tid] = r.qx[j + 1];
           p.ck_out[((int64_t)bb * 3 + j) * Cq + kh * K + tid] = r.kx[j + 1];
         }
@@ -431,10 +428,11 @@ __global__ void __launch_bounds__(REC_THREADS, 2) k_decode(const RecParams p) {
       }
     }
     const float gv = r.g, bv = r.b;
+    if (next_item < n_items) dec_load_qk<T>(p, next_item, r);  // prefetch, lands during this item
     float nq = 1.f, nk = 1.f;
     if (p.prologue != 0) {
-      nq = sqrtf(block_sum<REC_THREADS>(qv * qv, misc) + 1e-6f);
-      nk = sqrtf(block_sum<REC_THREADS>(kv * kv, misc) + 1e-6f);
+      nq = sqrtf(block_sum<DEC_THREADS>(qv * qv, misc) + 1e-6f);
+      nk = sqrtf(block_sum<DEC_THREADS>(kv * kv, misc) + 1e-6f);
     }
     float pqk = 0.f;
     if (tid < K) {
@@ -447,28 +445,32 @@ __global__ void __launch_bounds__(REC_THREADS, 2) k_decode(const RecParams p) {
       sqg[tid] = qv * e;
       pqk = qv * kv;
     }
-    const float qk = block_sum<REC_THREADS>(pqk, misc);
-    if (next_item < n_items) dec_load_qk<T>(p, next_item, r);  // prefetch, lands during the passes
+    const float qk = block_sum<DEC_THREADS>(pqk, misc);  // publishes sk/seg/sbk/sqg
 
     for (int j = 0; j < p.rep; ++j) {
       const int hv = kh * p.rep + j;
-      // ---- v prologue (once per value head) ----
-      const float gate_reg = r.gate;
-      if (tid < V) {
-        float vv;
-        if (p.prologue == 1) {
-          const float* wv = p.cwv + (int64_t)(hv * V + tid) * 4;
-          float av = 0.f;
-          #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) av += r.vx[jj] * wv[jj];
-          vv = silu_f(av);
-          #pragma unroll
-          for (int jj = 0; jj < 3; ++jj) p.cv_out[((int64_t)bb * 3 + jj) * Cv + hv * V + tid] = r.vx[jj + 1];
-        } else {
-          vv = r.vx[3];
-          if (p.prologue == 2) vv = silu_f(vv);
+      // ---- v prologue (once per value head) from the prefetched registers ----
+      float gate_reg[DEC_VCH];
+      #pragma unroll
+      for (int u = 0; u < DEC_VCH; ++u) {
+        const int c = tid + u * DEC_THREADS;
+        gate_reg[u] = r.gate[u];
+        if (c < V) {
+          float vv;
+          if (p.prologue == 1) {
+            float acc = 0.f;
+            #pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc += r.vx[u][jj] * r.wv[u][jj];
+            vv = silu_f(acc);
+            #pragma unroll
+            for (int jj = 0; jj < 3; ++jj)  // new v cache = x_pad rows 1..3, in place
+              p.cv_out[((int64_t)bb * 3 + jj) * Cv + hv * V + c] = r.vx[u][jj + 1];
+          } else {
+            vv = r.vx[u][3];
+            if (p.prologue == 2) vv = silu_f(vv);
+          }
+          svv[c] = r.w[u] * vv;
         }
-        svv[tid] = r.w * vv;
       }
       // prefetch the next value head's inputs
       if (j + 1 < p.rep)
@@ -477,103 +479,96 @@ __global__ void __launch_bounds__(REC_THREADS, 2) k_decode(const RecParams p) {
         dec_load_v<T>(p, next_item / p.Hq, (next_item % p.Hq) * p.rep, r);
       __syncthreads();
 
-      for (int vs = 0; vs < p.vsplit; ++vs) {
-        const int sub = j * p.vsplit + vs;
+      for (int vs = 0; vs < vsplit; ++vs) {
+        const int sub = j * vsplit + vs;
+        bool more = true;
         if (sub + 1 < nsub)
           issue(item, sub + 1, buf ^ 1);
         else if (next_item < n_items)
           issue(next_item, 0, buf ^ 1);
-        mbar_wait_bounded(&bars[buf], phase[buf]);
-        phase[buf] ^= 1u;
-        const float* sS = buf ? sS1 : sS0;
-        const int col0 = vs * VT;
+        else
+          more = false;
+        if (more)
+          cp_async_wait<1>();
+        else
+          cp_async_wait<0>();
+        const float* sS = wbuf + buf * K * 16 + cg * 4;
+        const int col = vs * DEC_VT + wc;
 
         float4 pe = make_float4(0.f, 0.f, 0.f, 0.f), pq = pe;
-        if (active) {
-          for (int i = 0; i < p.npass; ++i) {
-            const int kk = r0 + i * RPP;
-            if (kk < K) {
-              const float4 s = *reinterpret_cast<const float4*>(sS + kk * VT + cgi * 4);
-              const float a = sbk[kk], c = sqg[kk];
-              pe.x += a * s.x; pe.y += a * s.y; pe.z += a * s.z; pe.w += a * s.w;
-              pq.x += c * s.x; pq.y += c * s.y; pq.z += c * s.z; pq.w += c * s.w;
-            }
-          }
-          *reinterpret_cast<float4*>(red + r0 * VT + cgi * 4) = pe;
-          *reinterpret_cast<float4*>(red + (RPP + r0) * VT + cgi * 4) = pq;
+        for (int kk = rg; kk < K; kk += 8) {
+          const float4 s = *reinterpret_cast<const float4*>(sS + kk * 16);
+          const float a = sbk[kk], c = sqg[kk];
+          pe.x += a * s.x; pe.y += a * s.y; pe.z += a * s.z; pe.w += a * s.w;
+          pq.x += c * s.x; pq.y += c * s.y; pq.z += c * s.z; pq.w += c * s.w;
         }
-        __syncthreads();
-        for (int c = tid; c < VT; c += REC_THREADS) {
-          float e = 0.f, qs = 0.f;
-          for (int rr = 0; rr < RPP; ++rr) {
-            e += red[rr * VT + c];
-            qs += red[(RPP + rr) * VT + c];
-          }
-          const float vn = svv[col0 + c] - e;
-          svn[c] = vn;
-          so[col0 + c] = p.scale * (qs + qk * vn);
+        #pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          pe.x += __shfl_xor_sync(0xffffffffu, pe.x, o);
+          pe.y += __shfl_xor_sync(0xffffffffu, pe.y, o);
+          pe.z += __shfl_xor_sync(0xffffffffu, pe.z, o);
+          pe.w += __shfl_xor_sync(0xffffffffu, pe.w, o);
+          pq.x += __shfl_xor_sync(0xffffffffu, pq.x, o);
+          pq.y += __shfl_xor_sync(0xffffffffu, pq.y, o);
+          pq.z += __shfl_xor_sync(0xffffffffu, pq.z, o);
+          pq.w += __shfl_xor_sync(0xffffffffu, pq.w, o);
         }
-        __syncthreads();
-        if (active) {
-          const float4 vn = *reinterpret_cast<const float4*>(svn + cgi * 4);
-          float* dst = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V + col0 + cgi * 4;
-          for (int i = 0; i < p.npass; ++i) {
-            const int kk = r0 + i * RPP;
-            if (kk < K) {
-              float4 s = *reinterpret_cast<const float4*>(sS + kk * VT + cgi * 4);
-              const float e = seg[kk], kq = sk[kk];
-              s.x = e * s.x + kq * vn.x;
-              s.y = e * s.y + kq * vn.y;
-              s.z = e * s.z + kq * vn.z;
-              s.w = e * s.w + kq * vn.w;
-              *reinterpret_cast<float4*>(dst + (int64_t)kk * V) = s;
-            }
-          }
+        const float4 wv = *reinterpret_cast<const float4*>(svv + col);
+        const float4 vn = make_float4(wv.x - pe.x, wv.y - pe.y, wv.z - pe.z, wv.w - pe.w);
+        if (rg == 0)
+          *reinterpret_cast<float4*>(so + col) =
+              make_float4(p.scale * (pq.x + qk * vn.x), p.scale * (pq.y + qk * vn.y), p.scale * (pq.z + qk * vn.z),
+                          p.scale * (pq.w + qk * vn.w));
+        float* dst = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V + col;
+        for (int kk = rg; kk < K; kk += 8) {
+          float4 s = *reinterpret_cast<const float4*>(sS + kk * 16);
+          const float e = seg[kk], kq = sk[kk];
+          s.x = e * s.x + kq * vn.x;
+          s.y = e * s.y + kq * vn.y;
+          s.z = e * s.z + kq * vn.z;
+          s.w = e * s.w + kq * vn.w;
+          *reinterpret_cast<float4*>(dst + (int64_t)kk * V) = s;
         }
-        __syncthreads();  // buffer and svn free for the next step
         buf ^= 1;
       }
 
       // ---- epilogue over the whole value head ----
-      if (p.fuse_epilogue) {
-        const float o = tid < V ? so[tid] : 0.f;
-        const float tot = block_sum<REC_THREADS>(o * o, misc);
-        const float rms = sqrtf(tot / (float)V + p.eps);
-        if (tid < V) vstore<T>(p.out, bb, hv, 0, tid, o / rms * p.onw[tid] * silu_f(gate_reg));
-      } else if (tid < V) {
-        vstore<T>(p.out, bb, hv, 0, tid, so[tid]);
+      __syncthreads();  // so[] complete
+      float ss = 0.f;
+      for (int c = tid; c < V; c += DEC_THREADS) ss += so[c] * so[c];
+      const float rms = p.fuse_epilogue ? sqrtf(block_sum<DEC_THREADS>(ss, misc) / (float)V + p.eps) : 1.f;
+      #pragma unroll
+      for (int u = 0; u < DEC_VCH; ++u) {
+        const int c = tid + u * DEC_THREADS;
+        if (c < V) {
+          if (p.fuse_epilogue)
+            vstore<T>(p.out, bb, hv, 0, c, so[c] / rms * p.onw[c] * silu_f(gate_reg[u]));
+          else
+            vstore<T>(p.out, bb, hv, 0, c, so[c]);
+        }
       }
-      __syncthreads();
+      __syncthreads();  // svv / so reused by the next value head
     }
   }
+  cp_async_wait<0>();
 }
 
 static int launch_decode(const RecParams& p0, int dtype, cudaStream_t stream) {
   RecParams p = p0;
   const int K = p.K, V = p.V;
-  // slices of <= 32 KB so two CTAs (four buffers) share an SM
-  int vsplit = 1;
-  while ((int64_t)K * (V / vsplit) * 4 > REC_SLICE_BYTES && (V % (8 * vsplit)) == 0 && V / vsplit > 32) vsplit *= 2;
-  p.vsplit = vsplit;
-  p.VT = V / vsplit;
-  p.CPR = p.VT / 4;
-  p.RPP = REC_THREADS / p.CPR;
-  p.npass = (K + p.RPP - 1) / p.RPP;
-  const size_t smem = sizeof(float) * (2 * (size_t)K * p.VT + 4 + 4 * (size_t)K + 2 * (size_t)V + p.VT +
-                                       2 * (size_t)p.RPP * p.VT + 48);
-  if (smem > 220 * 1024) return set_error(GDN2_EUNSUPPORTED, "gdn2_recurrent_fwd: decode slice does not fit");
+  const size_t smem = sizeof(float) * (8 * (size_t)K * 16 + 4 * (size_t)K + 2 * (size_t)V + 32);
   void (*fn)(const RecParams) = dtype == GDN2_DTYPE_BF16 ? k_decode<__nv_bfloat16> : k_decode<float>;
   cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_fwd: smem attribute");
   int dev = 0, sms = 0, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, REC_THREADS, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, DEC_THREADS, smem);
   if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_fwd: occupancy");
   const int n_items = p.B * p.Hq;
   int grid = sms * (per_sm > 0 ? per_sm : 1);
   if (grid > n_items) grid = n_items;
-  fn<<<grid, REC_THREADS, smem, stream>>>(p);
+  fn<<<grid, DEC_THREADS, smem, stream>>>(p);
   return check_cuda(cudaGetLastError(), "gdn2_recurrent_fwd decode launch");
 }
 
@@ -628,7 +623,9 @@ int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream) {
   p.onw = a->o_norm_weight;
   p.state = a->state;
 
-  if (d.seq_len == 1 && K <= REC_THREADS && V <= REC_THREADS) return launch_decode(p, a->dtype, stream);
+  // decode hot path: one token, heads of <= 128 key channels, value heads in 64-column slices
+  if (d.seq_len == 1 && K <= DEC_THREADS && V % DEC_VT == 0 && V <= DEC_THREADS * DEC_VCH)
+    return launch_decode(p, a->dtype, stream);
 
   // CTAs that read a key head's conv cache which is overwritten in place
   // must finish reading before the owner writes: put them in one cluster.
