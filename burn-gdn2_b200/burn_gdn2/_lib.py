@@ -68,6 +68,7 @@ EXPORTS = (
     "gdn2_chunk_fwd_workspace_bytes", "gdn2_chunk_fwd", "gdn2_chunk_intra", "gdn2_chunk_inter",
     "gdn2_recurrent_fwd", "gdn2_short_conv", "gdn2_rms_norm_gate", "gdn2_config_validate",
     "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
+    "gdn2_selftest_umma",
 )
 
 
@@ -96,6 +97,8 @@ def _load():
     lib.gdn2_abi_version.restype = ctypes.c_int
     lib.gdn2_read_device_errors.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
     lib.gdn2_read_device_errors.restype = ctypes.c_int
+    lib.gdn2_selftest_umma.argtypes = [i32, vp, vp, vp, vp]
+    lib.gdn2_selftest_umma.restype = ctypes.c_int
     return lib
 
 

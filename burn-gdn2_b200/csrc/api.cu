@@ -29,6 +29,8 @@ int check_cuda(cudaError_t e, const char* where) {
 
 int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream);
 unsigned read_device_errors_recurrent();
+unsigned read_device_errors_selftest();
+int selftest_umma(int test, const float* A, const float* B, float* D, cudaStream_t st);
 int launch_short_conv(int B, int Tn, int C, int dtype, const void* x, const float* w, const float* cin, float* cout,
                       void* y, cudaStream_t st);
 int launch_rms_norm_gate(const gdn2_dims& d, int dtype, const gdn2_view& o, const gdn2_view& gate, const float* w,
@@ -97,7 +99,7 @@ int gdn2_read_device_errors(uint32_t* flags) {
   if (!flags) return set_error(GDN2_EINVAL, "gdn2_read_device_errors: null flags");
   int rc = check_cuda(cudaDeviceSynchronize(), "gdn2_read_device_errors");
   if (rc) return rc;
-  *flags = read_device_errors_recurrent();
+  *flags = read_device_errors_recurrent() | read_device_errors_selftest();
   return GDN2_OK;
 }
 
@@ -135,6 +137,12 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream)
   rc = launch_inter_simt(p, (cudaStream_t)stream);
   if (rc) return rc;
   return launch_chunk_out(p, a->dtype, (cudaStream_t)stream);
+}
+
+int gdn2_selftest_umma(int32_t test, const float* a, const float* b, float* d, void* stream) {
+  if (test < 0 || test > 3) return set_error(GDN2_EINVAL, "gdn2_selftest_umma: test %d not in 0..3", test);
+  if (!a || !b || !d) return set_error(GDN2_EINVAL, "gdn2_selftest_umma: null pointer");
+  return selftest_umma(test, a, b, d, (cudaStream_t)stream);
 }
 
 int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, void* stream) {

@@ -196,6 +196,16 @@ GDN2_API int gdn2_config_validate(const gdn2_config* cfg, char* msg, size_t msg_
  * invalid.  Synchronises the current device. */
 GDN2_API int gdn2_read_device_errors(uint32_t* flags);
 
+/* Diagnostic (no counterpart in the reference): one tcgen05 MMA tile,
+ * D[M][N] = A[M][K] . B[K][N] with bf16-rounded operands and f32
+ * accumulation, in the shared-memory layout of case `test`:
+ *   0: M=128 N=64  K=128, A K-major, B MN-major
+ *   1: M=64  N=32  K=128, A K-major, B K-major
+ *   2: M=128 N=64  K=64,  A MN-major, B MN-major
+ *   3: M=128 N=128 K=64,  A K-major, B MN-major (two N groups)
+ * a, b, d: row-major f32 device arrays. */
+GDN2_API int gdn2_selftest_umma(int32_t test, const float* a, const float* b, float* d, void* stream);
+
 /* Error / version queries. */
 GDN2_API const char* gdn2_last_error(void);
 GDN2_API int gdn2_last_cuda_error(void);
