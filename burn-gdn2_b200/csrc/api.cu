@@ -6,6 +6,7 @@
 #include <string.h>
 
 #include "chunk.cuh"
+#include "chunk_tc.cuh"
 #include "common.cuh"
 
 namespace gdn2 {
@@ -30,6 +31,8 @@ int check_cuda(cudaError_t e, const char* where) {
 int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream);
 unsigned read_device_errors_recurrent();
 unsigned read_device_errors_selftest();
+unsigned read_device_errors_intra_tc();
+unsigned read_device_errors_inter_tc();
 int selftest_umma(int test, const float* A, const float* B, float* D, cudaStream_t st);
 int launch_short_conv(int B, int Tn, int C, int dtype, const void* x, const float* w, const float* cin, float* cout,
                       void* y, cudaStream_t st);
@@ -44,6 +47,53 @@ static int check_dims(const gdn2_dims& d, const char* fn) {
   if (d.num_v_heads % d.num_heads)
     return set_error(GDN2_EINVAL, "%s: num_v_heads=%d must be a multiple of num_heads=%d", fn, d.num_v_heads,
                      d.num_heads);
+  return GDN2_OK;
+}
+
+static bool mult(int64_t x, int m) { return x % m == 0; }
+static bool align_ok(const void* ptr, int bytes) { return ((uintptr_t)ptr % bytes) == 0; }
+
+// The tensor-core path: bf16, K = 128, V in {64, 128}, 64-token chunks, and
+// views whose rows allow its vector accesses (8-byte q/k/b/v/w, 16-byte g,
+// gate and out).  Everything else runs on the CUDA-core path.
+static bool use_tc(const gdn2_chunk_args* a) {
+  const gdn2_dims& d = a->dims;
+  const int C = a->chunk_size < CP ? a->chunk_size : CP;
+  if (!tc_supported(d.head_k_dim, d.head_v_dim, C, a->dtype)) return false;
+  auto v_ok = [&](const gdn2_view& v, int elems, int bytes) {
+    return align_ok(v.data, bytes) && mult(v.stride0, elems) && mult(v.stride1, elems) && mult(v.stride2, elems);
+  };
+  if (!v_ok(a->q, 4, 8) || !v_ok(a->k, 4, 8) || !v_ok(a->b, 4, 8) || !v_ok(a->v, 4, 8) || !v_ok(a->w, 4, 8))
+    return false;
+  if (!v_ok(a->g, 4, 16) || !v_ok(a->out, 8, 16)) return false;
+  if (a->fuse_epilogue && !v_ok(a->gate, 8, 16)) return false;
+  return true;
+}
+
+static size_t tc_workspace_bytes(const gdn2_dims& d) {
+  const size_t nch = (size_t)d.batch * d.num_v_heads * ((d.seq_len + TC_C - 1) / TC_C);
+  return nch * tc_record_layout(d.head_v_dim).bytes;
+}
+
+static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, const char* fn) {
+  const gdn2_dims& d = a->dims;
+  const size_t need = tc_workspace_bytes(d);
+  if (wsb < need) return set_error(GDN2_EWORKSPACE, "%s: workspace %zu bytes < required %zu", fn, wsb, need);
+  p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.V = d.head_v_dim;
+  p.NC = (d.seq_len + TC_C - 1) / TC_C;
+  p.rep = a->key_heads_grouped ? d.num_v_heads / d.num_heads : 1;
+  p.vt = d.head_v_dim;
+  p.vsplit = 1;
+  p.scale = a->scale; p.eps = a->norm_eps;
+  p.fuse_epilogue = a->fuse_epilogue;
+  p.q = make_dview(a->q); p.k = make_dview(a->k); p.v = make_dview(a->v);
+  p.g = make_dview(a->g); p.b = make_dview(a->b); p.w = make_dview(a->w);
+  p.gate = make_dview(a->gate); p.out = make_dview(a->out);
+  p.onw = a->o_norm_weight;
+  p.state = a->state;
+  p.rec = static_cast<unsigned char*>(ws);
+  p.rec_bytes = tc_record_layout(d.head_v_dim).bytes;
+  p.o_ws = nullptr;
   return GDN2_OK;
 }
 
@@ -65,7 +115,7 @@ static int prep_chunk(const gdn2_chunk_args* a, void* ws, size_t wsb, ChunkParam
   const int C = a->chunk_size < CP ? a->chunk_size : CP;
   const ChunkWorkspace L = chunk_workspace_layout(d.batch, d.num_v_heads, d.seq_len, d.head_k_dim, d.head_v_dim, C);
   if (!ws) return set_error(GDN2_EINVAL, "%s: null workspace", fn);
-  if (wsb < L.total * sizeof(float))
+  if (!use_tc(a) && wsb < L.total * sizeof(float))
     return set_error(GDN2_EWORKSPACE, "%s: workspace %zu bytes < required %zu", fn, wsb, L.total * sizeof(float));
   if (((uintptr_t)ws & 255u) != 0) return set_error(GDN2_EINVAL, "%s: workspace must be 256-byte aligned", fn);
   p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.K = d.head_k_dim; p.V = d.head_v_dim;
@@ -99,12 +149,14 @@ int gdn2_read_device_errors(uint32_t* flags) {
   if (!flags) return set_error(GDN2_EINVAL, "gdn2_read_device_errors: null flags");
   int rc = check_cuda(cudaDeviceSynchronize(), "gdn2_read_device_errors");
   if (rc) return rc;
-  *flags = read_device_errors_recurrent() | read_device_errors_selftest();
+  *flags = read_device_errors_recurrent() | read_device_errors_selftest() | read_device_errors_intra_tc() |
+           read_device_errors_inter_tc();
   return GDN2_OK;
 }
 
 size_t gdn2_chunk_fwd_workspace_bytes(const gdn2_chunk_args* a) {
   if (!a || a->chunk_size <= 0 || a->dims.batch <= 0 || a->dims.seq_len <= 0) return 0;
+  if (use_tc(a)) return tc_workspace_bytes(a->dims);
   const int C = a->chunk_size < CP ? a->chunk_size : CP;
   return chunk_workspace_layout(a->dims.batch, a->dims.num_v_heads, a->dims.seq_len, a->dims.head_k_dim,
                                 a->dims.head_v_dim, C)
@@ -116,6 +168,12 @@ int gdn2_chunk_intra(const gdn2_chunk_args* a, void* ws, size_t wsb, void* strea
   ChunkParams p;
   int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_intra");
   if (rc) return rc;
+  if (use_tc(a)) {
+    TcParams t;
+    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_intra");
+    if (rc) return rc;
+    return launch_intra_tc(t, (cudaStream_t)stream);
+  }
   return launch_intra_simt(p, a->dtype, (cudaStream_t)stream);
 }
 
@@ -123,6 +181,12 @@ int gdn2_chunk_inter(const gdn2_chunk_args* a, void* ws, size_t wsb, void* strea
   ChunkParams p;
   int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_inter");
   if (rc) return rc;
+  if (use_tc(a)) {
+    TcParams t;
+    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_inter");
+    if (rc) return rc;
+    return launch_inter_tc(t, (cudaStream_t)stream);
+  }
   rc = launch_inter_simt(p, (cudaStream_t)stream);
   if (rc) return rc;
   return launch_chunk_out(p, a->dtype, (cudaStream_t)stream);
@@ -132,6 +196,14 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream)
   ChunkParams p;
   int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_fwd");
   if (rc) return rc;
+  if (use_tc(a)) {
+    TcParams t;
+    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_fwd");
+    if (rc) return rc;
+    rc = launch_intra_tc(t, (cudaStream_t)stream);
+    if (rc) return rc;
+    return launch_inter_tc(t, (cudaStream_t)stream);
+  }
   rc = launch_intra_simt(p, a->dtype, (cudaStream_t)stream);
   if (rc) return rc;
   rc = launch_inter_simt(p, (cudaStream_t)stream);

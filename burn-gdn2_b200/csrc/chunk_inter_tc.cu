@@ -1,0 +1,309 @@
+// Kernel (2) on tensor cores: chunk-inter for bf16 inputs, K = 128, C = 64,
+// with the SiLU-gated RMS-norm epilogue fused.
+//
+// Replaces gdn2_chunk_inter_kernel (src/kernel/chunk_cube.rs:300-610); math
+// of src/forward.rs:263-274 with the epilogue of src/module.rs:501-517.
+// One CTA (8 warps) per (value head, batch) walks the chunks in order.  The
+// state S [K][V] stays in TMEM in f32 for the whole sequence; a bf16 image
+// of it in shared memory is the MMA operand.  Per chunk:
+//   MMA1  D = [W; Qg] S                    (M=128, N=V, K=128)
+//   v_new = U - (W S)                      (rows 0..63 of D, to smem, bf16)
+//   MMA2  D += [0; Aqk] v_new              (rows 64..127 become o)
+//   MMA3  S = diag(gamma_last) S + Kd^T v_new   (S pre-scaled in TMEM)
+//   o -> gated RMS norm -> out; S -> bf16 image for the next chunk.
+// The per-chunk record written by the intra kernel (operand-tile images)
+// arrives by bulk copies into one of two stages while the previous chunk
+// computes.
+#include "chunk_tc.cuh"
+#include "umma.cuh"
+
+namespace gdn2 {
+
+namespace inter_smem {
+constexpr uint32_t ST_WQ = 0;         // K-major [128][128]
+constexpr uint32_t ST_TA = 32768;     // K-major [128][64]: rows 0..63 zero, 64..127 Aqk
+constexpr uint32_t ST_KD = 49152;     // MN-major [64][128]
+constexpr uint32_t ST_U = 65536;      // bf16 [64][V], V <= 128
+constexpr uint32_t ST_GL = 81920;     // f32 [128]
+constexpr uint32_t STAGE = 82944;     // 81 KB per stage
+constexpr uint32_t S_IMG = 2 * STAGE;           // MN-major [128][V]
+constexpr uint32_t VN_IMG = S_IMG + 32768;      // MN-major [64][V]
+constexpr uint32_t MISC = VN_IMG + 16384;       // rms partials [64][2], barriers, tmem slot
+constexpr uint32_t TOTAL = MISC + 512 + 64;
+}  // namespace inter_smem
+
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
+  using namespace inter_smem;
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  float* sRms = reinterpret_cast<float*>(sm + MISC);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + MISC + 512);  // full[2], mma1, mma2
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
+
+  const int hv = blockIdx.y, bb = blockIdx.z;
+  const int V = p.V, HALF = V / 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sp = warp & 3, half = warp >> 2;
+  const int col0 = half * HALF;
+  const TcRecord L = tc_record_layout(V);
+  const unsigned char* recs = p.rec + ((size_t)bb * p.HV + hv) * p.NC * p.rec_bytes;
+  float* st = p.state + ((size_t)bb * p.HV + hv) * (size_t)TC_K * V;
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 256);
+    umma::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  // zero halves of the [0; Aqk] tiles (never written by the copies)
+  for (int i = tid; i < 2 * 8192 / 16; i += 256) {
+    const int s = i / (8192 / 16), o = i % (8192 / 16);
+    reinterpret_cast<uint4*>(sm + s * STAGE + ST_TA)[o] = make_uint4(0, 0, 0, 0);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tD = *tslot;    // D: cols [0, V)
+  const uint32_t tS = tD + V;    // S master: cols [V, 2V)
+
+  auto issue = [&](int c) {  // thread 0: record of chunk c into stage c & 1
+    const int s = c & 1;
+    const unsigned char* r = recs + (size_t)c * p.rec_bytes;
+    unsigned char* d = sm + s * STAGE;
+    const unsigned ub = 64u * V * 2u;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&bars[s], 32768u + 8192u + 16384u + ub + 512u);
+    bulk_g2s(d + ST_WQ, r + L.wq, 32768u, &bars[s]);
+    bulk_g2s(d + ST_TA + 8192, r + L.aqk, 8192u, &bars[s]);
+    bulk_g2s(d + ST_KD, r + L.kd, 16384u, &bars[s]);
+    bulk_g2s(d + ST_U, r + L.u, ub, &bars[s]);
+    bulk_g2s(d + ST_GL, r + L.gl, 512u, &bars[s]);
+  };
+  if (tid == 0) issue(0);
+
+  // ---- initial state: f32 master in TMEM, bf16 image in smem ----
+  const int kk = 32 * sp + lane;  // key channel = TMEM lane of this thread
+  for (int c16 = 0; c16 < HALF / 16; ++c16) {
+    const int col = col0 + 16 * c16;
+    float v[16];
+    const float4* src = reinterpret_cast<const float4*>(st + (size_t)kk * V + col);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 f = src[j];
+      v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+    }
+    umma::st16(umma::taddr(tS, 32 * sp, col), v);
+    uint4 lo, hi;
+    lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
+    lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
+    hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
+    hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
+    *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8, TC_K)) = lo;
+    *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8 + 1, TC_K)) = hi;
+  }
+  umma::wait_st();
+  fence_proxy_async_smem();
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+
+  const uint32_t i1 = umma::idesc_bf16(128, V, false, true);  // [W;Qg] . S and [0;Aqk] . v_new
+  const uint32_t i3 = umma::idesc_bf16(128, V, true, true);   // Kd^T . v_new
+
+  for (int c = 0; c < p.NC; ++c) {
+    const int s = c & 1;
+    const int t0 = c * TC_C;
+    const int cv = min(TC_C, p.T - t0);
+    unsigned char* stg = sm + s * STAGE;
+    if (tid == 0 && c + 1 < p.NC) issue(c + 1);
+    mbar_wait_bounded(&bars[s], (c >> 1) & 1);
+    umma::fence_after_sync();
+
+    // MMA1: D = [W; Qg] S
+    if (tid == 0) {
+      #pragma unroll
+      for (int j = 0; j < 8; ++j)
+        umma::mma_bf16(tD, umma::desc_kmaj(sbase + s * STAGE + ST_WQ, 128, j),
+                       umma::desc_mnmaj(sbase + S_IMG, TC_K, j), i1, j > 0);
+      umma::commit(&bars[2]);
+    }
+    // meanwhile: S <- diag(gamma_last) S in TMEM
+    {
+      const float gam = reinterpret_cast<const float*>(stg + ST_GL)[kk];
+      for (int c16 = 0; c16 < HALF / 16; ++c16) {
+        const uint32_t a = umma::taddr(tS, 32 * sp, col0 + 16 * c16);
+        float v[16];
+        umma::ld16(a, v);
+        umma::wait_ld();
+        #pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] *= gam;
+        umma::st16(a, v);
+      }
+      umma::wait_st();
+    }
+    // gate of this chunk's rows (epilogue warps), prefetched during MMA1
+    uint4 graw[8];
+    const int orow = 32 * (sp - 2) + lane;  // o row for sp = 2, 3
+    if (sp >= 2 && p.fuse_epilogue && orow < cv) {
+      const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
+                                (int64_t)(t0 + orow) * p.gate.s2 + col0;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (16 * j < 2 * HALF) graw[j] = reinterpret_cast<const uint4*>(gp)[j];
+    }
+    mbar_wait_bounded(&bars[2], c & 1);
+    umma::fence_after_sync();
+
+    // v_new = U - W S  (rows 0..63 of D: sub-partitions 0, 1)
+    if (sp < 2) {
+      const int r = 32 * sp + lane;
+      const __nv_bfloat16* urow = reinterpret_cast<const __nv_bfloat16*>(stg + ST_U) + (size_t)r * V + col0;
+      for (int c16 = 0; c16 < HALF / 16; ++c16) {
+        float v[16];
+        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), v);
+        umma::wait_ld();
+        const uint4 u0 = reinterpret_cast<const uint4*>(urow + 16 * c16)[0];
+        const uint4 u1 = reinterpret_cast<const uint4*>(urow + 16 * c16)[1];
+        const __nv_bfloat162* uh0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
+        const __nv_bfloat162* uh1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+        float vn[16];
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          vn[2 * j] = __low2float(uh0[j]) - v[2 * j];
+          vn[2 * j + 1] = __high2float(uh0[j]) - v[2 * j + 1];
+          vn[8 + 2 * j] = __low2float(uh1[j]) - v[8 + 2 * j];
+          vn[8 + 2 * j + 1] = __high2float(uh1[j]) - v[8 + 2 * j + 1];
+        }
+        uint4 lo, hi;
+        lo.x = umma::pack_bf16x2(vn[0], vn[1]); lo.y = umma::pack_bf16x2(vn[2], vn[3]);
+        lo.z = umma::pack_bf16x2(vn[4], vn[5]); lo.w = umma::pack_bf16x2(vn[6], vn[7]);
+        hi.x = umma::pack_bf16x2(vn[8], vn[9]); hi.y = umma::pack_bf16x2(vn[10], vn[11]);
+        hi.z = umma::pack_bf16x2(vn[12], vn[13]); hi.w = umma::pack_bf16x2(vn[14], vn[15]);
+        const int col = col0 + 16 * c16;
+        *reinterpret_cast<uint4*>(sm + VN_IMG + umma::mnmaj_chunk(r, col / 8, TC_C)) = lo;
+        *reinterpret_cast<uint4*>(sm + VN_IMG + umma::mnmaj_chunk(r, col / 8 + 1, TC_C)) = hi;
+      }
+    }
+    fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+
+    // MMA2: D += [0; Aqk] v_new ; MMA3: S += Kd^T v_new
+    if (tid == 0) {
+      #pragma unroll
+      for (int j = 0; j < 4; ++j)
+        umma::mma_bf16(tD, umma::desc_kmaj(sbase + s * STAGE + ST_TA, 128, j),
+                       umma::desc_mnmaj(sbase + VN_IMG, TC_C, j), i1, true);
+      #pragma unroll
+      for (int j = 0; j < 4; ++j)
+        umma::mma_bf16(tS, umma::desc_mnmaj(sbase + s * STAGE + ST_KD, TC_C, j),
+                       umma::desc_mnmaj(sbase + VN_IMG, TC_C, j), i3, true);
+      umma::commit(&bars[3]);
+    }
+    mbar_wait_bounded(&bars[3], c & 1);
+    umma::fence_after_sync();
+
+    // epilogue: o = rows 64..127 of D (sub-partitions 2, 3)
+    if (sp >= 2) {
+      float ov[64];
+      float ss = 0.f;
+      #pragma unroll
+      for (int c16 = 0; c16 < 4; ++c16) {
+        if (16 * c16 < HALF) {
+          float v[16];
+          umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), v);
+          umma::wait_ld();
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            ov[16 * c16 + j] = v[j];
+            ss += v[j] * v[j];
+          }
+        }
+      }
+      sRms[orow * 2 + half] = ss;
+      named_bar(1, 128);
+      const float rms = sqrtf((sRms[orow * 2] + sRms[orow * 2 + 1]) / (float)V + p.eps);
+      if (orow < cv) {
+        __nv_bfloat16* op = static_cast<__nv_bfloat16*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 +
+                            hv * p.out.s1 + (int64_t)(t0 + orow) * p.out.s2 + col0;
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (16 * j >= 2 * HALF) break;
+          float y[8];
+          const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&graw[j]);
+          #pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float o = ov[8 * j + e];
+            if (p.fuse_epilogue) {
+              const float gt = (e & 1) ? __high2float(gh[e >> 1]) : __low2float(gh[e >> 1]);
+              y[e] = o / rms * p.onw[col0 + 8 * j + e] * silu_f(gt);
+            } else {
+              y[e] = o;
+            }
+          }
+          uint4 pk;
+          pk.x = umma::pack_bf16x2(y[0], y[1]); pk.y = umma::pack_bf16x2(y[2], y[3]);
+          pk.z = umma::pack_bf16x2(y[4], y[5]); pk.w = umma::pack_bf16x2(y[6], y[7]);
+          reinterpret_cast<uint4*>(op)[j] = pk;
+        }
+      }
+    }
+    // S (now S_{c+1}) -> bf16 image for the next chunk
+    for (int c16 = 0; c16 < HALF / 16; ++c16) {
+      const int col = col0 + 16 * c16;
+      float v[16];
+      umma::ld16(umma::taddr(tS, 32 * sp, col), v);
+      umma::wait_ld();
+      uint4 lo, hi;
+      lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
+      lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
+      hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
+      hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
+      *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8, TC_K)) = lo;
+      *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8 + 1, TC_K)) = hi;
+    }
+    fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+  }
+
+  // ---- final state back to HBM (f32, in place) ----
+  for (int c16 = 0; c16 < HALF / 16; ++c16) {
+    const int col = col0 + 16 * c16;
+    float v[16];
+    umma::ld16(umma::taddr(tS, 32 * sp, col), v);
+    umma::wait_ld();
+    float4* dst = reinterpret_cast<float4*>(st + (size_t)kk * V + col);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tD, 256);
+}
+
+int launch_inter_tc(const TcParams& p, cudaStream_t st) {
+  const size_t smem = inter_smem::TOTAL + 1024;
+  cudaError_t e = cudaFuncSetAttribute((const void*)k_inter_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "chunk inter (tc) smem attribute");
+  dim3 grid(1, p.HV, p.B);
+  k_inter_tc<<<grid, 256, smem, st>>>(p);
+  return check_cuda(cudaGetLastError(), "chunk inter (tc) launch");
+}
+
+bool tc_supported(int K, int V, int C, int dtype) {
+  return dtype == GDN2_DTYPE_BF16 && K == TC_K && C == TC_C && (V == 64 || V == 128);
+}
+
+GDN2_DEVICE_ERROR_READER(read_device_errors_inter_tc)
+
+}  // namespace gdn2

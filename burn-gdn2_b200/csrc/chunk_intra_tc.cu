@@ -1,0 +1,362 @@
+// Kernel (1) on tensor cores: chunk-intra for bf16 inputs, K = 128, C = 64.
+//
+// Replaces gdn2_chunk_intra_kernel (src/kernel/chunk_cube.rs:27-295) with the
+// numerics of the tensor path src/forward.rs:86-261 (tile-local decay).
+// One CTA (4 warps) per (chunk, value head, batch):
+//
+//  1. warp p owns the 16-row tile p, lane l owns key channels 4l..4l+3:
+//     tile-local cumsum gl of g, tile boundaries Gb_p, G_last.
+//  2. Score operands in shared memory (bf16, 128-byte swizzle):
+//       X_p  = [q e^{gl} ; b k e^{gl}] of tile p          (32 x 128)
+//       Ks_p = k e^{Gb_p - G} for rows s < 16(p+1)        (reference point
+//              Gb_p for all columns of row tile p, so no factor exceeds
+//              16 tokens of decay, forward.rs:131-157)
+//  3. Four M=64 N=32 K=128 MMAs: D_p = Ks_p X_p^T = [Aqk^T | Akk^T] columns of
+//     row tile p, accumulated in TMEM.
+//  4. While they run: Qg = scale q gamma, Kd = k e^{G_last - G},
+//     rhs_k = b k gamma, rhs_v = w v, gamma_last (forward.rs:189-190, :266-274).
+//  5. Aqk (scaled, causal) and Akk (strict) back from TMEM; (I + Akk)^-1 by
+//     blocked forward substitution over 16x16 tiles (forward.rs:192-261).
+//  6. Two M=64 MMAs: W = (I+Akk)^-1 rhs_k, U = (I+Akk)^-1 rhs_v.
+//  7. The record (chunk_tc.cuh) is written as operand-tile images.
+#include "chunk_tc.cuh"
+#include "umma.cuh"
+
+namespace gdn2 {
+
+namespace intra_smem {
+constexpr uint32_t X = 0;               // 4 x 8 KB: K-major [32][128] per row tile
+constexpr uint32_t KSV = 32768;         // Ks_p at KSV + 4096 * p(p+1)/2, [16(p+1)][128]
+constexpr uint32_t R1_END = 73728;      // 72 KB
+// reused after the score MMAs completed
+constexpr uint32_t AKK = 0;             // f32 [64][65]
+constexpr uint32_t TINV = 17408;        // f32 [64][65]
+constexpr uint32_t AQK_IMG = 36864;     // bf16 K-major [64][64]
+constexpr uint32_t TINV_IMG = 45056;    // bf16 K-major [64][64]
+constexpr uint32_t SCRATCH = 53248;     // 4 x f32 [16][17]
+constexpr uint32_t RK = R1_END;         // bf16 MN-major [64][128]
+constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][V], V <= 128
+constexpr uint32_t MISC = RV + 16384;   // sTot [4][128] f32, sGlast [128] f32, barriers, tmem base
+constexpr uint32_t TOTAL = MISC + 2048 + 512 + 64;
+}  // namespace intra_smem
+
+__device__ __forceinline__ void ld4_bf16(const DView& v, int bb, int h, int t, int c, bool ok, float (&x)[4]) {
+  if (ok) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + h * v.s1 +
+                                                      (int64_t)t * v.s2 + c);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
+  } else {
+    x[0] = x[1] = x[2] = x[3] = 0.f;
+  }
+}
+
+__device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
+  return make_uint2(umma::pack_bf16x2(a, b), umma::pack_bf16x2(c, d));
+}
+
+__global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
+  using namespace intra_smem;
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  float* sTot = reinterpret_cast<float*>(sm + MISC);
+  float* sGlast = sTot + 4 * 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sGlast + 128);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+
+  const int c = blockIdx.x, hv = blockIdx.y, bb = blockIdx.z;
+  const int kh = hv / p.rep;
+  const int t0 = c * TC_C;
+  const int cv = min(TC_C, p.T - t0);
+  const int V = p.V;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tp = warp;       // row tile
+  const int ch = lane * 4;   // first of 4 key channels
+  const int lt = (cv - 1) >> 4, lr = (cv - 1) & 15;
+  unsigned char* rec = p.rec + (((size_t)bb * p.HV + hv) * p.NC + c) * p.rec_bytes;
+  const TcRecord L = tc_record_layout(V);
+
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 256);
+    umma::tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+
+  // ---- 1. tile-local cumsum of g ----
+  float gl[16][4];
+  {
+    float run[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int r = tp * 16 + i;
+      float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < cv) gv = *reinterpret_cast<const float4*>(gbase + (int64_t)(t0 + r) * p.g.s2);
+      run[0] += gv.x; run[1] += gv.y; run[2] += gv.z; run[3] += gv.w;
+      gl[i][0] = run[0]; gl[i][1] = run[1]; gl[i][2] = run[2]; gl[i][3] = run[3];
+    }
+    *reinterpret_cast<float4*>(sTot + tp * 128 + ch) = make_float4(run[0], run[1], run[2], run[3]);
+  }
+  __syncthreads();
+  float Gb[4][4];  // Gb[pp][j]: G at the end of tile pp-1 (0 for pp = 0)
+  #pragma unroll
+  for (int j = 0; j < 4; ++j) Gb[0][j] = 0.f;
+  #pragma unroll
+  for (int pp = 1; pp < 4; ++pp) {
+    const float4 t = *reinterpret_cast<const float4*>(sTot + (pp - 1) * 128 + ch);
+    Gb[pp][0] = Gb[pp - 1][0] + t.x; Gb[pp][1] = Gb[pp - 1][1] + t.y;
+    Gb[pp][2] = Gb[pp - 1][2] + t.z; Gb[pp][3] = Gb[pp - 1][3] + t.w;
+  }
+  if (tp == lt) {
+    float gsel[4] = {0.f, 0.f, 0.f, 0.f};
+    #pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i == lr) {
+        gsel[0] = gl[i][0]; gsel[1] = gl[i][1]; gsel[2] = gl[i][2]; gsel[3] = gl[i][3];
+      }
+    *reinterpret_cast<float4*>(sGlast + ch) =
+        make_float4(Gb[tp][0] + gsel[0], Gb[tp][1] + gsel[1], Gb[tp][2] + gsel[2], Gb[tp][3] + gsel[3]);
+  }
+  float Gbp[4];
+  #pragma unroll
+  for (int j = 0; j < 4; ++j) Gbp[j] = tp == 0 ? Gb[0][j] : tp == 1 ? Gb[1][j] : tp == 2 ? Gb[2][j] : Gb[3][j];
+
+  // ---- 2. score operands ----
+  #pragma unroll 2
+  for (int i = 0; i < 16; ++i) {
+    const int r = tp * 16 + i;
+    const bool ok = r < cv;
+    float q[4], k[4], b[4];
+    ld4_bf16(p.q, bb, kh, t0 + r, ch, ok, q);
+    ld4_bf16(p.k, bb, kh, t0 + r, ch, ok, k);
+    ld4_bf16(p.b, bb, kh, t0 + r, ch, ok, b);
+    float e[4], qs[4], bks[4];
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      e[j] = expf(gl[i][j]);
+      qs[j] = q[j] * e[j];
+      bks[j] = b[j] * k[j] * e[j];
+    }
+    unsigned char* xt = sm + X + tp * 8192;
+    *reinterpret_cast<uint2*>(xt + umma::kmaj_off(i, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
+    *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + i, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
+    #pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      if (pp < tp) continue;
+      float ks[4];
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float gbpp = pp == 0 ? Gb[0][j] : pp == 1 ? Gb[1][j] : pp == 2 ? Gb[2][j] : Gb[3][j];
+        ks[j] = k[j] * expf(gbpp - Gbp[j] - gl[i][j]);
+      }
+      unsigned char* kt = sm + KSV + 4096 * (pp * (pp + 1) / 2);
+      *reinterpret_cast<uint2*>(kt + umma::kmaj_off(r, ch, 16 * (pp + 1))) = pack4(ks[0], ks[1], ks[2], ks[3]);
+    }
+  }
+  fence_proxy_async_smem();
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tA = *tslot;
+
+  // ---- 3. score MMAs ----
+  if (tid == 0) {
+    const uint32_t idesc = umma::idesc_bf16(64, 32, false, false);
+    const uint32_t sbase = smem_u32(sm);
+    #pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      const uint32_t ks = sbase + KSV + 4096 * (pp * (pp + 1) / 2);
+      const uint32_t xs = sbase + X + pp * 8192;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j)
+        umma::mma_bf16(tA + 32 * pp, umma::desc_kmaj(ks, 16 * (pp + 1), j), umma::desc_kmaj(xs, 32, j), idesc, j > 0);
+    }
+    umma::commit(&bars[0]);
+  }
+
+  // ---- 4. operands of the recurrence (overlaps the MMAs) ----
+  const float glast[4] = {sGlast[ch], sGlast[ch + 1], sGlast[ch + 2], sGlast[ch + 3]};
+  if (tp == 0)
+    *reinterpret_cast<float4*>(rec + L.gl + ch * 4) =
+        make_float4(expf(glast[0]), expf(glast[1]), expf(glast[2]), expf(glast[3]));
+  #pragma unroll 2
+  for (int i = 0; i < 16; ++i) {
+    const int r = tp * 16 + i;
+    const bool ok = r < cv;
+    float q[4], k[4], b[4];
+    ld4_bf16(p.q, bb, kh, t0 + r, ch, ok, q);
+    ld4_bf16(p.k, bb, kh, t0 + r, ch, ok, k);
+    ld4_bf16(p.b, bb, kh, t0 + r, ch, ok, b);
+    float qg[4], rk[4], kd[4];
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float G = Gbp[j] + gl[i][j];
+      const float gam = expf(G);
+      qg[j] = q[j] * gam * p.scale;
+      rk[j] = b[j] * k[j] * gam;
+      kd[j] = k[j] * expf(glast[j] - G);
+    }
+    *reinterpret_cast<uint2*>(rec + L.wq + umma::kmaj_off(64 + r, ch, 128)) = pack4(qg[0], qg[1], qg[2], qg[3]);
+    *reinterpret_cast<uint2*>(rec + L.kd + umma::mnmaj_off(r, ch, 64)) = pack4(kd[0], kd[1], kd[2], kd[3]);
+    *reinterpret_cast<uint2*>(sm + RK + umma::mnmaj_off(r, ch, 64)) = pack4(rk[0], rk[1], rk[2], rk[3]);
+    for (int col = ch; col < V; col += 128) {
+      float vv[4], ww[4];
+      ld4_bf16(p.v, bb, hv, t0 + r, col, ok, vv);
+      ld4_bf16(p.w, bb, hv, t0 + r, col, ok, ww);
+      *reinterpret_cast<uint2*>(sm + RV + umma::mnmaj_off(r, col, 64)) =
+          pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
+    }
+  }
+
+  // ---- 5. scores back from TMEM ----
+  mbar_wait_bounded(&bars[0], 0);
+  umma::fence_after_sync();
+  float* sAkk = reinterpret_cast<float*>(sm + AKK);
+  float* sTinv = reinterpret_cast<float*>(sm + TINV);
+  {
+    const int s = 16 * warp + lane;  // valid for lane < 16 (M = 64 TMEM layout)
+    #pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      float vq[16], vk[16];
+      umma::ld16(umma::taddr(tA, 32 * warp, 32 * pp), vq);
+      umma::ld16(umma::taddr(tA, 32 * warp, 32 * pp + 16), vk);
+      umma::wait_ld();
+      if (lane < 16) {
+        #pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int r = 16 * pp + j;
+          const float aq = (s <= r) ? vq[j] * p.scale : 0.f;
+          *reinterpret_cast<__nv_bfloat16*>(sm + AQK_IMG + umma::kmaj_off(r, s, 64)) = __float2bfloat16_rn(aq);
+          sAkk[r * 65 + s] = (s < r) ? vk[j] : 0.f;
+        }
+      }
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+
+  // ---- 6. (I + Akk)^-1, blocked over 16 x 16 tiles ----
+  if (lane < 16) {  // diagonal tile `warp`, column `lane`
+    const int o = 16 * warp, j = lane;
+    float x[16];
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float acc = 0.f;
+      #pragma unroll
+      for (int m = 0; m < i; ++m) acc += sAkk[(o + i) * 65 + o + m] * x[m];
+      x[i] = (i == j) ? 1.f : ((i < j) ? 0.f : -acc);
+    }
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) sTinv[(o + i) * 65 + o + j] = x[i];
+  }
+  __syncthreads();
+  float* scr = reinterpret_cast<float*>(sm + SCRATCH) + warp * 16 * 17;
+  for (int d = 1; d < 4; ++d) {
+    const int bi = warp + d, bj = warp;
+    if (bi < 4) {
+      const int row = lane >> 1, c0 = (lane & 1) * 8;
+      float tmp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int m = 16 * bj; m < 16 * bi; ++m) {
+        const float a = sAkk[(16 * bi + row) * 65 + m];
+        #pragma unroll
+        for (int cc = 0; cc < 8; ++cc) tmp[cc] += a * sTinv[m * 65 + 16 * bj + c0 + cc];
+      }
+      #pragma unroll
+      for (int cc = 0; cc < 8; ++cc) scr[row * 17 + c0 + cc] = tmp[cc];
+      __syncwarp();
+      float res[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int m = 0; m < 16; ++m) {
+        const float li = sTinv[(16 * bi + row) * 65 + 16 * bi + m];
+        #pragma unroll
+        for (int cc = 0; cc < 8; ++cc) res[cc] -= li * scr[m * 17 + c0 + cc];
+      }
+      #pragma unroll
+      for (int cc = 0; cc < 8; ++cc) sTinv[(16 * bi + row) * 65 + 16 * bj + c0 + cc] = res[cc];
+    }
+    __syncthreads();
+  }
+  for (int idx = tid; idx < 64 * 64; idx += 128) {
+    const int r = idx >> 6, s = idx & 63;
+    const float val = (s == r) ? 1.f : ((s < r) ? sTinv[r * 65 + s] : 0.f);
+    *reinterpret_cast<__nv_bfloat16*>(sm + TINV_IMG + umma::kmaj_off(r, s, 64)) = __float2bfloat16_rn(val);
+  }
+  fence_proxy_async_smem();
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+
+  // ---- 7. W = T^-1 rhs_k, U = T^-1 rhs_v ----
+  if (tid == 0) {
+    const uint32_t sbase = smem_u32(sm);
+    const uint32_t iw = umma::idesc_bf16(64, 128, false, true);
+    const uint32_t iu = umma::idesc_bf16(64, V, false, true);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j)
+      umma::mma_bf16(tA, umma::desc_kmaj(sbase + TINV_IMG, 64, j), umma::desc_mnmaj(sbase + RK, 64, j), iw, j > 0);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j)
+      umma::mma_bf16(tA + 128, umma::desc_kmaj(sbase + TINV_IMG, 64, j), umma::desc_mnmaj(sbase + RV, 64, j), iu,
+                     j > 0);
+    umma::commit(&bars[1]);
+  }
+  // Aqk image to the record while the MMAs run
+  for (int idx = tid; idx < 64 * 64 * 2 / 16; idx += 128)
+    reinterpret_cast<uint4*>(rec + L.aqk)[idx] = reinterpret_cast<const uint4*>(sm + AQK_IMG)[idx];
+  mbar_wait_bounded(&bars[1], 0);
+  umma::fence_after_sync();
+  {
+    const int r = 16 * warp + lane;  // valid for lane < 16
+    #pragma unroll
+    for (int c16 = 0; c16 < 8; ++c16) {
+      float v[16];
+      umma::ld16(umma::taddr(tA, 32 * warp, 16 * c16), v);
+      umma::wait_ld();
+      if (lane < 16) {
+        uint4 lo, hi;
+        lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
+        lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
+        hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
+        hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
+        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, 2 * c16, 128)) = lo;
+        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, 2 * c16 + 1, 128)) = hi;
+      }
+    }
+    for (int c16 = 0; c16 < V / 16; ++c16) {
+      float v[16];
+      umma::ld16(umma::taddr(tA, 32 * warp, 128 + 16 * c16), v);
+      umma::wait_ld();
+      if (lane < 16) {
+        const int col = 16 * c16, sl = col / p.vt, cc = col % p.vt;
+        uint4 lo, hi;
+        lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
+        lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
+        hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
+        hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
+        uint4* dst = reinterpret_cast<uint4*>(rec + L.u + ((size_t)sl * 64 * p.vt + (size_t)r * p.vt + cc) * 2);
+        dst[0] = lo;
+        dst[1] = hi;
+      }
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tA, 256);
+}
+
+int launch_intra_tc(const TcParams& p, cudaStream_t st) {
+  const size_t smem = intra_smem::TOTAL + 1024;
+  cudaError_t e = cudaFuncSetAttribute((const void*)k_intra_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "chunk intra (tc) smem attribute");
+  dim3 grid(p.NC, p.HV, p.B);
+  k_intra_tc<<<grid, 128, smem, st>>>(p);
+  return check_cuda(cudaGetLastError(), "chunk intra (tc) launch");
+}
+
+GDN2_DEVICE_ERROR_READER(read_device_errors_intra_tc)
+
+}  // namespace gdn2

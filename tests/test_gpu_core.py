@@ -211,3 +211,62 @@ def test_short_conv_and_rms_norm_gate_kernels():
     y = bg.rms_norm_gate_per_head(t(o), t(gate), t(wn), 1e-5)
     yr = O.rms_norm_gate_per_head(o.astype(np.float64), gate.astype(np.float64), wn.astype(np.float64), 1e-5)
     assert_close(y.cpu().numpy(), yr, what="rms", **F32_TOL)
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 190, 128, 64), (1, 2, 64, 128, 128), (2, 2, 1, 128, 128)])
+def test_chunk_tensor_core_path_bf16(shape):
+    """bf16, K = 128, chunk 64 (the tcgen05 path), V = 64 / 128, full and
+    partial chunks including T = 1; permuted [B,T,H,D] storage views like
+    the module's; random initial state; vs the f64 oracle."""
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = shape
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=91, dtype=np.float32)
+    # storage [B,T,H,D], passed as [B,H,T,D] views
+    d = {n: torch.tensor(np.ascontiguousarray(a.transpose(0, 2, 1, 3)), device=DEV,
+                         dtype=torch.float32 if n == "g" else torch.bfloat16).permute(0, 2, 1, 3)
+         for n, a in arrs.items() if n in "qkvgbw"}
+    s0 = np.random.default_rng(92).standard_normal((B, HV, K, V)).astype(np.float32) * 0.5
+    o, s = bg.chunk_wy_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"],
+                               torch.tensor(s0, device=DEV), K ** -0.5, 64)
+    ref = {n: v.float().cpu().numpy().astype(np.float64) for n, v in d.items()}
+    o_ref, s_ref = O.chunk_wy_forward(ref["q"], ref["k"], ref["v"], ref["g"], ref["b"], ref["w"],
+                                      s0.astype(np.float64), K ** -0.5, 64)
+    assert_close_bf16(o.float().cpu().numpy(), o_ref, what="out")
+    assert_close_bf16(s.cpu().numpy(), s_ref, what="state")
+
+
+def test_chunk_tensor_core_grouped_heads_and_epilogue():
+    """GVA without a materialised repeat (key_heads_grouped = 1: value head
+    hv reads key head hv // 2) and the fused gated RMS-norm epilogue, on the
+    tcgen05 path, vs the oracle (np.repeat over heads + rms_norm_gate)."""
+    import ctypes
+    import burn_gdn2 as bg
+    from burn_gdn2 import ops
+
+    B, H, HV, T, K, V = 2, 2, 4, 130, 128, 128
+    rng = np.random.default_rng(93)
+    kq = O.make_core_inputs(B, H, T, K, V, seed=94, dtype=np.float32)
+    kv = O.make_core_inputs(B, HV, T, K, V, seed=95, dtype=np.float32)
+    gate = rng.standard_normal((B, T, HV, V)).astype(np.float32)
+    onw = rng.uniform(0.5, 1.5, V).astype(np.float32)
+    t = lambda a, dt=torch.bfloat16: torch.tensor(a, device=DEV, dtype=dt)
+    q, k, b = t(kq["q"]), t(kq["k"]), t(kq["b"])
+    g = t(kq["g"], torch.float32)
+    v, w = t(kv["v"]), t(kv["w"])
+    gt = t(gate)
+    st = torch.zeros(B, HV, K, V, device=DEV)
+    out = torch.empty(B, T, HV, V, device=DEV, dtype=torch.bfloat16)
+    a = ops.chunk_args(q, k, v, g, b, w, st, out.permute(0, 2, 1, 3), K ** -0.5, 64, num_heads=H, grouped=True,
+                       gate=gt.permute(0, 2, 1, 3), o_norm_weight=t(onw, torch.float32), norm_eps=1e-5)
+    ws = ops.chunk_workspace(a, DEV)
+    bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a), ops.ptr(ws), ws.numel(), ops.stream_handle()))
+    torch.cuda.synchronize()
+    r = lambda x: x.float().cpu().numpy().astype(np.float64)
+    rep = lambda x: np.repeat(x, HV // H, axis=1)
+    o_ref, s_ref = O.chunk_wy_forward(rep(r(q)), rep(r(k)), r(v), rep(r(g)), rep(r(b)), r(w),
+                                      np.zeros((B, HV, K, V)), K ** -0.5, 64)
+    y_ref = O.rms_norm_gate_per_head(o_ref.transpose(0, 2, 1, 3), r(gt), onw.astype(np.float64), 1e-5)
+    assert_close_bf16(out.float().cpu().numpy(), y_ref, what="gated out")
+    assert_close_bf16(st.cpu().numpy(), s_ref, what="state")
+    assert bg._lib.read_device_errors() == 0
