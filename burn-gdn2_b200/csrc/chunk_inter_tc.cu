@@ -28,8 +28,10 @@ constexpr uint32_t ST_GL = 81920;     // f32 [128]
 constexpr uint32_t STAGE = 82944;     // 81 KB per stage
 constexpr uint32_t S_IMG = 2 * STAGE;           // MN-major [128][V]
 constexpr uint32_t VN_IMG = S_IMG + 32768;      // MN-major [64][V]
-constexpr uint32_t MISC = VN_IMG + 16384;       // rms partials [64][2], barriers, tmem slot
-constexpr uint32_t TOTAL = MISC + 512 + 64;
+constexpr uint32_t MISC = VN_IMG + 16384;       // rms partials [64][2], o-norm weight [V], barriers, tmem slot
+constexpr uint32_t ONW = MISC + 512;
+constexpr uint32_t BARS = ONW + 512;
+constexpr uint32_t TOTAL = BARS + 64;
 }  // namespace inter_smem
 
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
@@ -41,7 +43,8 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
   float* sRms = reinterpret_cast<float*>(sm + MISC);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + MISC + 512);  // full[2], mma1, mma2
+  float* sOnw = reinterpret_cast<float*>(sm + ONW);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);  // full[2], mma1, mma2
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
 
   const int hv = blockIdx.y, bb = blockIdx.z;
@@ -55,9 +58,11 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   const uint32_t sbase = smem_u32(sm);
 
   if (warp == 0) {
-    umma::tmem_alloc(tslot, 256);
+    umma::tmem_alloc(tslot, 512);
     umma::tmem_relinquish();
   }
+  if (p.fuse_epilogue)
+    for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[i];
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
@@ -70,8 +75,8 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
-  const uint32_t tD = *tslot;    // D: cols [0, V)
-  const uint32_t tS = tD + V;    // S master: cols [V, 2V)
+  const uint32_t tD0 = *tslot;   // D of even chunks: cols [0, V); odd chunks: [V, 2V)
+  const uint32_t tS = tD0 + 2 * V;  // S master: cols [2V, 3V)
 
   auto issue = [&](int c) {  // thread 0: record of chunk c into stage c & 1
     const int s = c & 1;
@@ -117,10 +122,69 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   const uint32_t i1 = umma::idesc_bf16(128, V, false, true);  // [W;Qg] . S and [0;Aqk] . v_new
   const uint32_t i3 = umma::idesc_bf16(128, V, true, true);   // Kd^T . v_new
 
-  for (int c = 0; c < p.NC; ++c) {
-    const int s = c & 1;
+  // o rows of chunk c live in rows 64..127 of D[c & 1] (sub-partitions 2, 3);
+  // their epilogue runs while the tensor core does MMA1 of chunk c + 1.
+  auto epilogue = [&](int c) {
     const int t0 = c * TC_C;
     const int cv = min(TC_C, p.T - t0);
+    const uint32_t tD = tD0 + (c & 1) * V;
+    const int orow = 32 * (sp - 2) + lane;
+    float ov[64];
+    #pragma unroll
+    for (int c16 = 0; c16 < 4; ++c16) {
+      float v[16];
+      if (16 * c16 < HALF) {
+        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), v);
+        #pragma unroll
+        for (int j = 0; j < 16; ++j) ov[16 * c16 + j] = v[j];
+      }
+    }
+    umma::wait_ld();
+    uint4 graw[8];
+    if (p.fuse_epilogue && orow < cv) {
+      const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
+                                (int64_t)(t0 + orow) * p.gate.s2 + col0;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (8 * j < HALF) graw[j] = reinterpret_cast<const uint4*>(gp)[j];
+    }
+    float ss = 0.f;
+    #pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (j < HALF) ss += ov[j] * ov[j];
+    sRms[orow * 2 + half] = ss;
+    named_bar(1, 128);
+    const float inv = 1.f / sqrtf((sRms[orow * 2] + sRms[orow * 2 + 1]) / (float)V + p.eps);
+    named_bar(1, 128);  // sRms reusable
+    if (orow < cv) {
+      __nv_bfloat16* op = static_cast<__nv_bfloat16*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
+                          (int64_t)(t0 + orow) * p.out.s2 + col0;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (8 * j >= HALF) break;
+        float y[8];
+        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&graw[j]);
+        #pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float o = ov[8 * j + e];
+          if (p.fuse_epilogue) {
+            const float gt = (e & 1) ? __high2float(gh[e >> 1]) : __low2float(gh[e >> 1]);
+            y[e] = o * inv * sOnw[col0 + 8 * j + e] * silu_f(gt);
+          } else {
+            y[e] = o;
+          }
+        }
+        uint4 pk;
+        pk.x = umma::pack_bf16x2(y[0], y[1]); pk.y = umma::pack_bf16x2(y[2], y[3]);
+        pk.z = umma::pack_bf16x2(y[4], y[5]); pk.w = umma::pack_bf16x2(y[6], y[7]);
+        reinterpret_cast<uint4*>(op)[j] = pk;
+      }
+    }
+  };
+
+  for (int c = 0; c < p.NC; ++c) {
+    const int s = c & 1;
+    const uint32_t tD = tD0 + s * V;
     unsigned char* stg = sm + s * STAGE;
     if (tid == 0 && c + 1 < p.NC) issue(c + 1);
     mbar_wait_bounded(&bars[s], (c >> 1) & 1);
@@ -134,30 +198,25 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
                        umma::desc_mnmaj(sbase + S_IMG, TC_K, j), i1, j > 0);
       umma::commit(&bars[2]);
     }
-    // meanwhile: S <- diag(gamma_last) S in TMEM
+    // meanwhile: S <- diag(gamma_last) S in TMEM (all warps), then the
+    // epilogue of the previous chunk (sub-partitions 2, 3)
     {
       const float gam = reinterpret_cast<const float*>(stg + ST_GL)[kk];
-      for (int c16 = 0; c16 < HALF / 16; ++c16) {
-        const uint32_t a = umma::taddr(tS, 32 * sp, col0 + 16 * c16);
-        float v[16];
-        umma::ld16(a, v);
+      for (int b32 = 0; b32 < HALF; b32 += 32) {
+        float v[2][16];
+        #pragma unroll
+        for (int c16 = 0; c16 < 2; ++c16) umma::ld16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
         umma::wait_ld();
         #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] *= gam;
-        umma::st16(a, v);
+        for (int c16 = 0; c16 < 2; ++c16) {
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) v[c16][j] *= gam;
+          umma::st16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
+        }
       }
       umma::wait_st();
     }
-    // gate of this chunk's rows (epilogue warps), prefetched during MMA1
-    uint4 graw[8];
-    const int orow = 32 * (sp - 2) + lane;  // o row for sp = 2, 3
-    if (sp >= 2 && p.fuse_epilogue && orow < cv) {
-      const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
-                                (int64_t)(t0 + orow) * p.gate.s2 + col0;
-      #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (16 * j < 2 * HALF) graw[j] = reinterpret_cast<const uint4*>(gp)[j];
-    }
+    if (sp >= 2 && c > 0) epilogue(c - 1);
     mbar_wait_bounded(&bars[2], c & 1);
     umma::fence_after_sync();
 
@@ -165,30 +224,34 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     if (sp < 2) {
       const int r = 32 * sp + lane;
       const __nv_bfloat16* urow = reinterpret_cast<const __nv_bfloat16*>(stg + ST_U) + (size_t)r * V + col0;
-      for (int c16 = 0; c16 < HALF / 16; ++c16) {
-        float v[16];
-        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), v);
-        umma::wait_ld();
-        const uint4 u0 = reinterpret_cast<const uint4*>(urow + 16 * c16)[0];
-        const uint4 u1 = reinterpret_cast<const uint4*>(urow + 16 * c16)[1];
-        const __nv_bfloat162* uh0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
-        const __nv_bfloat162* uh1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
-        float vn[16];
+      for (int b32 = 0; b32 < HALF; b32 += 32) {
+        float v[2][16];
         #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          vn[2 * j] = __low2float(uh0[j]) - v[2 * j];
-          vn[2 * j + 1] = __high2float(uh0[j]) - v[2 * j + 1];
-          vn[8 + 2 * j] = __low2float(uh1[j]) - v[8 + 2 * j];
-          vn[8 + 2 * j + 1] = __high2float(uh1[j]) - v[8 + 2 * j + 1];
+        for (int c16 = 0; c16 < 2; ++c16) umma::ld16(umma::taddr(tD, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
+        umma::wait_ld();
+        #pragma unroll
+        for (int c16 = 0; c16 < 2; ++c16) {
+          const int col = col0 + b32 + 16 * c16;
+          const uint4 u0 = reinterpret_cast<const uint4*>(urow + b32 + 16 * c16)[0];
+          const uint4 u1 = reinterpret_cast<const uint4*>(urow + b32 + 16 * c16)[1];
+          const __nv_bfloat162* uh0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
+          const __nv_bfloat162* uh1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+          float vn[16];
+          #pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            vn[2 * j] = __low2float(uh0[j]) - v[c16][2 * j];
+            vn[2 * j + 1] = __high2float(uh0[j]) - v[c16][2 * j + 1];
+            vn[8 + 2 * j] = __low2float(uh1[j]) - v[c16][8 + 2 * j];
+            vn[8 + 2 * j + 1] = __high2float(uh1[j]) - v[c16][8 + 2 * j + 1];
+          }
+          uint4 lo, hi;
+          lo.x = umma::pack_bf16x2(vn[0], vn[1]); lo.y = umma::pack_bf16x2(vn[2], vn[3]);
+          lo.z = umma::pack_bf16x2(vn[4], vn[5]); lo.w = umma::pack_bf16x2(vn[6], vn[7]);
+          hi.x = umma::pack_bf16x2(vn[8], vn[9]); hi.y = umma::pack_bf16x2(vn[10], vn[11]);
+          hi.z = umma::pack_bf16x2(vn[12], vn[13]); hi.w = umma::pack_bf16x2(vn[14], vn[15]);
+          *reinterpret_cast<uint4*>(sm + VN_IMG + umma::mnmaj_chunk(r, col / 8, TC_C)) = lo;
+          *reinterpret_cast<uint4*>(sm + VN_IMG + umma::mnmaj_chunk(r, col / 8 + 1, TC_C)) = hi;
         }
-        uint4 lo, hi;
-        lo.x = umma::pack_bf16x2(vn[0], vn[1]); lo.y = umma::pack_bf16x2(vn[2], vn[3]);
-        lo.z = umma::pack_bf16x2(vn[4], vn[5]); lo.w = umma::pack_bf16x2(vn[6], vn[7]);
-        hi.x = umma::pack_bf16x2(vn[8], vn[9]); hi.y = umma::pack_bf16x2(vn[10], vn[11]);
-        hi.z = umma::pack_bf16x2(vn[12], vn[13]); hi.w = umma::pack_bf16x2(vn[14], vn[15]);
-        const int col = col0 + 16 * c16;
-        *reinterpret_cast<uint4*>(sm + VN_IMG + umma::mnmaj_chunk(r, col / 8, TC_C)) = lo;
-        *reinterpret_cast<uint4*>(sm + VN_IMG + umma::mnmaj_chunk(r, col / 8 + 1, TC_C)) = hi;
       }
     }
     fence_proxy_async_smem();
@@ -211,70 +274,30 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     mbar_wait_bounded(&bars[3], c & 1);
     umma::fence_after_sync();
 
-    // epilogue: o = rows 64..127 of D (sub-partitions 2, 3)
-    if (sp >= 2) {
-      float ov[64];
-      float ss = 0.f;
-      #pragma unroll
-      for (int c16 = 0; c16 < 4; ++c16) {
-        if (16 * c16 < HALF) {
-          float v[16];
-          umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), v);
-          umma::wait_ld();
-          #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            ov[16 * c16 + j] = v[j];
-            ss += v[j] * v[j];
-          }
-        }
-      }
-      sRms[orow * 2 + half] = ss;
-      named_bar(1, 128);
-      const float rms = sqrtf((sRms[orow * 2] + sRms[orow * 2 + 1]) / (float)V + p.eps);
-      if (orow < cv) {
-        __nv_bfloat16* op = static_cast<__nv_bfloat16*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 +
-                            hv * p.out.s1 + (int64_t)(t0 + orow) * p.out.s2 + col0;
-        #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (16 * j >= 2 * HALF) break;
-          float y[8];
-          const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&graw[j]);
-          #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float o = ov[8 * j + e];
-            if (p.fuse_epilogue) {
-              const float gt = (e & 1) ? __high2float(gh[e >> 1]) : __low2float(gh[e >> 1]);
-              y[e] = o / rms * p.onw[col0 + 8 * j + e] * silu_f(gt);
-            } else {
-              y[e] = o;
-            }
-          }
-          uint4 pk;
-          pk.x = umma::pack_bf16x2(y[0], y[1]); pk.y = umma::pack_bf16x2(y[2], y[3]);
-          pk.z = umma::pack_bf16x2(y[4], y[5]); pk.w = umma::pack_bf16x2(y[6], y[7]);
-          reinterpret_cast<uint4*>(op)[j] = pk;
-        }
-      }
-    }
     // S (now S_{c+1}) -> bf16 image for the next chunk
-    for (int c16 = 0; c16 < HALF / 16; ++c16) {
-      const int col = col0 + 16 * c16;
-      float v[16];
-      umma::ld16(umma::taddr(tS, 32 * sp, col), v);
+    for (int b32 = 0; b32 < HALF; b32 += 32) {
+      float v[2][16];
+      #pragma unroll
+      for (int c16 = 0; c16 < 2; ++c16) umma::ld16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
       umma::wait_ld();
-      uint4 lo, hi;
-      lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
-      lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
-      hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
-      hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
-      *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8, TC_K)) = lo;
-      *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8 + 1, TC_K)) = hi;
+      #pragma unroll
+      for (int c16 = 0; c16 < 2; ++c16) {
+        const int col = col0 + b32 + 16 * c16;
+        uint4 lo, hi;
+        lo.x = umma::pack_bf16x2(v[c16][0], v[c16][1]); lo.y = umma::pack_bf16x2(v[c16][2], v[c16][3]);
+        lo.z = umma::pack_bf16x2(v[c16][4], v[c16][5]); lo.w = umma::pack_bf16x2(v[c16][6], v[c16][7]);
+        hi.x = umma::pack_bf16x2(v[c16][8], v[c16][9]); hi.y = umma::pack_bf16x2(v[c16][10], v[c16][11]);
+        hi.z = umma::pack_bf16x2(v[c16][12], v[c16][13]); hi.w = umma::pack_bf16x2(v[c16][14], v[c16][15]);
+        *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8, TC_K)) = lo;
+        *reinterpret_cast<uint4*>(sm + S_IMG + umma::mnmaj_chunk(kk, col / 8 + 1, TC_K)) = hi;
+      }
     }
     fence_proxy_async_smem();
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
   }
+  if (sp >= 2) epilogue(p.NC - 1);
 
   // ---- final state back to HBM (f32, in place) ----
   for (int c16 = 0; c16 < HALF / 16; ++c16) {
@@ -288,7 +311,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   }
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tD, 256);
+  if (warp == 0) umma::tmem_dealloc(tD0, 512);
 }
 
 int launch_inter_tc(const TcParams& p, cudaStream_t st) {

@@ -13,8 +13,9 @@
 //              16 tokens of decay, forward.rs:131-157)
 //  3. Four M=64 N=32 K=128 MMAs: D_p = Ks_p X_p^T = [Aqk^T | Akk^T] columns of
 //     row tile p, accumulated in TMEM.
-//  4. While they run: Qg = scale q gamma, Kd = k e^{G_last - G},
-//     rhs_k = b k gamma, rhs_v = w v, gamma_last (forward.rs:189-190, :266-274).
+//     Qg = scale q gamma, Kd = k e^{G_last - G}, rhs_k = b k gamma and
+//     gamma_last come out of the same pass (forward.rs:189-190, :266-274).
+//  4. While the MMAs run: rhs_v = w v.
 //  5. Aqk (scaled, causal) and Akk (strict) back from TMEM; (I + Akk)^-1 by
 //     blocked forward substitution over 16x16 tiles (forward.rs:192-261).
 //  6. Two M=64 MMAs: W = (I+Akk)^-1 rhs_k, U = (I+Akk)^-1 rhs_v.
@@ -40,17 +41,19 @@ constexpr uint32_t MISC = RV + 16384;   // sTot [4][128] f32, sGlast [128] f32, 
 constexpr uint32_t TOTAL = MISC + 2048 + 512 + 64;
 }  // namespace intra_smem
 
-__device__ __forceinline__ void ld4_bf16(const DView& v, int bb, int h, int t, int c, bool ok, float (&x)[4]) {
-  if (ok) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + h * v.s1 +
-                                                      (int64_t)t * v.s2 + c);
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-    x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
-  } else {
-    x[0] = x[1] = x[2] = x[3] = 0.f;
-  }
+__device__ __forceinline__ uint2 ld4_raw(const DView& v, int bb, int h, int t, int c, bool ok) {
+  if (!ok) return make_uint2(0u, 0u);
+  return *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + h * v.s1 +
+                                         (int64_t)t * v.s2 + c);
 }
+
+__device__ __forceinline__ void unpack4(uint2 raw, float (&x)[4]) {
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+  x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
+}
+
+__device__ __forceinline__ float sGlast_pre(const float* s, int ch, int j) { return s[ch + j]; }
 
 __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
   return make_uint2(umma::pack_bf16x2(a, b), umma::pack_bf16x2(c, d));
@@ -125,39 +128,62 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
   float Gbp[4];
   #pragma unroll
   for (int j = 0; j < 4; ++j) Gbp[j] = tp == 0 ? Gb[0][j] : tp == 1 ? Gb[1][j] : tp == 2 ? Gb[2][j] : Gb[3][j];
+  __syncthreads();  // sGlast
 
-  // ---- 2. score operands ----
-  #pragma unroll 2
-  for (int i = 0; i < 16; ++i) {
-    const int r = tp * 16 + i;
-    const bool ok = r < cv;
-    float q[4], k[4], b[4];
-    ld4_bf16(p.q, bb, kh, t0 + r, ch, ok, q);
-    ld4_bf16(p.k, bb, kh, t0 + r, ch, ok, k);
-    ld4_bf16(p.b, bb, kh, t0 + r, ch, ok, b);
-    float e[4], qs[4], bks[4];
+  // ---- 2. operands from q, k, b (all 16 rows' loads issued up front) ----
+  const float glast[4] = {sGlast_pre(sGlast, ch, 0), sGlast_pre(sGlast, ch, 1), sGlast_pre(sGlast, ch, 2),
+                          sGlast_pre(sGlast, ch, 3)};
+  {
+    uint2 qr[16], kr[16], br[16];
     #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      e[j] = expf(gl[i][j]);
-      qs[j] = q[j] * e[j];
-      bks[j] = b[j] * k[j] * e[j];
+    for (int i = 0; i < 16; ++i) {
+      const int r = tp * 16 + i;
+      qr[i] = ld4_raw(p.q, bb, kh, t0 + r, ch, r < cv);
+      kr[i] = ld4_raw(p.k, bb, kh, t0 + r, ch, r < cv);
+      br[i] = ld4_raw(p.b, bb, kh, t0 + r, ch, r < cv);
     }
     unsigned char* xt = sm + X + tp * 8192;
-    *reinterpret_cast<uint2*>(xt + umma::kmaj_off(i, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
-    *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + i, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
     #pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
-      if (pp < tp) continue;
-      float ks[4];
+    for (int i = 0; i < 16; ++i) {
+      const int r = tp * 16 + i;
+      float q[4], k[4], b[4];
+      unpack4(qr[i], q);
+      unpack4(kr[i], k);
+      unpack4(br[i], b);
+      float qs[4], bks[4], qg[4], rk[4], kd[4];
       #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float gbpp = pp == 0 ? Gb[0][j] : pp == 1 ? Gb[1][j] : pp == 2 ? Gb[2][j] : Gb[3][j];
-        ks[j] = k[j] * expf(gbpp - Gbp[j] - gl[i][j]);
+        const float e = expf(gl[i][j]);
+        const float G = Gbp[j] + gl[i][j];
+        const float gam = expf(G);
+        qs[j] = q[j] * e;
+        bks[j] = b[j] * k[j] * e;
+        qg[j] = q[j] * gam * p.scale;
+        rk[j] = b[j] * k[j] * gam;
+        kd[j] = k[j] * expf(glast[j] - G);
       }
-      unsigned char* kt = sm + KSV + 4096 * (pp * (pp + 1) / 2);
-      *reinterpret_cast<uint2*>(kt + umma::kmaj_off(r, ch, 16 * (pp + 1))) = pack4(ks[0], ks[1], ks[2], ks[3]);
+      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(i, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
+      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + i, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
+      *reinterpret_cast<uint2*>(rec + L.wq + umma::kmaj_off(64 + r, ch, 128)) = pack4(qg[0], qg[1], qg[2], qg[3]);
+      *reinterpret_cast<uint2*>(rec + L.kd + umma::mnmaj_off(r, ch, 64)) = pack4(kd[0], kd[1], kd[2], kd[3]);
+      *reinterpret_cast<uint2*>(sm + RK + umma::mnmaj_off(r, ch, 64)) = pack4(rk[0], rk[1], rk[2], rk[3]);
+      #pragma unroll
+      for (int pp = 0; pp < 4; ++pp) {
+        if (pp < tp) continue;
+        float ks[4];
+        #pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float gbpp = pp == 0 ? Gb[0][j] : pp == 1 ? Gb[1][j] : pp == 2 ? Gb[2][j] : Gb[3][j];
+          ks[j] = k[j] * expf(gbpp - Gbp[j] - gl[i][j]);
+        }
+        unsigned char* kt = sm + KSV + 4096 * (pp * (pp + 1) / 2);
+        *reinterpret_cast<uint2*>(kt + umma::kmaj_off(r, ch, 16 * (pp + 1))) = pack4(ks[0], ks[1], ks[2], ks[3]);
+      }
     }
   }
+  if (tp == 0)
+    *reinterpret_cast<float4*>(rec + L.gl + ch * 4) =
+        make_float4(expf(glast[0]), expf(glast[1]), expf(glast[2]), expf(glast[3]));
   fence_proxy_async_smem();
   umma::fence_before_sync();
   __syncthreads();
@@ -179,37 +205,26 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
     umma::commit(&bars[0]);
   }
 
-  // ---- 4. operands of the recurrence (overlaps the MMAs) ----
-  const float glast[4] = {sGlast[ch], sGlast[ch + 1], sGlast[ch + 2], sGlast[ch + 3]};
-  if (tp == 0)
-    *reinterpret_cast<float4*>(rec + L.gl + ch * 4) =
-        make_float4(expf(glast[0]), expf(glast[1]), expf(glast[2]), expf(glast[3]));
-  #pragma unroll 2
-  for (int i = 0; i < 16; ++i) {
-    const int r = tp * 16 + i;
-    const bool ok = r < cv;
-    float q[4], k[4], b[4];
-    ld4_bf16(p.q, bb, kh, t0 + r, ch, ok, q);
-    ld4_bf16(p.k, bb, kh, t0 + r, ch, ok, k);
-    ld4_bf16(p.b, bb, kh, t0 + r, ch, ok, b);
-    float qg[4], rk[4], kd[4];
+  // ---- 4. rhs_v = w v (overlaps the score MMAs) ----
+  for (int col = ch; col < V; col += 128) {
     #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float G = Gbp[j] + gl[i][j];
-      const float gam = expf(G);
-      qg[j] = q[j] * gam * p.scale;
-      rk[j] = b[j] * k[j] * gam;
-      kd[j] = k[j] * expf(glast[j] - G);
-    }
-    *reinterpret_cast<uint2*>(rec + L.wq + umma::kmaj_off(64 + r, ch, 128)) = pack4(qg[0], qg[1], qg[2], qg[3]);
-    *reinterpret_cast<uint2*>(rec + L.kd + umma::mnmaj_off(r, ch, 64)) = pack4(kd[0], kd[1], kd[2], kd[3]);
-    *reinterpret_cast<uint2*>(sm + RK + umma::mnmaj_off(r, ch, 64)) = pack4(rk[0], rk[1], rk[2], rk[3]);
-    for (int col = ch; col < V; col += 128) {
-      float vv[4], ww[4];
-      ld4_bf16(p.v, bb, hv, t0 + r, col, ok, vv);
-      ld4_bf16(p.w, bb, hv, t0 + r, col, ok, ww);
-      *reinterpret_cast<uint2*>(sm + RV + umma::mnmaj_off(r, col, 64)) =
-          pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
+    for (int h = 0; h < 2; ++h) {
+      uint2 vr[8], wr[8];
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = tp * 16 + 8 * h + i;
+        vr[i] = ld4_raw(p.v, bb, hv, t0 + r, col, r < cv);
+        wr[i] = ld4_raw(p.w, bb, hv, t0 + r, col, r < cv);
+      }
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = tp * 16 + 8 * h + i;
+        float vv[4], ww[4];
+        unpack4(vr[i], vv);
+        unpack4(wr[i], ww);
+        *reinterpret_cast<uint2*>(sm + RV + umma::mnmaj_off(r, col, 64)) =
+            pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
+      }
     }
   }
 

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import gdn2_oracle as O
-from helpers import F32_TOL, assert_close, assert_close_bf16
+from helpers import BF16_NORMWISE, F32_TOL, assert_close, assert_close_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -188,7 +188,7 @@ def test_chunk_full_size_matches_recurrent_bf16():
     oc, sc = bg.chunk_wy_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], s0, K ** -0.5, 64)
     orr, sr = bg.fused_recurrent_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], s0, K ** -0.5)
     assert_close_bf16(oc.float().cpu().numpy(), orr.float().cpu().numpy(), what="out")
-    assert_close(sc.cpu().numpy(), sr.cpu().numpy(), rtol=1e-3, atol=1e-3, what="state")
+    assert_close_bf16(sc.cpu().numpy(), sr.cpu().numpy(), what="state")
 
 
 def test_short_conv_and_rms_norm_gate_kernels():
@@ -267,6 +267,12 @@ def test_chunk_tensor_core_grouped_heads_and_epilogue():
     o_ref, s_ref = O.chunk_wy_forward(rep(r(q)), rep(r(k)), r(v), rep(r(g)), rep(r(b)), r(w),
                                       np.zeros((B, HV, K, V)), K ** -0.5, 64)
     y_ref = O.rms_norm_gate_per_head(o_ref.transpose(0, 2, 1, 3), r(gt), onw.astype(np.float64), 1e-5)
-    assert_close_bf16(out.float().cpu().numpy(), y_ref, what="gated out")
+    # The RMS norm rescales every row to O(1), so a row whose pre-norm output
+    # is a cancellation (e.g. t = 0 with q.k ~ 0) keeps its bf16 relative
+    # error at full scale: judge the gated output normwise and against the
+    # largest magnitude.  The pre-norm path is checked elementwise above.
+    y = out.float().cpu().numpy()
+    assert np.linalg.norm(y - y_ref) / np.linalg.norm(y_ref) <= BF16_NORMWISE
+    assert np.abs(y - y_ref).max() <= 0.05 * np.abs(y_ref).max()
     assert_close_bf16(st.cpu().numpy(), s_ref, what="state")
     assert bg._lib.read_device_errors() == 0
