@@ -44,8 +44,8 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
   float* sRms = reinterpret_cast<float*>(sm + MISC);
   float* sOnw = reinterpret_cast<float*>(sm + ONW);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);  // full[2], mma1, mma2
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);  // full[2], mma1, mma2/3, operands ready
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
 
   const int hv = blockIdx.y, bb = blockIdx.z;
   const int V = p.V, HALF = V / 2;
@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[i];
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&bars[4], 256);  // every thread: its v_new rows / S rescale done
     fence_mbar_init();
   }
   // zero halves of the [0; Aqk] tiles (never written by the copies)
@@ -124,11 +125,22 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
 
   // o rows of chunk c live in rows 64..127 of D[c & 1] (sub-partitions 2, 3);
   // their epilogue runs while the tensor core does MMA1 of chunk c + 1.
+  uint4 graw[8];  // gate rows of the chunk whose epilogue runs next (sub-partitions 2, 3)
+  const int orow = 32 * (sp - 2) + lane;
+  auto load_gate = [&](int c) {
+    const int t0 = c * TC_C;
+    if (p.fuse_epilogue && orow < min(TC_C, p.T - t0)) {
+      const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
+                                (int64_t)(t0 + orow) * p.gate.s2 + col0;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (8 * j < HALF) graw[j] = reinterpret_cast<const uint4*>(gp)[j];
+    }
+  };
   auto epilogue = [&](int c) {
     const int t0 = c * TC_C;
     const int cv = min(TC_C, p.T - t0);
     const uint32_t tD = tD0 + (c & 1) * V;
-    const int orow = 32 * (sp - 2) + lane;
     float ov[64];
     #pragma unroll
     for (int c16 = 0; c16 < 4; ++c16) {
@@ -140,21 +152,13 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       }
     }
     umma::wait_ld();
-    uint4 graw[8];
-    if (p.fuse_epilogue && orow < cv) {
-      const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
-                                (int64_t)(t0 + orow) * p.gate.s2 + col0;
-      #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (8 * j < HALF) graw[j] = reinterpret_cast<const uint4*>(gp)[j];
-    }
     float ss = 0.f;
     #pragma unroll
     for (int j = 0; j < 64; ++j)
       if (j < HALF) ss += ov[j] * ov[j];
     sRms[orow * 2 + half] = ss;
     named_bar(1, 128);
-    const float inv = 1.f / sqrtf((sRms[orow * 2] + sRms[orow * 2 + 1]) / (float)V + p.eps);
+    const float inv = rsqrtf((sRms[orow * 2] + sRms[orow * 2 + 1]) / (float)V + p.eps);
     named_bar(1, 128);  // sRms reusable
     if (orow < cv) {
       __nv_bfloat16* op = static_cast<__nv_bfloat16*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
           const float o = ov[8 * j + e];
           if (p.fuse_epilogue) {
             const float gt = (e & 1) ? __high2float(gh[e >> 1]) : __low2float(gh[e >> 1]);
-            y[e] = o * inv * sOnw[col0 + 8 * j + e] * silu_f(gt);
+            y[e] = o * inv * sOnw[col0 + 8 * j + e] * __fdividef(gt, 1.f + __expf(-gt));
           } else {
             y[e] = o;
           }
@@ -181,6 +185,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       }
     }
   };
+  if (sp >= 2) load_gate(0);
 
   for (int c = 0; c < p.NC; ++c) {
     const int s = c & 1;
@@ -216,9 +221,18 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       }
       umma::wait_st();
     }
-    if (sp >= 2 && c > 0) epilogue(c - 1);
-    mbar_wait_bounded(&bars[2], c & 1);
-    umma::fence_after_sync();
+    if (sp >= 2) {
+      // rows 64..127 of S rescaled: this thread's part of the MMA3 operands is ready
+      umma::fence_before_sync();
+      mbar_arrive(&bars[4]);
+      if (c > 0) {
+        epilogue(c - 1);
+        load_gate(c);  // lands while chunk c runs; used by its epilogue in chunk c + 1
+      }
+    } else {
+      mbar_wait_bounded(&bars[2], c & 1);
+      umma::fence_after_sync();
+    }
 
     // v_new = U - W S  (rows 0..63 of D: sub-partitions 0, 1)
     if (sp < 2) {
@@ -254,13 +268,16 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
         }
       }
     }
-    fence_proxy_async_smem();
-    umma::fence_before_sync();
-    __syncthreads();
-    umma::fence_after_sync();
+    if (sp < 2) {
+      fence_proxy_async_smem();
+      umma::fence_before_sync();
+      mbar_arrive(&bars[4]);
+    }
 
     // MMA2: D += [0; Aqk] v_new ; MMA3: S += Kd^T v_new
     if (tid == 0) {
+      mbar_wait_bounded(&bars[4], c & 1);
+      umma::fence_after_sync();
       #pragma unroll
       for (int j = 0; j < 4; ++j)
         umma::mma_bf16(tD, umma::desc_kmaj(sbase + s * STAGE + ST_TA, 128, j),

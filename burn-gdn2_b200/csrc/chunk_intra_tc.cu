@@ -130,37 +130,32 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
   for (int j = 0; j < 4; ++j) Gbp[j] = tp == 0 ? Gb[0][j] : tp == 1 ? Gb[1][j] : tp == 2 ? Gb[2][j] : Gb[3][j];
   __syncthreads();  // sGlast
 
-  // ---- 2. operands from q, k, b (all 16 rows' loads issued up front) ----
+  // ---- 2. operands from q, k, b (compact loop: the code must stay in the instruction cache) ----
   const float glast[4] = {sGlast_pre(sGlast, ch, 0), sGlast_pre(sGlast, ch, 1), sGlast_pre(sGlast, ch, 2),
                           sGlast_pre(sGlast, ch, 3)};
+  float eGbp[4];
+  #pragma unroll
+  for (int j = 0; j < 4; ++j) eGbp[j] = __expf(Gbp[j]);
   {
-    uint2 qr[16], kr[16], br[16];
-    #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int r = tp * 16 + i;
-      qr[i] = ld4_raw(p.q, bb, kh, t0 + r, ch, r < cv);
-      kr[i] = ld4_raw(p.k, bb, kh, t0 + r, ch, r < cv);
-      br[i] = ld4_raw(p.b, bb, kh, t0 + r, ch, r < cv);
-    }
     unsigned char* xt = sm + X + tp * 8192;
-    #pragma unroll
+    #pragma unroll 2
     for (int i = 0; i < 16; ++i) {
       const int r = tp * 16 + i;
       float q[4], k[4], b[4];
-      unpack4(qr[i], q);
-      unpack4(kr[i], k);
-      unpack4(br[i], b);
+      unpack4(ld4_raw(p.q, bb, kh, t0 + r, ch, r < cv), q);
+      unpack4(ld4_raw(p.k, bb, kh, t0 + r, ch, r < cv), k);
+      unpack4(ld4_raw(p.b, bb, kh, t0 + r, ch, r < cv), b);
       float qs[4], bks[4], qg[4], rk[4], kd[4];
       #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float e = expf(gl[i][j]);
+        const float e = __expf(gl[i][j]);
         const float G = Gbp[j] + gl[i][j];
-        const float gam = expf(G);
+        const float gam = eGbp[j] * e;
         qs[j] = q[j] * e;
         bks[j] = b[j] * k[j] * e;
         qg[j] = q[j] * gam * p.scale;
         rk[j] = b[j] * k[j] * gam;
-        kd[j] = k[j] * expf(glast[j] - G);
+        kd[j] = k[j] * __expf(glast[j] - G);
       }
       *reinterpret_cast<uint2*>(xt + umma::kmaj_off(i, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
       *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + i, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
@@ -174,7 +169,7 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
         #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float gbpp = pp == 0 ? Gb[0][j] : pp == 1 ? Gb[1][j] : pp == 2 ? Gb[2][j] : Gb[3][j];
-          ks[j] = k[j] * expf(gbpp - Gbp[j] - gl[i][j]);
+          ks[j] = k[j] * __expf(gbpp - Gbp[j] - gl[i][j]);
         }
         unsigned char* kt = sm + KSV + 4096 * (pp * (pp + 1) / 2);
         *reinterpret_cast<uint2*>(kt + umma::kmaj_off(r, ch, 16 * (pp + 1))) = pack4(ks[0], ks[1], ks[2], ks[3]);
