@@ -258,6 +258,12 @@ def run_ours(args):
 
     # ---- decode step, BASELINE config 3 (one token, B = 256) ----
     decode = run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world)
+    # ---- whole layer forward_train (projections on cuBLAS + the core) ----
+    layer = run_layer(torch, bg, dev, stream, args, max_over_ranks, world) if not args.core_only else None
+    # ---- N > 1: one config-2 layer split by heads, o_proj all-reduce timed apart ----
+    layer_tp = run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world) if world > 1 else None
+    # ---- the f32 configuration of BASELINE config 2 (CUDA-core path) ----
+    f32 = run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world) if not args.core_only else None
 
     # ---- roofline of the dominant kernel ----
     peaks = load_peaks()
@@ -283,17 +289,144 @@ def run_ours(args):
                     "ms_per_step": e2e_ms},
             "roofline": {"bound": "hbm", "kernel": "chunk core (intra + inter + epilogue) per step",
                          "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic("chunk_core_bf16_cfg2"),
                          "peak_src": peaks["src"], "alg_bytes_per_step": alg_bytes,
                          "tc_frac": flops / (core_ms / 1e3) / (peaks["bf16_tflops"] * 1e12)},
             "kernels_ms": {"chunk_intra": intra_ms, "chunk_inter_plus_epilogue": inter_ms, "dominant": dom_name},
             "decode": decode,
+            "layer": layer,
+            "layer_head_sharded": layer_tp,
+            "f32": f32,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
     if world > 1:
         dist.destroy_process_group()
     return result
+
+
+def ncu_traffic(key):
+    """DRAM bytes per step measured by ncu (profiles/roofline_traffic.txt)."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", "roofline_traffic.txt")):
+            k, _, v = line.partition("=")
+            if k.strip() == key:
+                return float(v.split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def run_layer(torch, bg, dev, stream, args, max_over_ranks, world):
+    """GatedDeltaNet2.forward_train at BASELINE config 2 (hidden 2048,
+    16 x 128 heads, chunk 64, bf16, B=8, T=4096): tokens/s and the fraction
+    of the dense bf16 tensor-core peak the whole layer reaches."""
+    c = CFG2
+    cfg = bg.Gdn2Config(hidden_size=2048, num_heads=16, head_dim=128, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
+    m = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=0)
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(c["B"], c["T"], 2048, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    for _ in range(2):
+        m.forward_train(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 5
+    e0.record(stream)
+    for _ in range(n):
+        m.forward_train(x)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    D, kd, vd, vh = 2048, 16 * 128, 16 * 128, 128
+    tokens = c["B"] * c["T"]
+    # q, k, b (D x KD); v, w (D x VD); f_proj_0, g_proj_0 (D x vh); f_proj_1 (vh x KD);
+    # g_proj_1 (vh x VD); o_proj (VD x D)  -> 52.4 MFLOP per token
+    proj_flops = 2 * tokens * (3 * D * kd + 2 * D * vd + 2 * D * vh + vh * kd + vh * vd + vd * D)
+    core_flops = core_flops_per_token_head(128, 128, 64) * tokens * 16
+    peaks = load_peaks()
+    flops = proj_flops + core_flops
+    return {"value": tokens * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "workload": "GatedDeltaNet2.forward_train, BASELINE config 2 (D=2048, 16x128 heads, B=8, T=4096, bf16)",
+            "tflops": flops / (ms / 1e3) / 1e12, "tc_frac": flops / (ms / 1e3) / (peaks["bf16_tflops"] * 1e12),
+            "flops_per_step": flops}
+
+
+def run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world):
+    """BASELINE config 2 layer (16 heads) split by heads over the N ranks
+    (strong scaling of one layer): forward_train time per step (max over
+    ranks) and the NCCL all-reduce of the o_proj partials [B,T,2048] bf16,
+    timed separately."""
+    from burn_gdn2 import sharding
+    c = CFG2
+    cfg = bg.Gdn2Config(hidden_size=2048, num_heads=16, head_dim=128, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
+    full = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=0)
+    W = {n: getattr(full, a).weight.detach().float().cpu() for n, a in
+         (("q_proj", "q_proj"), ("k_proj", "k_proj"), ("v_proj", "v_proj"), ("f_proj_0", "f_proj_0"),
+          ("f_proj_1", "f_proj_1"), ("b_proj", "b_proj"), ("w_proj", "w_proj"), ("g_proj_0", "g_proj_0"),
+          ("o_proj", "o_proj"))}
+    W["g_proj_1_w"] = full.g_proj_1.weight.float().cpu()
+    W["g_proj_1_b"] = full.g_proj_1.bias.float().cpu()
+    for n, a in (("A_log", "a_log"), ("dt_bias", "dt_bias"), ("o_norm_w", "o_norm_weight"), ("q_conv_w", "q_conv_w"),
+                 ("k_conv_w", "k_conv_w"), ("v_conv_w", "v_conv_w")):
+        W[n] = getattr(full, a).float().cpu()
+    del full
+    m = sharding.ShardedGatedDeltaNet2(cfg, W, device=dev, dtype=torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(c["B"], c["T"], 2048, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    for _ in range(2):
+        m.forward_train(x)
+    torch.cuda.synchronize()
+    n = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ar = 0.0
+    e0.record(stream)
+    for _ in range(n):
+        m.forward_train(x)
+        ar += m.allreduce_ms()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    ar_ms = max_over_ranks(ar / n)
+    nbytes = c["B"] * c["T"] * 2048 * 2
+    return {"value": c["B"] * c["T"] / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
+            "workload": f"GatedDeltaNet2.forward_train, BASELINE config 2, 16 heads split over {world} GPUs",
+            "allreduce_ms": ar_ms, "allreduce_bytes": nbytes,
+            "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / (ar_ms / 1e3) / 1e9}
+
+
+def run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world):
+    """BASELINE config 2 core in f32 (the exact CUDA-core path)."""
+    c = CFG2
+    B, HV, T, K, V = c["B"], c["HV"], c["T"], c["K"], c["V"]
+    x = make_inputs(torch, B, HV, T, K, V, torch.float32, dev, seed=2000)
+    view = lambda t: t.permute(0, 2, 1, 3)
+    state = torch.zeros(B, HV, K, V, dtype=torch.float32, device=dev)
+    out = torch.empty(B, T, HV, V, dtype=torch.float32, device=dev)
+    onw = torch.ones(V, dtype=torch.float32, device=dev)
+    a = ops.chunk_args(view(x["q"]), view(x["k"]), view(x["v"]), view(x["g"]), view(x["b"]), view(x["w"]), state,
+                       view(out), K ** -0.5, c["chunk"], num_heads=c["H"], gate=view(x["gate"]), o_norm_weight=onw,
+                       norm_eps=1e-5)
+    ws = ops.chunk_workspace(a, dev)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    run = lambda: bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ws.numel(), sh))
+    run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 3
+    e0.record(stream)
+    for _ in range(n):
+        state.zero_()
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    del ws
+    alg = core_bytes_per_token_head(K, V, 4) * B * T * HV
+    peaks = load_peaks()
+    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "workload": "BASELINE config 2 chunked forward core in f32 (CUDA-core path, exact f32)",
+            "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
 
 
 def run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world):
@@ -338,7 +471,8 @@ def run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world):
             "workload": "BASELINE config 3 decode step: B=256 (per rank), HV=16, K=V=128, state f32 in place, "
                         "fused short-conv + L2 prologue and gated RMS-norm epilogue",
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / peaks["hbm_gbs"], "bytes_per_step": state_bytes + vec_bytes}}
+                         "frac": gbs / peaks["hbm_gbs"], "bytes_per_step": state_bytes + vec_bytes,
+                         "traffic": ncu_traffic("decode_cfg3")}}
 
 
 # ---------------------------------------------------------------------------
@@ -402,6 +536,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--core-only", action="store_true", help="skip the layer and f32 side measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
