@@ -273,7 +273,10 @@ def run_ours(args):
     core_ms = intra_ms + inter_ms
     achieved = alg_bytes / (core_ms / 1e3) / 1e9
     flops = core_flops_per_token_head(K, V, c["chunk"]) * tokens * HV
-    launches_per_step = 3  # intra, inter, output stage
+    # bf16, K = 128, V in {64, 128}, chunk 64: tensor-core path (k_intra_tc + k_inter_tc);
+    # otherwise the CUDA-core path (k_intra_simt + k_inter_simt + k_chunk_out)
+    tc_path = dtype == torch.bfloat16 and K == 128 and V in (64, 128) and c["chunk"] == 64
+    launches_per_step = 2 if tc_path else 3
     result = None
     if rank == 0:
         result = {
