@@ -2,10 +2,11 @@
 //
 // Replaces gdn2_chunk_intra_kernel (src/kernel/chunk_cube.rs:27-295) with the
 // numerics of the tensor path src/forward.rs:86-261 (tile-local decay).
-// One CTA (4 warps) per (chunk, value head, batch):
+// One CTA (8 warps, two per SM) per (chunk, value head, batch):
 //
-//  1. warp p owns the 16-row tile p, lane l owns key channels 4l..4l+3:
-//     tile-local cumsum gl of g, tile boundaries Gb_p, G_last.
+//  1. warps 2p, 2p+1 own the two 8-row halves of the 16-row tile p, lane l
+//     owns key channels 4l..4l+3: g sums per half tile -> tile boundaries
+//     Gb_p, G_last; the tile-local cumsum gl is rebuilt row by row.
 //  2. Score operands in shared memory (bf16, 128-byte swizzle):
 //       X_p  = [q e^{gl} ; b k e^{gl}] of tile p          (32 x 128)
 //       Ks_p = k e^{Gb_p - G} for rows s < 16(p+1)        (reference point
@@ -13,9 +14,9 @@
 //              16 tokens of decay, forward.rs:131-157)
 //  3. Four M=64 N=32 K=128 MMAs: D_p = Ks_p X_p^T = [Aqk^T | Akk^T] columns of
 //     row tile p, accumulated in TMEM.
-//     Qg = scale q gamma, Kd = k e^{G_last - G}, rhs_k = b k gamma and
-//     gamma_last come out of the same pass (forward.rs:189-190, :266-274).
-//  4. While the MMAs run: rhs_v = w v.
+//     Qg = scale q gamma, Kd = k e^{G_last - G}, rhs_k = b k gamma,
+//     rhs_v = w v and gamma_last come out of the same pass
+//     (forward.rs:189-190, :266-274).
 //  5. Aqk (scaled, causal) and Akk (strict) back from TMEM; (I + Akk)^-1 by
 //     blocked forward substitution over 16x16 tiles (forward.rs:192-261).
 //  6. Two M=64 MMAs: W = (I+Akk)^-1 rhs_k, U = (I+Akk)^-1 rhs_v.
@@ -37,8 +38,8 @@ constexpr uint32_t TINV_IMG = 45056;    // bf16 K-major [64][64]
 constexpr uint32_t SCRATCH = 53248;     // 4 x f32 [16][17]
 constexpr uint32_t RK = R1_END;         // bf16 MN-major [64][128]
 constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][V], V <= 128
-constexpr uint32_t MISC = RV + 16384;   // sTot [4][128] f32, sGlast [128] f32, barriers, tmem base
-constexpr uint32_t TOTAL = MISC + 2048 + 512 + 64;
+constexpr uint32_t MISC = RV + 16384;   // half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem base
+constexpr uint32_t TOTAL = MISC + 4096 + 512 + 64;
 }  // namespace intra_smem
 
 __device__ __forceinline__ uint2 ld4_raw(const DView& v, int bb, int h, int t, int c, bool ok) {
@@ -53,18 +54,17 @@ __device__ __forceinline__ void unpack4(uint2 raw, float (&x)[4]) {
   x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
 }
 
-__device__ __forceinline__ float sGlast_pre(const float* s, int ch, int j) { return s[ch + j]; }
 
 __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
   return make_uint2(umma::pack_bf16x2(a, b), umma::pack_bf16x2(c, d));
 }
 
-__global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
+__global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   using namespace intra_smem;
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
-  float* sTot = reinterpret_cast<float*>(sm + MISC);
-  float* sGlast = sTot + 4 * 128;
+  float* sHalf = reinterpret_cast<float*>(sm + MISC);  // [8][128] g sums of each 8-row half tile
+  float* sGlast = sHalf + 8 * 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGlast + 128);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
 
@@ -74,9 +74,9 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
   const int cv = min(TC_C, p.T - t0);
   const int V = p.V;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tp = warp;       // row tile
-  const int ch = lane * 4;   // first of 4 key channels
-  const int lt = (cv - 1) >> 4, lr = (cv - 1) & 15;
+  const int tp = warp >> 1, hh = warp & 1;  // row tile, half of it (rows 16 tp + 8 hh + i)
+  const int r0 = tp * 16 + hh * 8;
+  const int ch = lane * 4;                  // first of 4 key channels
   unsigned char* rec = p.rec + (((size_t)bb * p.HV + hv) * p.NC + c) * p.rec_bytes;
   const TcRecord L = tc_record_layout(V);
 
@@ -90,20 +90,22 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
     fence_mbar_init();
   }
 
-  // ---- 1. tile-local cumsum of g ----
-  float gl[16][4];
+  // ---- 1. sums of g over each half tile (the per-row cumsum is rebuilt below) ----
+  const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
+  float glr[4] = {0.f, 0.f, 0.f, 0.f};  // half-local cumsum at the last valid row, if it is ours
   {
     float run[4] = {0.f, 0.f, 0.f, 0.f};
-    const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
     #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int r = tp * 16 + i;
+    for (int i = 0; i < 8; ++i) {
+      const int r = r0 + i;
       float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
       if (r < cv) gv = *reinterpret_cast<const float4*>(gbase + (int64_t)(t0 + r) * p.g.s2);
       run[0] += gv.x; run[1] += gv.y; run[2] += gv.z; run[3] += gv.w;
-      gl[i][0] = run[0]; gl[i][1] = run[1]; gl[i][2] = run[2]; gl[i][3] = run[3];
+      if (r == cv - 1) {
+        glr[0] = run[0]; glr[1] = run[1]; glr[2] = run[2]; glr[3] = run[3];
+      }
     }
-    *reinterpret_cast<float4*>(sTot + tp * 128 + ch) = make_float4(run[0], run[1], run[2], run[3]);
+    *reinterpret_cast<float4*>(sHalf + warp * 128 + ch) = make_float4(run[0], run[1], run[2], run[3]);
   }
   __syncthreads();
   float Gb[4][4];  // Gb[pp][j]: G at the end of tile pp-1 (0 for pp = 0)
@@ -111,72 +113,93 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
   for (int j = 0; j < 4; ++j) Gb[0][j] = 0.f;
   #pragma unroll
   for (int pp = 1; pp < 4; ++pp) {
-    const float4 t = *reinterpret_cast<const float4*>(sTot + (pp - 1) * 128 + ch);
-    Gb[pp][0] = Gb[pp - 1][0] + t.x; Gb[pp][1] = Gb[pp - 1][1] + t.y;
-    Gb[pp][2] = Gb[pp - 1][2] + t.z; Gb[pp][3] = Gb[pp - 1][3] + t.w;
+    const float4 a = *reinterpret_cast<const float4*>(sHalf + (2 * pp - 2) * 128 + ch);
+    const float4 b = *reinterpret_cast<const float4*>(sHalf + (2 * pp - 1) * 128 + ch);
+    Gb[pp][0] = Gb[pp - 1][0] + a.x + b.x; Gb[pp][1] = Gb[pp - 1][1] + a.y + b.y;
+    Gb[pp][2] = Gb[pp - 1][2] + a.z + b.z; Gb[pp][3] = Gb[pp - 1][3] + a.w + b.w;
   }
-  if (tp == lt) {
-    float gsel[4] = {0.f, 0.f, 0.f, 0.f};
+  float Gbp[4], off[4];  // Gb of this tile; tile-local cumsum before row r0
+  {
+    const float4 h0 = *reinterpret_cast<const float4*>(sHalf + (2 * tp) * 128 + ch);
+    const float hv0[4] = {h0.x, h0.y, h0.z, h0.w};
     #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (i == lr) {
-        gsel[0] = gl[i][0]; gsel[1] = gl[i][1]; gsel[2] = gl[i][2]; gsel[3] = gl[i][3];
-      }
-    *reinterpret_cast<float4*>(sGlast + ch) =
-        make_float4(Gb[tp][0] + gsel[0], Gb[tp][1] + gsel[1], Gb[tp][2] + gsel[2], Gb[tp][3] + gsel[3]);
+    for (int j = 0; j < 4; ++j) {
+      Gbp[j] = tp == 0 ? Gb[0][j] : tp == 1 ? Gb[1][j] : tp == 2 ? Gb[2][j] : Gb[3][j];
+      off[j] = hh ? hv0[j] : 0.f;
+    }
   }
-  float Gbp[4];
-  #pragma unroll
-  for (int j = 0; j < 4; ++j) Gbp[j] = tp == 0 ? Gb[0][j] : tp == 1 ? Gb[1][j] : tp == 2 ? Gb[2][j] : Gb[3][j];
+  if (r0 <= cv - 1 && cv - 1 < r0 + 8)
+    *reinterpret_cast<float4*>(sGlast + ch) = make_float4(Gbp[0] + off[0] + glr[0], Gbp[1] + off[1] + glr[1],
+                                                          Gbp[2] + off[2] + glr[2], Gbp[3] + off[3] + glr[3]);
   __syncthreads();  // sGlast
 
-  // ---- 2. operands from q, k, b (compact loop: the code must stay in the instruction cache) ----
-  const float glast[4] = {sGlast_pre(sGlast, ch, 0), sGlast_pre(sGlast, ch, 1), sGlast_pre(sGlast, ch, 2),
-                          sGlast_pre(sGlast, ch, 3)};
-  float eGbp[4];
+  // ---- 2. operands (compact loop: the code must stay in the instruction cache) ----
+  float glast[4];
   #pragma unroll
-  for (int j = 0; j < 4; ++j) eGbp[j] = __expf(Gbp[j]);
+  for (int j = 0; j < 4; ++j) glast[j] = sGlast[ch + j];
+  // per-channel constants of this row tile: gamma = e^{Gb_p} E, Ks_pp = k E^-1 e^{Gb_pp - Gb_p}
+  float eGbp[4], cks[4][4];
+  #pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    eGbp[j] = __expf(Gbp[j]);
+    #pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      const float gbpp = pp == 0 ? Gb[0][j] : pp == 1 ? Gb[1][j] : pp == 2 ? Gb[2][j] : Gb[3][j];
+      cks[pp][j] = __expf(gbpp - Gbp[j]);
+    }
+  }
   {
     unsigned char* xt = sm + X + tp * 8192;
+    float gl[4] = {off[0], off[1], off[2], off[3]};  // tile-local cumsum of g at row r
     #pragma unroll 2
-    for (int i = 0; i < 16; ++i) {
-      const int r = tp * 16 + i;
+    for (int i = 0; i < 8; ++i) {
+      const int r = r0 + i, ti = hh * 8 + i;
+      const bool ok = r < cv;
+      if (ok) {
+        const float4 gv = *reinterpret_cast<const float4*>(gbase + (int64_t)(t0 + r) * p.g.s2);
+        gl[0] += gv.x; gl[1] += gv.y; gl[2] += gv.z; gl[3] += gv.w;
+      }
       float q[4], k[4], b[4];
-      unpack4(ld4_raw(p.q, bb, kh, t0 + r, ch, r < cv), q);
-      unpack4(ld4_raw(p.k, bb, kh, t0 + r, ch, r < cv), k);
-      unpack4(ld4_raw(p.b, bb, kh, t0 + r, ch, r < cv), b);
-      float qs[4], bks[4], qg[4], rk[4], kd[4];
+      unpack4(ld4_raw(p.q, bb, kh, t0 + r, ch, ok), q);
+      unpack4(ld4_raw(p.k, bb, kh, t0 + r, ch, ok), k);
+      unpack4(ld4_raw(p.b, bb, kh, t0 + r, ch, ok), b);
+      float vv[4] = {0.f, 0.f, 0.f, 0.f}, ww[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ch < V) {
+        unpack4(ld4_raw(p.v, bb, hv, t0 + r, ch, ok), vv);
+        unpack4(ld4_raw(p.w, bb, hv, t0 + r, ch, ok), ww);
+      }
+      float qs[4], bks[4], qg[4], rk[4], kd[4], kinv[4];
       #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float e = __expf(gl[i][j]);
-        const float G = Gbp[j] + gl[i][j];
+        const float e = __expf(gl[j]);
+        const float ei = __expf(-gl[j]);
+        const float G = Gbp[j] + gl[j];
         const float gam = eGbp[j] * e;
         qs[j] = q[j] * e;
         bks[j] = b[j] * k[j] * e;
         qg[j] = q[j] * gam * p.scale;
         rk[j] = b[j] * k[j] * gam;
         kd[j] = k[j] * __expf(glast[j] - G);
+        kinv[j] = k[j] * ei;
       }
-      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(i, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
-      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + i, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
+      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(ti, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
+      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + ti, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
       *reinterpret_cast<uint2*>(rec + L.wq + umma::kmaj_off(64 + r, ch, 128)) = pack4(qg[0], qg[1], qg[2], qg[3]);
       *reinterpret_cast<uint2*>(rec + L.kd + umma::mnmaj_off(r, ch, 64)) = pack4(kd[0], kd[1], kd[2], kd[3]);
       *reinterpret_cast<uint2*>(sm + RK + umma::mnmaj_off(r, ch, 64)) = pack4(rk[0], rk[1], rk[2], rk[3]);
+      if (ch < V)
+        *reinterpret_cast<uint2*>(sm + RV + umma::mnmaj_off(r, ch, 64)) =
+            pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
       #pragma unroll
       for (int pp = 0; pp < 4; ++pp) {
         if (pp < tp) continue;
-        float ks[4];
-        #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float gbpp = pp == 0 ? Gb[0][j] : pp == 1 ? Gb[1][j] : pp == 2 ? Gb[2][j] : Gb[3][j];
-          ks[j] = k[j] * __expf(gbpp - Gbp[j] - gl[i][j]);
-        }
         unsigned char* kt = sm + KSV + 4096 * (pp * (pp + 1) / 2);
-        *reinterpret_cast<uint2*>(kt + umma::kmaj_off(r, ch, 16 * (pp + 1))) = pack4(ks[0], ks[1], ks[2], ks[3]);
+        *reinterpret_cast<uint2*>(kt + umma::kmaj_off(r, ch, 16 * (pp + 1))) =
+            pack4(kinv[0] * cks[pp][0], kinv[1] * cks[pp][1], kinv[2] * cks[pp][2], kinv[3] * cks[pp][3]);
       }
     }
   }
-  if (tp == 0)
+  if (warp == 0)
     *reinterpret_cast<float4*>(rec + L.gl + ch * 4) =
         make_float4(expf(glast[0]), expf(glast[1]), expf(glast[2]), expf(glast[3]));
   fence_proxy_async_smem();
@@ -200,41 +223,19 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
     umma::commit(&bars[0]);
   }
 
-  // ---- 4. rhs_v = w v (overlaps the score MMAs) ----
-  for (int col = ch; col < V; col += 128) {
-    #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint2 vr[8], wr[8];
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int r = tp * 16 + 8 * h + i;
-        vr[i] = ld4_raw(p.v, bb, hv, t0 + r, col, r < cv);
-        wr[i] = ld4_raw(p.w, bb, hv, t0 + r, col, r < cv);
-      }
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int r = tp * 16 + 8 * h + i;
-        float vv[4], ww[4];
-        unpack4(vr[i], vv);
-        unpack4(wr[i], ww);
-        *reinterpret_cast<uint2*>(sm + RV + umma::mnmaj_off(r, col, 64)) =
-            pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
-      }
-    }
-  }
-
-  // ---- 5. scores back from TMEM ----
+  // ---- 4. scores back from TMEM (warp w: sub-partition w % 4, row tiles 2 (w / 4) .. +1) ----
   mbar_wait_bounded(&bars[0], 0);
   umma::fence_after_sync();
   float* sAkk = reinterpret_cast<float*>(sm + AKK);
   float* sTinv = reinterpret_cast<float*>(sm + TINV);
   {
-    const int s = 16 * warp + lane;  // valid for lane < 16 (M = 64 TMEM layout)
+    const int sp = warp & 3, s = 16 * sp + lane;  // valid for lane < 16 (M = 64 TMEM layout)
     #pragma unroll
-    for (int pp = 0; pp < 4; ++pp) {
+    for (int pq = 0; pq < 2; ++pq) {
+      const int pp = 2 * (warp >> 2) + pq;
       float vq[16], vk[16];
-      umma::ld16(umma::taddr(tA, 32 * warp, 32 * pp), vq);
-      umma::ld16(umma::taddr(tA, 32 * warp, 32 * pp + 16), vk);
+      umma::ld16(umma::taddr(tA, 32 * sp, 32 * pp), vq);
+      umma::ld16(umma::taddr(tA, 32 * sp, 32 * pp + 16), vk);
       umma::wait_ld();
       if (lane < 16) {
         #pragma unroll
@@ -250,8 +251,8 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
   umma::fence_before_sync();
   __syncthreads();
 
-  // ---- 6. (I + Akk)^-1, blocked over 16 x 16 tiles ----
-  if (lane < 16) {  // diagonal tile `warp`, column `lane`
+  // ---- 5. (I + Akk)^-1, blocked over 16 x 16 tiles ----
+  if (warp < 4 && lane < 16) {  // diagonal tile `warp`, column `lane`
     const int o = 16 * warp, j = lane;
     float x[16];
     #pragma unroll
@@ -265,42 +266,46 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
     for (int i = 0; i < 16; ++i) sTinv[(o + i) * 65 + o + j] = x[i];
   }
   __syncthreads();
-  float* scr = reinterpret_cast<float*>(sm + SCRATCH) + warp * 16 * 17;
+  float* scr = reinterpret_cast<float*>(sm + SCRATCH);  // 4 x [16][17]
   for (int d = 1; d < 4; ++d) {
-    const int bi = warp + d, bj = warp;
-    if (bi < 4) {
-      const int row = lane >> 1, c0 = (lane & 1) * 8;
-      float tmp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int bj = warp & 3, bi = bj + d, rh = warp >> 2;
+    const int row = rh * 8 + (lane >> 2), c0 = (lane & 3) * 4;
+    float* sc = scr + bj * 16 * 17;
+    if (bi < 4) {  // tmp = sum_m A[bi][m] Tinv[m][bj] over tiles bj .. bi-1
+      float tmp[4] = {0.f, 0.f, 0.f, 0.f};
       for (int m = 16 * bj; m < 16 * bi; ++m) {
         const float a = sAkk[(16 * bi + row) * 65 + m];
         #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) tmp[cc] += a * sTinv[m * 65 + 16 * bj + c0 + cc];
+        for (int cc = 0; cc < 4; ++cc) tmp[cc] += a * sTinv[m * 65 + 16 * bj + c0 + cc];
       }
       #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) scr[row * 17 + c0 + cc] = tmp[cc];
-      __syncwarp();
-      float res[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int cc = 0; cc < 4; ++cc) sc[row * 17 + c0 + cc] = tmp[cc];
+    }
+    __syncthreads();
+    if (bi < 4) {  // Tinv[bi][bj] = -Tinv[bi][bi] tmp
+      float res[4] = {0.f, 0.f, 0.f, 0.f};
+      #pragma unroll
       for (int m = 0; m < 16; ++m) {
         const float li = sTinv[(16 * bi + row) * 65 + 16 * bi + m];
         #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) res[cc] -= li * scr[m * 17 + c0 + cc];
+        for (int cc = 0; cc < 4; ++cc) res[cc] -= li * sc[m * 17 + c0 + cc];
       }
       #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) sTinv[(16 * bi + row) * 65 + 16 * bj + c0 + cc] = res[cc];
+      for (int cc = 0; cc < 4; ++cc) sTinv[(16 * bi + row) * 65 + 16 * bj + c0 + cc] = res[cc];
     }
     __syncthreads();
   }
-  for (int idx = tid; idx < 64 * 64; idx += 128) {
-    const int r = idx >> 6, s = idx & 63;
-    const float val = (s == r) ? 1.f : ((s < r) ? sTinv[r * 65 + s] : 0.f);
-    *reinterpret_cast<__nv_bfloat16*>(sm + TINV_IMG + umma::kmaj_off(r, s, 64)) = __float2bfloat16_rn(val);
+  for (int idx = tid; idx < 64 * 64; idx += 256) {
+    const int r = idx >> 6, s2 = idx & 63;
+    const float val = (s2 == r) ? 1.f : ((s2 < r) ? sTinv[r * 65 + s2] : 0.f);
+    *reinterpret_cast<__nv_bfloat16*>(sm + TINV_IMG + umma::kmaj_off(r, s2, 64)) = __float2bfloat16_rn(val);
   }
   fence_proxy_async_smem();
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
 
-  // ---- 7. W = T^-1 rhs_k, U = T^-1 rhs_v ----
+  // ---- 6. W = T^-1 rhs_k, U = T^-1 rhs_v ----
   if (tid == 0) {
     const uint32_t sbase = smem_u32(sm);
     const uint32_t iw = umma::idesc_bf16(64, 128, false, true);
@@ -315,16 +320,20 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
     umma::commit(&bars[1]);
   }
   // Aqk image to the record while the MMAs run
-  for (int idx = tid; idx < 64 * 64 * 2 / 16; idx += 128)
+  for (int idx = tid; idx < 64 * 64 * 2 / 16; idx += 256)
     reinterpret_cast<uint4*>(rec + L.aqk)[idx] = reinterpret_cast<const uint4*>(sm + AQK_IMG)[idx];
   mbar_wait_bounded(&bars[1], 0);
   umma::fence_after_sync();
+
+  // ---- 7. W and U to the record (warp w: sub-partition w % 4, column half w / 4) ----
   {
-    const int r = 16 * warp + lane;  // valid for lane < 16
+    const int sp = warp & 3, half = warp >> 2;
+    const int r = 16 * sp + lane;  // valid for lane < 16
     #pragma unroll
-    for (int c16 = 0; c16 < 8; ++c16) {
+    for (int c16 = 0; c16 < 4; ++c16) {
+      const int col = half * 64 + 16 * c16;
       float v[16];
-      umma::ld16(umma::taddr(tA, 32 * warp, 16 * c16), v);
+      umma::ld16(umma::taddr(tA, 32 * sp, col), v);
       umma::wait_ld();
       if (lane < 16) {
         uint4 lo, hi;
@@ -332,16 +341,17 @@ __global__ void __launch_bounds__(128, 2) k_intra_tc(const TcParams p) {
         lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
         hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
         hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
-        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, 2 * c16, 128)) = lo;
-        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, 2 * c16 + 1, 128)) = hi;
+        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, col / 8, 128)) = lo;
+        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, col / 8 + 1, 128)) = hi;
       }
     }
-    for (int c16 = 0; c16 < V / 16; ++c16) {
+    for (int c16 = 0; c16 < V / 32; ++c16) {
+      const int col = half * (V / 2) + 16 * c16;
       float v[16];
-      umma::ld16(umma::taddr(tA, 32 * warp, 128 + 16 * c16), v);
+      umma::ld16(umma::taddr(tA, 32 * sp, 128 + col), v);
       umma::wait_ld();
       if (lane < 16) {
-        const int col = 16 * c16, sl = col / p.vt, cc = col % p.vt;
+        const int sl = col / p.vt, cc = col % p.vt;
         uint4 lo, hi;
         lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
         lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
@@ -363,7 +373,7 @@ int launch_intra_tc(const TcParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute((const void*)k_intra_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "chunk intra (tc) smem attribute");
   dim3 grid(p.NC, p.HV, p.B);
-  k_intra_tc<<<grid, 128, smem, st>>>(p);
+  k_intra_tc<<<grid, 256, smem, st>>>(p);
   return check_cuda(cudaGetLastError(), "chunk intra (tc) launch");
 }
 
