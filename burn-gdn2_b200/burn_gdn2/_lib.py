@@ -68,7 +68,7 @@ EXPORTS = (
     "gdn2_chunk_fwd_workspace_bytes", "gdn2_chunk_fwd", "gdn2_chunk_intra", "gdn2_chunk_inter",
     "gdn2_recurrent_fwd", "gdn2_short_conv", "gdn2_rms_norm_gate", "gdn2_config_validate",
     "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
-    "gdn2_selftest_umma",
+    "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc",
 )
 
 
@@ -83,6 +83,8 @@ def _load():
     for fn in ("gdn2_chunk_fwd", "gdn2_chunk_intra", "gdn2_chunk_inter"):
         getattr(lib, fn).argtypes = [P(ChunkArgs), vp, sz, vp]
         getattr(lib, fn).restype = ctypes.c_int
+    lib.gdn2_chunk_fwd_noalloc.argtypes = [P(ChunkArgs), vp]
+    lib.gdn2_chunk_fwd_noalloc.restype = ctypes.c_int
     lib.gdn2_recurrent_fwd.argtypes = [P(RecurrentArgs), vp]
     lib.gdn2_recurrent_fwd.restype = ctypes.c_int
     lib.gdn2_short_conv.argtypes = [i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]

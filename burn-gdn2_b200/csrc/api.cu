@@ -5,6 +5,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "chunk.cuh"
 #include "chunk_tc.cuh"
 #include "common.cuh"
@@ -135,6 +137,36 @@ static int prep_chunk(const gdn2_chunk_args* a, void* ws, size_t wsb, ChunkParam
   return GDN2_OK;
 }
 
+// Workspace of gdn2_chunk_fwd_noalloc: one copy per device, shared by every
+// call on that device.  Host code reaches it only through the address that
+// cudaGetSymbolAddress returns.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GDN2_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoallocMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+// Address of the current device's scratch copy, looked up on the first call
+// for that device and cached.
+static int noalloc_scratch(void** out, const char* fn) {
+  int dev = -1;
+  int rc = check_cuda(cudaGetDevice(&dev), fn);
+  if (rc) return rc;
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return set_error(GDN2_EUNSUPPORTED, "%s: device %d beyond the %d devices the scratch table covers", fn, dev,
+                     kNoallocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), fn);
+    if (rc) return rc;
+    if (!p) return set_error(GDN2_ECUDA, "%s: cudaGetSymbolAddress gave a null scratch address", fn);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return GDN2_OK;
+}
+
 }  // namespace gdn2
 
 using namespace gdn2;
@@ -209,6 +241,21 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream)
   rc = launch_inter_simt(p, (cudaStream_t)stream);
   if (rc) return rc;
   return launch_chunk_out(p, a->dtype, (cudaStream_t)stream);
+}
+
+int gdn2_chunk_fwd_noalloc(const gdn2_chunk_args* a, void* stream) {
+  const char* fn = "gdn2_chunk_fwd_noalloc";
+  if (!a) return set_error(GDN2_EINVAL, "%s: null args", fn);
+  const size_t need = gdn2_chunk_fwd_workspace_bytes(a);
+  if (need > GDN2_NOALLOC_SCRATCH_BYTES)
+    return set_error(GDN2_EWORKSPACE,
+                     "%s: needs %zu bytes of scratch, more than the %zu of the static array; split the batch or "
+                     "call gdn2_chunk_fwd with a workspace",
+                     fn, need, (size_t)GDN2_NOALLOC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  int rc = noalloc_scratch(&ws, fn);
+  if (rc) return rc;
+  return gdn2_chunk_fwd(a, ws, GDN2_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 int gdn2_selftest_umma(int32_t test, const float* a, const float* b, float* d, void* stream) {

@@ -12,8 +12,9 @@
  *    the kernels do not implement returns GDN2_EUNSUPPORTED.  The message
  *    of the last failure on the calling thread is gdn2_last_error().
  *  - Device pointers are caller-owned.  Launches are asynchronous on the
- *    given stream.  Calls on different streams are independent; the only
- *    hidden state is a lazily built per-device attribute cache.
+ *    given stream.  Calls on different streams are independent (except
+ *    gdn2_chunk_fwd_noalloc, below); the only hidden state is a lazily
+ *    built per-device attribute cache and that entry point's scratch.
  *  - Tensors are passed as gdn2_view: a 4-D view [d0][d1][d2][d3] whose
  *    last dim is contiguous and whose first three dims have arbitrary
  *    element strides, so the reference's permuted [B,T,H,K] -> [B,H,T,K]
@@ -112,6 +113,39 @@ GDN2_API int gdn2_chunk_fwd(const gdn2_chunk_args* args, void* workspace, size_t
  * :817-887) and gdn2_chunk_inter_kernel (:300-610, host :889-917). */
 GDN2_API int gdn2_chunk_intra(const gdn2_chunk_args* args, void* workspace, size_t workspace_bytes, void* stream);
 GDN2_API int gdn2_chunk_inter(const gdn2_chunk_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Size of the scratch array behind gdn2_chunk_fwd_noalloc: 32 MiB per
+ * device.  That holds 448 tensor-core chunk records of head_v_dim 128
+ * (batch * num_v_heads * ceil(seq_len / 64) <= 448, e.g. 16 value heads
+ * over 1792 tokens), or 185 f32 CUDA-core chunks of K = V = 128. */
+#define GDN2_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+
+/* The chunked forward of gdn2_chunk_fwd without a caller workspace and
+ * without allocating device memory.  No counterpart in the reference: its
+ * chunk path allocates its intermediates as tensors on every call.
+ *
+ * For hosts that cannot allocate device memory at the point of the call: a
+ * serving engine that has reserved the device's free memory up front for
+ * its own pool, a plugin hook handed only tensor pointers and a stream, or
+ * a latency-critical path where cudaMalloc / cudaFree would synchronise
+ * the device.
+ *
+ * The workspace is one file-scope device array of
+ * GDN2_NOALLOC_SCRATCH_BYTES, a separate copy on each device.  The first
+ * call on a device looks up that copy's address (cudaGetSymbolAddress, with
+ * the device current) and caches it; make that first call before any
+ * stream capture on the device.  A call that needs more scratch than the
+ * array holds (gdn2_chunk_fwd_workspace_bytes > GDN2_NOALLOC_SCRATCH_BYTES)
+ * returns GDN2_EWORKSPACE and launches nothing.
+ *
+ * Every call on a device shares the one array, and it keeps the last
+ * call's contents: no byte of it needs to start at zero, since each call
+ * writes every scratch byte before its kernels read it.  Calls on one
+ * stream are ordered and safe; calls whose kernels may overlap on the GPU
+ * (different streams without an ordering between them, or host threads
+ * using different streams) race on the array and corrupt each other's
+ * results. */
+GDN2_API int gdn2_chunk_fwd_noalloc(const gdn2_chunk_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
  * Fused recurrent forward: kernel (3).  T >= 1 tokens in one launch with

@@ -118,6 +118,20 @@ def test_chunk_fwd_dims_and_workspace_errors():
     assert LIB.gdn2_chunk_fwd(ctypes.byref(a), ctypes.c_void_p(1 << 20), 1 << 30, None) == _lib.GDN2_EUNSUPPORTED
 
 
+def test_chunk_fwd_noalloc_size_limit():
+    """Calls that need more than the 32 MiB static scratch are refused before
+    any CUDA call, so this runs without a GPU."""
+    from burn_gdn2 import LIB, _lib
+
+    assert LIB.gdn2_chunk_fwd_noalloc(None, None) == _lib.GDN2_EINVAL
+    a = _chunk_args()
+    a.dims = _lib.Dims(1, 1 << 16, 1, 16, 16, 16)
+    assert LIB.gdn2_chunk_fwd_workspace_bytes(ctypes.byref(a)) > 32 << 20
+    assert LIB.gdn2_chunk_fwd_noalloc(ctypes.byref(a), None) == _lib.GDN2_EWORKSPACE
+    msg = LIB.gdn2_last_error().decode()
+    assert msg.startswith("gdn2_chunk_fwd_noalloc") and str(32 << 20) in msg
+
+
 def test_recurrent_argument_errors():
     from burn_gdn2 import LIB, _lib
 
