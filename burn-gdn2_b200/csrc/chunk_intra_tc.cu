@@ -42,10 +42,22 @@ constexpr uint32_t MISC = RV + 16384;   // half-tile g sums [8][128] f32, sGlast
 constexpr uint32_t TOTAL = MISC + 4096 + 512 + 64;
 }  // namespace intra_smem
 
+// Loads of the kernel's read-only inputs.  Written as non-volatile asm
+// without a memory clobber, so the compiler may move them above the stores
+// into the record, which it would otherwise have to assume alias them.
 __device__ __forceinline__ uint2 ld4_raw(const DView& v, int bb, int h, int t, int c, bool ok) {
-  if (!ok) return make_uint2(0u, 0u);
-  return *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + h * v.s1 +
-                                         (int64_t)t * v.s2 + c);
+  uint2 r = make_uint2(0u, 0u);
+  if (ok) {
+    const void* ptr = static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + h * v.s1 + (int64_t)t * v.s2 + c;
+    asm("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(ptr));
+  }
+  return r;
+}
+
+__device__ __forceinline__ float4 ld_f4_nc(const float* ptr) {
+  float4 r;
+  asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(ptr));
+  return r;
 }
 
 __device__ __forceinline__ void unpack4(uint2 raw, float (&x)[4]) {
@@ -99,7 +111,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     for (int i = 0; i < 8; ++i) {
       const int r = r0 + i;
       float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < cv) gv = *reinterpret_cast<const float4*>(gbase + (int64_t)(t0 + r) * p.g.s2);
+      if (r < cv) gv = ld_f4_nc(gbase + (int64_t)(t0 + r) * p.g.s2);
       run[0] += gv.x; run[1] += gv.y; run[2] += gv.z; run[3] += gv.w;
       if (r == cv - 1) {
         glr[0] = run[0]; glr[1] = run[1]; glr[2] = run[2]; glr[3] = run[3];
@@ -151,23 +163,36 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   {
     unsigned char* xt = sm + X + tp * 8192;
     float gl[4] = {off[0], off[1], off[2], off[3]};  // tile-local cumsum of g at row r
+    // row i + 1 is loaded while row i is computed and stored
+    uint2 nq, nk, nb, nv = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
+    float4 ng = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto fetch = [&](int i) {
+      const int r = r0 + i;
+      const bool ok = r < cv;
+      if (ok) ng = ld_f4_nc(gbase + (int64_t)(t0 + r) * p.g.s2);
+      nq = ld4_raw(p.q, bb, kh, t0 + r, ch, ok);
+      nk = ld4_raw(p.k, bb, kh, t0 + r, ch, ok);
+      nb = ld4_raw(p.b, bb, kh, t0 + r, ch, ok);
+      if (ch < V) {
+        nv = ld4_raw(p.v, bb, hv, t0 + r, ch, ok);
+        nw = ld4_raw(p.w, bb, hv, t0 + r, ch, ok);
+      }
+    };
+    fetch(0);
     #pragma unroll 2
     for (int i = 0; i < 8; ++i) {
       const int r = r0 + i, ti = hh * 8 + i;
-      const bool ok = r < cv;
-      if (ok) {
-        const float4 gv = *reinterpret_cast<const float4*>(gbase + (int64_t)(t0 + r) * p.g.s2);
-        gl[0] += gv.x; gl[1] += gv.y; gl[2] += gv.z; gl[3] += gv.w;
+      const uint2 cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw;
+      if (r < cv) {
+        gl[0] += ng.x; gl[1] += ng.y; gl[2] += ng.z; gl[3] += ng.w;
       }
-      float q[4], k[4], b[4];
-      unpack4(ld4_raw(p.q, bb, kh, t0 + r, ch, ok), q);
-      unpack4(ld4_raw(p.k, bb, kh, t0 + r, ch, ok), k);
-      unpack4(ld4_raw(p.b, bb, kh, t0 + r, ch, ok), b);
-      float vv[4] = {0.f, 0.f, 0.f, 0.f}, ww[4] = {0.f, 0.f, 0.f, 0.f};
-      if (ch < V) {
-        unpack4(ld4_raw(p.v, bb, hv, t0 + r, ch, ok), vv);
-        unpack4(ld4_raw(p.w, bb, hv, t0 + r, ch, ok), ww);
-      }
+      if (i + 1 < 8) fetch(i + 1);
+      float q[4], k[4], b[4], vv[4], ww[4];
+      unpack4(cq, q);
+      unpack4(ck, k);
+      unpack4(cb, b);
+      unpack4(cvv, vv);
+      unpack4(cw, ww);
       float qs[4], bks[4], qg[4], rk[4], kd[4], kinv[4];
       #pragma unroll
       for (int j = 0; j < 4; ++j) {
