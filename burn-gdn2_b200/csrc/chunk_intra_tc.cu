@@ -31,11 +31,12 @@ constexpr uint32_t X = 0;               // 4 x 8 KB: K-major [32][128] per row t
 constexpr uint32_t KSV = 32768;         // Ks_p at KSV + 4096 * p(p+1)/2, [16(p+1)][128]
 constexpr uint32_t R1_END = 73728;      // 72 KB
 // reused after the score MMAs completed
-constexpr uint32_t AKK = 0;             // f32 [64][65]
-constexpr uint32_t TINV = 17408;        // f32 [64][65]
+constexpr int SS = 68;                  // row stride (floats) of AKK and TINV: 16-byte rows
+constexpr uint32_t AKK = 0;             // f32 [64][SS]
+constexpr uint32_t TINV = 17408;        // f32 [64][SS]
 constexpr uint32_t AQK_IMG = 36864;     // bf16 K-major [64][64]
 constexpr uint32_t TINV_IMG = 45056;    // bf16 K-major [64][64]
-constexpr uint32_t SCRATCH = 53248;     // 4 x f32 [16][17]
+constexpr uint32_t SCRATCH = 53248;     // 6 x f32 [16][20] blocks of the inverse
 constexpr uint32_t RK = R1_END;         // bf16 MN-major [64][128]
 constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][V], V <= 128
 constexpr uint32_t MISC = RV + 16384;   // half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem base
@@ -104,6 +105,22 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
 
   // ---- 1. sums of g over each half tile (the per-row cumsum is rebuilt below) ----
   const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
+  // inputs of row r0 + i, fetched one row ahead of their use in step 2
+  uint2 nq, nk, nb, nv = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
+  float4 ng = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto fetch = [&](int i) {
+    const int r = r0 + i;
+    const bool ok = r < cv;
+    if (ok) ng = ld_f4_nc(gbase + (int64_t)(t0 + r) * p.g.s2);
+    nq = ld4_raw(p.q, bb, kh, t0 + r, ch, ok);
+    nk = ld4_raw(p.k, bb, kh, t0 + r, ch, ok);
+    nb = ld4_raw(p.b, bb, kh, t0 + r, ch, ok);
+    if (ch < V) {
+      nv = ld4_raw(p.v, bb, hv, t0 + r, ch, ok);
+      nw = ld4_raw(p.w, bb, hv, t0 + r, ch, ok);
+    }
+  };
+  fetch(0);
   float glr[4] = {0.f, 0.f, 0.f, 0.f};  // half-local cumsum at the last valid row, if it is ours
   {
     float run[4] = {0.f, 0.f, 0.f, 0.f};
@@ -164,21 +181,6 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     unsigned char* xt = sm + X + tp * 8192;
     float gl[4] = {off[0], off[1], off[2], off[3]};  // tile-local cumsum of g at row r
     // row i + 1 is loaded while row i is computed and stored
-    uint2 nq, nk, nb, nv = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
-    float4 ng = make_float4(0.f, 0.f, 0.f, 0.f);
-    auto fetch = [&](int i) {
-      const int r = r0 + i;
-      const bool ok = r < cv;
-      if (ok) ng = ld_f4_nc(gbase + (int64_t)(t0 + r) * p.g.s2);
-      nq = ld4_raw(p.q, bb, kh, t0 + r, ch, ok);
-      nk = ld4_raw(p.k, bb, kh, t0 + r, ch, ok);
-      nb = ld4_raw(p.b, bb, kh, t0 + r, ch, ok);
-      if (ch < V) {
-        nv = ld4_raw(p.v, bb, hv, t0 + r, ch, ok);
-        nw = ld4_raw(p.w, bb, hv, t0 + r, ch, ok);
-      }
-    };
-    fetch(0);
     #pragma unroll 2
     for (int i = 0; i < 8; ++i) {
       const int r = r0 + i, ti = hh * 8 + i;
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
           const int r = 16 * pp + j;
           const float aq = (s <= r) ? vq[j] * p.scale : 0.f;
           *reinterpret_cast<__nv_bfloat16*>(sm + AQK_IMG + umma::kmaj_off(r, s, 64)) = __float2bfloat16_rn(aq);
-          sAkk[r * 65 + s] = (s < r) ? vk[j] : 0.f;
+          sAkk[r * SS + s] = (s < r) ? vk[j] : 0.f;
         }
       }
     }
@@ -276,54 +278,108 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   umma::fence_before_sync();
   __syncthreads();
 
-  // ---- 5. (I + Akk)^-1, blocked over 16 x 16 tiles ----
-  if (warp < 4 && lane < 16) {  // diagonal tile `warp`, column `lane`
+  // ---- 5. T = (I + Akk)^-1 over 16 x 16 blocks ----
+  // Diagonal blocks T_ii by forward substitution, then the blocks below
+  // them from T_ij = -T_ii sum_{m=j}^{i-1} A_im T_mj, scheduled by doubling
+  // so that four rounds of 16 x 16 block products on all warps suffice.
+  if (warp < 4 && lane < 16) {  // diagonal block `warp`, column `lane`
     const int o = 16 * warp, j = lane;
     float x[16];
     #pragma unroll
     for (int i = 0; i < 16; ++i) {
       float acc = 0.f;
       #pragma unroll
-      for (int m = 0; m < i; ++m) acc += sAkk[(o + i) * 65 + o + m] * x[m];
+      for (int m = 0; m < i; ++m) acc += sAkk[(o + i) * SS + o + m] * x[m];
       x[i] = (i == j) ? 1.f : ((i < j) ? 0.f : -acc);
     }
     #pragma unroll
-    for (int i = 0; i < 16; ++i) sTinv[(o + i) * 65 + o + j] = x[i];
+    for (int i = 0; i < 16; ++i) sTinv[(o + i) * SS + o + j] = x[i];
   }
   __syncthreads();
-  float* scr = reinterpret_cast<float*>(sm + SCRATCH);  // 4 x [16][17]
-  for (int d = 1; d < 4; ++d) {
-    const int bj = warp & 3, bi = bj + d, rh = warp >> 2;
-    const int row = rh * 8 + (lane >> 2), c0 = (lane & 3) * 4;
-    float* sc = scr + bj * 16 * 17;
-    if (bi < 4) {  // tmp = sum_m A[bi][m] Tinv[m][bj] over tiles bj .. bi-1
-      float tmp[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int m = 16 * bj; m < 16 * bi; ++m) {
-        const float a = sAkk[(16 * bi + row) * 65 + m];
-        #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) tmp[cc] += a * sTinv[m * 65 + 16 * bj + c0 + cc];
-      }
-      #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) sc[row * 17 + c0 + cc] = tmp[cc];
-    }
-    __syncthreads();
-    if (bi < 4) {  // Tinv[bi][bj] = -Tinv[bi][bi] tmp
-      float res[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    float* scr = reinterpret_cast<float*>(sm + SCRATCH);  // 6 blocks [16][20]: X10 X32 X20 X30 X21 X31
+    const int pair = warp >> 1;
+    const int row = (warp & 1) * 8 + (lane >> 2), c0 = (lane & 3) * 4;  // 4 outputs of a 16 x 16 block
+    auto AK = [&](int i, int j) { return sAkk + 16 * i * SS + 16 * j; };
+    auto TI = [&](int i, int j) { return sTinv + 16 * i * SS + 16 * j; };
+    auto XS = [&](int k) { return scr + k * 16 * 20; };
+    // acc += a_block[row][:] * b_block[:][c0 .. c0 + 3]
+    auto mac = [&](float (&acc)[4], const float* a, int as, const float* b, int bs) {
       #pragma unroll
       for (int m = 0; m < 16; ++m) {
-        const float li = sTinv[(16 * bi + row) * 65 + 16 * bi + m];
-        #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) res[cc] -= li * sc[m * 17 + c0 + cc];
+        const float x = a[row * as + m];
+        const float4 y = *reinterpret_cast<const float4*>(b + m * bs + c0);
+        acc[0] += x * y.x; acc[1] += x * y.y; acc[2] += x * y.z; acc[3] += x * y.w;
       }
-      #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) sTinv[(16 * bi + row) * 65 + 16 * bj + c0 + cc] = res[cc];
+    };
+    auto put = [&](float* d, int ds, const float (&acc)[4], float sg) {
+      *reinterpret_cast<float4*>(d + row * ds + c0) = make_float4(sg * acc[0], sg * acc[1], sg * acc[2], sg * acc[3]);
+    };
+    {  // X10 = A10 T00, X32 = A32 T22, X20 = A20 T00 (first term), X30 = A30 T00 (first term)
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int ai = pair == 0 ? 1 : pair == 2 ? 2 : 3, aj = pair == 1 ? 2 : 0;
+      mac(acc, AK(ai, aj), SS, TI(aj, aj), SS);
+      put(XS(pair), 20, acc, 1.f);
+    }
+    __syncthreads();
+    {  // T10 = -T11 X10, T32 = -T33 X32, X21 = A21 T11, X31 = A31 T11
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (pair < 2) {
+        const int d = pair == 0 ? 1 : 3;
+        mac(acc, TI(d, d), SS, XS(pair), 20);
+        put(TI(d, d - 1), SS, acc, -1.f);
+      } else {
+        mac(acc, AK(pair, 1), SS, TI(1, 1), SS);
+        put(XS(pair + 2), 20, acc, 1.f);
+      }
+    }
+    __syncthreads();
+    {  // X20 += A21 T10, X30 += A31 T10, T21 = -T22 X21, T31 = -(T32 X21 + T33 X31)
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (pair < 2) {
+        const float4 x0 = *reinterpret_cast<const float4*>(XS(2 + pair) + row * 20 + c0);
+        acc[0] = x0.x; acc[1] = x0.y; acc[2] = x0.z; acc[3] = x0.w;
+        mac(acc, AK(2 + pair, 1), SS, TI(1, 0), SS);
+        put(XS(2 + pair), 20, acc, 1.f);
+      } else if (pair == 2) {
+        mac(acc, TI(2, 2), SS, XS(4), 20);
+        put(TI(2, 1), SS, acc, -1.f);
+      } else {
+        mac(acc, TI(3, 2), SS, XS(4), 20);
+        mac(acc, TI(3, 3), SS, XS(5), 20);
+        put(TI(3, 1), SS, acc, -1.f);
+      }
+    }
+    __syncthreads();
+    if (pair < 2) {  // T20 = -T22 X20, T30 = -(T32 X20 + T33 X30)
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (pair == 0) {
+        mac(acc, TI(2, 2), SS, XS(2), 20);
+        put(TI(2, 0), SS, acc, -1.f);
+      } else {
+        mac(acc, TI(3, 2), SS, XS(2), 20);
+        mac(acc, TI(3, 3), SS, XS(3), 20);
+        put(TI(3, 0), SS, acc, -1.f);
+      }
     }
     __syncthreads();
   }
-  for (int idx = tid; idx < 64 * 64; idx += 256) {
-    const int r = idx >> 6, s2 = idx & 63;
-    const float val = (s2 == r) ? 1.f : ((s2 < r) ? sTinv[r * 65 + s2] : 0.f);
-    *reinterpret_cast<__nv_bfloat16*>(sm + TINV_IMG + umma::kmaj_off(r, s2, 64)) = __float2bfloat16_rn(val);
+  // bf16 image of T (unit diagonal, zero above), 8 elements per store
+  for (int idx = tid; idx < 64 * 8; idx += 256) {
+    const int r = idx >> 3, c8 = idx & 7;
+    const float4 lo = *reinterpret_cast<const float4*>(sTinv + r * SS + 8 * c8);
+    const float4 hi = *reinterpret_cast<const float4*>(sTinv + r * SS + 8 * c8 + 4);
+    const float in[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    float val[8];
+    #pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int s2 = 8 * c8 + e;
+      val[e] = (s2 == r) ? 1.f : ((s2 < r) ? in[e] : 0.f);
+    }
+    uint4 o;
+    o.x = umma::pack_bf16x2(val[0], val[1]); o.y = umma::pack_bf16x2(val[2], val[3]);
+    o.z = umma::pack_bf16x2(val[4], val[5]); o.w = umma::pack_bf16x2(val[6], val[7]);
+    *reinterpret_cast<uint4*>(sm + TINV_IMG + umma::kmaj_chunk(r, c8, 64)) = o;
   }
   fence_proxy_async_smem();
   umma::fence_before_sync();
