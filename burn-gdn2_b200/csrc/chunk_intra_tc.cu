@@ -61,6 +61,22 @@ __device__ __forceinline__ float4 ld_f4_nc(const float* ptr) {
   return r;
 }
 
+__device__ __forceinline__ void l2_prefetch(const void* a) { asm volatile("prefetch.global.L2 [%0];" ::"l"(a)); }
+
+// Line j (0..13) of token t's inputs: q k b v w (two 128-byte lines each), g (four).
+__device__ __forceinline__ void prefetch_line(const TcParams& p, int bb, int kh, int hv, int t, int j) {
+  if (j < 10) {
+    if (j >= 6 && (j & 1) && p.V <= 64) return;
+    const DView& v = j < 2 ? p.q : j < 4 ? p.k : j < 6 ? p.b : j < 8 ? p.v : p.w;
+    const int h = j < 6 ? kh : hv;
+    l2_prefetch(reinterpret_cast<const char*>(static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + h * v.s1 +
+                                              (int64_t)t * v.s2) + (j & 1) * 128);
+  } else {
+    l2_prefetch(reinterpret_cast<const char*>(static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 +
+                                              (int64_t)t * p.g.s2) + (j - 10) * 128);
+  }
+}
+
 __device__ __forceinline__ void unpack4(uint2 raw, float (&x)[4]) {
   const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
   const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
@@ -101,6 +117,12 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_mbar_init();
+  }
+
+  // every input line of this warp's 8 rows on its way to L2 before the first use
+  for (int idx = lane; idx < 8 * 14; idx += 32) {
+    const int r = r0 + idx / 14;
+    if (r < cv) prefetch_line(p, bb, kh, hv, t0 + r, idx % 14);
   }
 
   // ---- 1. sums of g over each half tile (the per-row cumsum is rebuilt below) ----
@@ -163,14 +185,16 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   __syncthreads();  // sGlast
 
   // ---- 2. operands (compact loop: the code must stay in the instruction cache) ----
-  float glast[4];
-  #pragma unroll
-  for (int j = 0; j < 4; ++j) glast[j] = sGlast[ch + j];
-  // per-channel constants of this row tile: gamma = e^{Gb_p} E, Ks_pp = k E^-1 e^{Gb_pp - Gb_p}
-  float eGbp[4], cks[4][4];
+  const float4 glast4 = *reinterpret_cast<const float4*>(sGlast + ch);
+  const float glast[4] = {glast4.x, glast4.y, glast4.z, glast4.w};
+  // per-channel constants of this row tile (E = e^{gl}, the tile-local decay):
+  // gamma = e^{Gb_p} E, Kd = k E^-1 e^{G_last - Gb_p}, Ks_pp = k E^-1 e^{Gb_pp - Gb_p}
+  float eGbp[4], eGbpS[4], edk[4], cks[4][4];
   #pragma unroll
   for (int j = 0; j < 4; ++j) {
     eGbp[j] = __expf(Gbp[j]);
+    eGbpS[j] = eGbp[j] * p.scale;
+    edk[j] = __expf(glast[j] - Gbp[j]);
     #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
       const float gbpp = pp == 0 ? Gb[0][j] : pp == 1 ? Gb[1][j] : pp == 2 ? Gb[2][j] : Gb[3][j];
@@ -200,14 +224,12 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
       for (int j = 0; j < 4; ++j) {
         const float e = __expf(gl[j]);
         const float ei = __expf(-gl[j]);
-        const float G = Gbp[j] + gl[j];
-        const float gam = eGbp[j] * e;
         qs[j] = q[j] * e;
         bks[j] = b[j] * k[j] * e;
-        qg[j] = q[j] * gam * p.scale;
-        rk[j] = b[j] * k[j] * gam;
-        kd[j] = k[j] * __expf(glast[j] - G);
+        qg[j] = qs[j] * eGbpS[j];
+        rk[j] = bks[j] * eGbp[j];
         kinv[j] = k[j] * ei;
+        kd[j] = kinv[j] * edk[j];
       }
       *reinterpret_cast<uint2*>(xt + umma::kmaj_off(ti, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
       *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + ti, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
