@@ -56,6 +56,21 @@ class RecurrentArgs(ctypes.Structure):
                 ("gate", View), ("o_norm_weight", ctypes.c_void_p), ("state", ctypes.c_void_p), ("out", View)]
 
 
+class PrologueArgs(ctypes.Structure):
+    _fields_ = [("dims", Dims), ("dtype", ctypes.c_int32), ("use_short_conv", ctypes.c_int32),
+                ("allow_neg_eigval", ctypes.c_int32), ("min_decay", ctypes.c_float),
+                ("q_raw", ctypes.c_void_p), ("k_raw", ctypes.c_void_p), ("v_raw", ctypes.c_void_p),
+                ("b_raw", ctypes.c_void_p), ("w_raw", ctypes.c_void_p), ("f_raw", ctypes.c_void_p),
+                ("ld_q", ctypes.c_int64), ("ld_k", ctypes.c_int64), ("ld_v", ctypes.c_int64),
+                ("ld_b", ctypes.c_int64), ("ld_w", ctypes.c_int64), ("ld_f", ctypes.c_int64),
+                ("conv_w_q", ctypes.c_void_p), ("conv_w_k", ctypes.c_void_p), ("conv_w_v", ctypes.c_void_p),
+                ("conv_q_in", ctypes.c_void_p), ("conv_k_in", ctypes.c_void_p), ("conv_v_in", ctypes.c_void_p),
+                ("conv_q_out", ctypes.c_void_p), ("conv_k_out", ctypes.c_void_p), ("conv_v_out", ctypes.c_void_p),
+                ("a_log", ctypes.c_void_p), ("dt_bias", ctypes.c_void_p), ("decay_factors", ctypes.c_void_p),
+                ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("b", ctypes.c_void_p),
+                ("w", ctypes.c_void_p), ("g", ctypes.c_void_p)]
+
+
 class Config(ctypes.Structure):
     _fields_ = [("hidden_size", ctypes.c_int64), ("num_heads", ctypes.c_int64), ("head_dim", ctypes.c_int64),
                 ("expand_v", ctypes.c_float), ("num_v_heads", ctypes.c_int64), ("use_short_conv", ctypes.c_int32),
@@ -68,7 +83,7 @@ EXPORTS = (
     "gdn2_chunk_fwd_workspace_bytes", "gdn2_chunk_fwd", "gdn2_chunk_intra", "gdn2_chunk_inter",
     "gdn2_recurrent_fwd", "gdn2_short_conv", "gdn2_rms_norm_gate", "gdn2_config_validate",
     "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
-    "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc",
+    "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc", "gdn2_project_activations",
 )
 
 
@@ -83,6 +98,8 @@ def _load():
     for fn in ("gdn2_chunk_fwd", "gdn2_chunk_intra", "gdn2_chunk_inter"):
         getattr(lib, fn).argtypes = [P(ChunkArgs), vp, sz, vp]
         getattr(lib, fn).restype = ctypes.c_int
+    lib.gdn2_project_activations.argtypes = [P(PrologueArgs), vp]
+    lib.gdn2_project_activations.restype = ctypes.c_int
     lib.gdn2_chunk_fwd_noalloc.argtypes = [P(ChunkArgs), vp]
     lib.gdn2_chunk_fwd_noalloc.restype = ctypes.c_int
     lib.gdn2_recurrent_fwd.argtypes = [P(RecurrentArgs), vp]

@@ -29,8 +29,8 @@ import torch.nn.functional as F
 from . import _lib
 from ._lib import LIB, check
 from .config import Gdn2Config, Gdn2Mode
-from .ops import (SHORT_CONV_CACHE, chunk_args, chunk_workspace, l2_normalize_4d, recurrent_args,
-                  rms_norm_gate_per_head, short_conv_1d, stream_handle, view4)
+from .ops import (SHORT_CONV_CACHE, chunk_args, chunk_workspace, project_activations, recurrent_args,
+                  rms_norm_gate_per_head, stream_handle, view4)
 
 FUSED_RECURRENT_MAX_SEQ = 64  # src/module.rs:17
 
@@ -180,37 +180,51 @@ class GatedDeltaNet2:
         return g.contiguous(), b, w, gate
 
     # -- src/module.rs:381-498 ----------------------------------------------
+    def _proj_weight(self):
+        """[D, 3*KD + 2*VD + 2*vh] concatenation of the q, k, v, b, w,
+        f_proj_0 and g_proj_0 weights: one GEMM reads x once.  Rebuilt when
+        any of the weights is replaced or modified in place."""
+        parts = (self.q_proj, self.k_proj, self.v_proj, self.b_proj, self.w_proj, self.f_proj_0, self.g_proj_0)
+        key = tuple((l.weight.data_ptr(), l.weight._version) for l in parts)
+        if getattr(self, "_wcat_key", None) != key:
+            self._wcat = torch.cat([l.weight for l in parts], dim=1).contiguous()
+            self._wcat_key = key
+        return self._wcat
+
     def project(self, x, conv_cache=None, grouped=None):
         """Projection pipeline.  Returns (ProjectedInputs, conv_out or None).
-        q,k,g,b are [B,HV,T,K] views (or [B,H,T,K] with grouped=True)."""
+        q,k,g,b are [B,HV,T,K] views (or [B,H,T,K] with grouped=True).
+
+        One GEMM for the q, k, v, b, w and low-rank f / gate projections,
+        the two low-rank up-projections, then gdn2_project_activations for
+        every elementwise step (short conv, SiLU, L2, sigmoid gates, decay)."""
         self._validate_input(x)
         c = self.config
         h, hk, hv, vh = self._dims
         B, T, _ = x.shape
-        x = x.to(self.dtype)
+        kd, vd = h * hk, hv * vh
+        x2 = x.to(self.dtype).reshape(B * T, -1)
         grouped = (self.gva_mode == "grouped") if grouped is None else grouped
-        q_raw, k_raw, v_raw = self.q_proj.forward(x), self.k_proj.forward(x), self.v_proj.forward(x)
-        if c.use_short_conv:
-            cq, ck, cv = conv_cache if conv_cache is not None else (None, None, None)
-            q_act, nq = short_conv_1d(q_raw, self.q_conv_w, cq)
-            k_act, nk = short_conv_1d(k_raw, self.k_conv_w, ck)
-            v_act, nv = short_conv_1d(v_raw, self.v_conv_w, cv)
-            conv_out = (nq, nk, nv)
-        else:
-            q_act, k_act, v_act = F.silu(q_raw), F.silu(k_raw), F.silu(v_raw)
-            conv_out = None
-        g, b, w, gate = self._gates(x)
+        y = x2 @ self._proj_weight()
+        o = [0, kd, 2 * kd, 2 * kd + vd, 3 * kd + vd, 3 * kd + 2 * vd, 3 * kd + 2 * vd + vh]
+        cols = lambda i, n: y[:, o[i]:o[i] + n]
+        f_raw = cols(5, vh) @ self.f_proj_1.weight
+        gate = torch.addmm(self.g_proj_1.bias, cols(6, vh), self.g_proj_1.weight)
+        conv_w = (self.q_conv_w, self.k_conv_w, self.v_conv_w) if c.use_short_conv else None
+        (q, k, v, b, w, g), conv_out = project_activations(
+            cols(0, kd), cols(1, kd), cols(2, vd), cols(3, kd), cols(4, vd), f_raw, batch=B, num_heads=h,
+            head_k_dim=hk, num_v_heads=hv, head_v_dim=vh, a_log=self.a_log, dt_bias=self.dt_bias, conv_w=conv_w,
+            conv_in=conv_cache if c.use_short_conv else None, allow_neg_eigval=c.allow_neg_eigval,
+            min_decay=c.min_decay, decay_factors=self.decay_factors)
         to4 = lambda t, n, d: t.reshape(B, T, n, d).permute(0, 2, 1, 3)
-        q4 = l2_normalize_4d(to4(q_act, h, hk), 1e-6)
-        k4 = l2_normalize_4d(to4(k_act, h, hk), 1e-6)
-        g4, b4 = to4(g, h, hk), to4(b, h, hk)
+        q4, k4, g4, b4 = to4(q, h, hk), to4(k, h, hk), to4(g, h, hk), to4(b, h, hk)
         if hv > h and not grouped:
             rep = hv // h
             r = lambda t: t.unsqueeze(3).repeat(1, 1, 1, rep, 1).reshape(B, hv, T, hk)
             q4, k4, g4, b4 = r(q4), r(k4), r(g4), r(b4)
-        p = ProjectedInputs(q=q4, k=k4, v=to4(v_act, hv, vh), g=g4, b=b4, w=to4(w, hv, vh),
+        p = ProjectedInputs(q=q4, k=k4, v=to4(v, hv, vh), g=g4, b=b4, w=to4(w, hv, vh),
                             gate=gate.reshape(B, T, hv, vh), o_norm=self.o_norm_weight, eps=c.norm_eps, hv=hv,
-                            vd=hv * vh, grouped=bool(grouped and hv > h))
+                            vd=vd, grouped=bool(grouped and hv > h))
         return p, conv_out
 
     # -- cores ----------------------------------------------------------------

@@ -195,6 +195,68 @@ def short_conv_1d(x, weight, cache=None):
     return y, cout
 
 
+def project_activations(q_raw, k_raw, v_raw, b_raw, w_raw, f_raw, *, batch, num_heads, head_k_dim, num_v_heads,
+                        head_v_dim, a_log, dt_bias, conv_w=None, conv_in=None, allow_neg_eigval=False,
+                        min_decay=None, decay_factors=None):
+    """Elementwise part of ``project`` (src/module.rs:381-498) in one launch:
+    q, k = L2(SiLU(conv4(raw))), v = SiLU(conv4(v_raw)), b, w = sigmoid
+    (b x 2 with neg-eig), g = -exp(A_log) softplus(f_raw + dt_bias) (f32,
+    min_decay remap).  Raw inputs: [B*T, C] row-major views (unit column
+    stride, any row stride, e.g. column slices of one GEMM output).
+    ``conv_w`` = (q, k, v) [C,4] weights or None (no short conv);
+    ``conv_in`` = (q, k, v) [B,3,C] caches or None (replicate token 0).
+    Returns (q, k, v, b, w, g) as [B*T, C] tensors and the new conv caches
+    (or None)."""
+    raws = (q_raw, k_raw, v_raw, b_raw, w_raw, f_raw)
+    _require_cuda(*raws)
+    dt = q_raw.dtype
+    for r in raws:
+        if r.dtype != dt or r.dim() != 2 or r.stride(1) != 1:
+            raise ValueError("project_activations: raw inputs must be 2-D, unit column stride, one dtype")
+    N = q_raw.shape[0]
+    kd, vd = num_heads * head_k_dim, num_v_heads * head_v_dim
+    dev = q_raw.device
+    a = _lib.PrologueArgs()
+    a.dims = _lib.Dims(batch, N // batch, num_heads, num_v_heads, head_k_dim, head_v_dim)
+    a.dtype = dtype_code(dt)
+    a.use_short_conv = int(conv_w is not None)
+    a.allow_neg_eigval = int(bool(allow_neg_eigval))
+    a.min_decay = -1.0 if min_decay is None else float(min_decay)
+    for name, r in zip(("q", "k", "v", "b", "w", "f"), raws):
+        setattr(a, name + "_raw", r.data_ptr())
+        setattr(a, "ld_" + name, r.stride(0))
+    f32 = lambda t: None if t is None else t.to(dev, torch.float32).contiguous()
+    keep = []
+    conv_out = None
+    if conv_w is not None:
+        cw = [f32(w) for w in conv_w]
+        keep += cw
+        a.conv_w_q, a.conv_w_k, a.conv_w_v = (t.data_ptr() for t in cw)
+        if conv_in is not None:
+            ci = [f32(c) for c in conv_in]
+            keep += ci
+            a.conv_q_in, a.conv_k_in, a.conv_v_in = (t.data_ptr() for t in ci)
+        conv_out = tuple(torch.empty(batch, SHORT_CONV_CACHE, n, dtype=torch.float32, device=dev)
+                         for n in (kd, kd, vd))
+        a.conv_q_out, a.conv_k_out, a.conv_v_out = (t.data_ptr() for t in conv_out)
+    al, dtb = f32(a_log), f32(dt_bias)
+    keep += [al, dtb]
+    a.a_log, a.dt_bias = al.data_ptr(), dtb.data_ptr()
+    if min_decay is not None:
+        dfac = f32(decay_factors).reshape(-1)
+        keep.append(dfac)
+        a.decay_factors = dfac.data_ptr()
+    q = torch.empty(N, kd, dtype=dt, device=dev)
+    k = torch.empty_like(q)
+    b = torch.empty_like(q)
+    v = torch.empty(N, vd, dtype=dt, device=dev)
+    w = torch.empty_like(v)
+    g = torch.empty(N, kd, dtype=torch.float32, device=dev)
+    a.q, a.k, a.v, a.b, a.w, a.g = (t.data_ptr() for t in (q, k, v, b, w, g))
+    check(LIB.gdn2_project_activations(ctypes.byref(a), stream_handle(dev)))
+    return (q, k, v, b, w, g), conv_out
+
+
 def l2_normalize_4d(x, eps=1e-6):
     """x / sqrt(sum_K x^2 + eps) (src/l2norm.rs:13-16)."""
     xf = x.float()

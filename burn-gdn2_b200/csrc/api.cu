@@ -40,6 +40,7 @@ int launch_short_conv(int B, int Tn, int C, int dtype, const void* x, const floa
                       void* y, cudaStream_t st);
 int launch_rms_norm_gate(const gdn2_dims& d, int dtype, const gdn2_view& o, const gdn2_view& gate, const float* w,
                          float eps, const gdn2_view& out, cudaStream_t st);
+int launch_project_activations(const gdn2_prologue_args* a, cudaStream_t st);
 
 static int check_dims(const gdn2_dims& d, const char* fn) {
   if (d.batch <= 0 || d.seq_len <= 0 || d.num_heads <= 0 || d.num_v_heads <= 0 || d.head_k_dim <= 0 ||
@@ -267,6 +268,11 @@ int gdn2_selftest_umma(int32_t test, const float* a, const float* b, float* d, v
 int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, void* stream) {
   if (!a) return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: null args");
   return launch_recurrent(a, (cudaStream_t)stream);
+}
+
+int gdn2_project_activations(const gdn2_prologue_args* a, void* stream) {
+  if (!a) return set_error(GDN2_EINVAL, "gdn2_project_activations: null args");
+  return launch_project_activations(a, (cudaStream_t)stream);
 }
 
 int gdn2_short_conv(int32_t batch, int32_t seq_len, int32_t channels, int32_t dtype, const void* x,

@@ -191,6 +191,50 @@ typedef struct gdn2_recurrent_args {
 GDN2_API int gdn2_recurrent_fwd(const gdn2_recurrent_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Projection activations: everything elementwise in GatedDeltaNet2::project
+ * (src/module.rs:381-498) between the caller's projection GEMMs and the
+ * core, in one launch.  Replaces short_conv_1d (src/short_conv.rs:22-65),
+ * the SiLU, l2_normalize_4d (src/l2norm.rs:13-16), the decay
+ * g = -exp(A_log) softplus(f + dt_bias) with the min_decay remap
+ * (src/module.rs:417-440) and the sigmoid gates (:441-443, b x 2 with
+ * allow_neg_eigval :470-472):
+ *
+ *   q, k = L2(SiLU(conv4(q_raw / k_raw)))   per head of K, eps 1e-6 in the sqrt
+ *   v    = SiLU(conv4(v_raw))
+ *   b    = sigmoid(b_raw) (x 2 with allow_neg_eigval),   w = sigmoid(w_raw)
+ *   g    = -exp(A_log[h]) softplus(f_raw + dt_bias)        (f32)
+ *   min_decay >= 0: g = log(sigmoid(decay_factors) (1 - min_decay) e^g + min_decay)
+ *
+ * use_short_conv = 0 drops conv4 (src/module.rs:415).  Raw inputs are
+ * row-major [B*T][ld_*] in `dtype`, channel c at column c (column slices of
+ * one concatenated GEMM output work; ld and the base must allow 8-byte bf16
+ * / 16-byte f32 vector loads).  Outputs q, k, b: [B*T][H*K], v, w:
+ * [B*T][HV*V] contiguous in `dtype`; g: [B*T][H*K] f32.  conv_*_in [B,3,C]
+ * f32 or NULL (replicate token 0, src/short_conv.rs:42-54); conv_*_out
+ * [B,3,C] f32 or NULL receives the last three raw rows and must not alias
+ * conv_*_in.  K <= 256; K and V multiples of 4.
+ * ---------------------------------------------------------------------- */
+typedef struct gdn2_prologue_args {
+  gdn2_dims dims; /* num_heads = key heads H, num_v_heads = HV */
+  int32_t dtype;
+  int32_t use_short_conv;
+  int32_t allow_neg_eigval;
+  float min_decay; /* < 0: no remap */
+  const void *q_raw, *k_raw, *v_raw, *b_raw, *w_raw, *f_raw;
+  int64_t ld_q, ld_k, ld_v, ld_b, ld_w, ld_f;
+  const float *conv_w_q, *conv_w_k, *conv_w_v;       /* [C][4] */
+  const float *conv_q_in, *conv_k_in, *conv_v_in;    /* [B,3,C] or NULL */
+  float *conv_q_out, *conv_k_out, *conv_v_out;       /* [B,3,C] or NULL */
+  const float* a_log;         /* [H] */
+  const float* dt_bias;       /* [H*K] */
+  const float* decay_factors; /* [H*K], read when min_decay >= 0 */
+  void *q, *k, *v, *b, *w;
+  float* g;
+} gdn2_prologue_args;
+
+GDN2_API int gdn2_project_activations(const gdn2_prologue_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
  * Standalone pieces of the layer around the core.
  * ---------------------------------------------------------------------- */
 /* short_conv_1d (src/short_conv.rs:22-65): y = silu(causal conv4(x)).

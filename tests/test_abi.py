@@ -39,8 +39,12 @@ def test_struct_layout_matches_header():
 #include "gdn2.h"
 #define P(T, F) printf(#T "." #F " %zu\n", offsetof(T, F));
 int main() {
-  printf("view %zu\ndims %zu\nchunk %zu\nrec %zu\ncfg %zu\n", sizeof(gdn2_view), sizeof(gdn2_dims),
-         sizeof(gdn2_chunk_args), sizeof(gdn2_recurrent_args), sizeof(gdn2_config));
+  printf("view %zu\ndims %zu\nchunk %zu\nrec %zu\ncfg %zu\npro %zu\n", sizeof(gdn2_view), sizeof(gdn2_dims),
+         sizeof(gdn2_chunk_args), sizeof(gdn2_recurrent_args), sizeof(gdn2_config), sizeof(gdn2_prologue_args));
+  P(gdn2_prologue_args, min_decay) P(gdn2_prologue_args, q_raw) P(gdn2_prologue_args, ld_q)
+  P(gdn2_prologue_args, ld_f) P(gdn2_prologue_args, conv_w_q) P(gdn2_prologue_args, conv_v_out)
+  P(gdn2_prologue_args, a_log) P(gdn2_prologue_args, decay_factors) P(gdn2_prologue_args, q)
+  P(gdn2_prologue_args, g)
   P(gdn2_chunk_args, scale) P(gdn2_chunk_args, q) P(gdn2_chunk_args, gate) P(gdn2_chunk_args, o_norm_weight)
   P(gdn2_chunk_args, state) P(gdn2_chunk_args, out)
   P(gdn2_recurrent_args, q) P(gdn2_recurrent_args, conv_w_q) P(gdn2_recurrent_args, conv_v_out)
@@ -62,8 +66,9 @@ int main() {
     assert got["chunk"] == ctypes.sizeof(_lib.ChunkArgs)
     assert got["rec"] == ctypes.sizeof(_lib.RecurrentArgs)
     assert got["cfg"] == ctypes.sizeof(_lib.Config)
+    assert got["pro"] == ctypes.sizeof(_lib.PrologueArgs)
     names = {"gdn2_chunk_args": _lib.ChunkArgs, "gdn2_recurrent_args": _lib.RecurrentArgs,
-             "gdn2_config": _lib.Config}
+             "gdn2_config": _lib.Config, "gdn2_prologue_args": _lib.PrologueArgs}
     for key, off in got.items():
         if "." in key:
             t, f = key.split(".")
