@@ -22,7 +22,7 @@ int set_error(int code, const char* fmt, ...);
 
 namespace {
 
-constexpr int PRO_ROWS = 32;    // tokens per warp task
+constexpr int PRO_ROWS = 64;    // tokens per warp task
 constexpr int PRO_WARPS = 8;    // warps per CTA
 
 struct ProParams {
@@ -91,11 +91,35 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// Approximate reciprocal division (MUFU) instead of the IEEE sequence: the
+// results are rounded to bf16 or checked at f32 tolerance, and for x -> -inf
+// the reciprocal of +inf is 0, so both functions still go to 0.
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// softplus(x) = log(1 + e^x) (burn's activation::softplus, beta 1); above 20
-// it equals x to f32 precision, and taking x there keeps e^x from overflowing.
-__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+// softplus(x) = log(1 + e^x) (burn's activation::softplus, beta 1), with
+// y = e^x:
+//  - y < 1/8: the alternating series log(1 + y) = y - y^2/2 + y^3/3 - ...
+//    up to y^7/7; the truncation error is below y^8/8, i.e. under 1e-7 of
+//    the result;
+//  - otherwise ln 2 * log2(1 + y) with the hardware base-2 logarithm
+//    (lg2.approx, absolute error ~2^-22 against log2(1 + y) >= 0.17);
+//  - above 20 the result is x to f32 precision (and e^x could overflow).
+// Relative error about 1e-6 over the whole range (checked against numpy).
+__device__ __forceinline__ float softplus_f(float x) {
+  const float y = __expf(x);
+  float s = fmaf(y, 1.f / 7.f, -1.f / 6.f);
+  s = fmaf(y, s, 1.f / 5.f);
+  s = fmaf(y, s, -1.f / 4.f);
+  s = fmaf(y, s, 1.f / 3.f);
+  s = fmaf(y, s, -1.f / 2.f);
+  s = fmaf(y, s, 1.f);
+  const float small = y * s;
+  float l2;
+  asm("lg2.approx.f32 %0, %1;" : "=f"(l2) : "f"(1.f + y));
+  const float large = l2 * 0.6931471805599453f;  // ln 2
+  return x > 20.f ? x : (y < 0.125f ? small : large);
+}
 
 // Three halo rows (oldest first) of channels c..c+3 before token t0.
 template <typename T>
@@ -128,12 +152,12 @@ __device__ __forceinline__ void store_cache(float* cout, int C, int b, int c, co
 }
 
 // conv4 + SiLU of one 4-channel slice; shifts the window.
-__device__ __forceinline__ void conv_silu(bool use_conv, const float (&w)[4][4], float (&h)[3][4], const float (&x)[4],
-                                          float (&y)[4]) {
+template <bool CONV>
+__device__ __forceinline__ void conv_silu(const float (&w)[4][4], float (&h)[3][4], const float (&x)[4], float (&y)[4]) {
   #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const float s = use_conv ? (w[j][0] * h[0][j] + w[j][1] * h[1][j] + w[j][2] * h[2][j] + w[j][3] * x[j]) : x[j];
-    y[j] = silu_f(s);
+    const float s = CONV ? (w[j][0] * h[0][j] + w[j][1] * h[1][j] + w[j][2] * h[2][j] + w[j][3] * x[j]) : x[j];
+    y[j] = silu_fast(s);
     h[0][j] = h[1][j];
     h[1][j] = h[2][j];
     h[2][j] = x[j];
@@ -154,7 +178,7 @@ constexpr int PRO_BATCH = 4;
 
 // conv4 + SiLU stream over tokens [t0, t1), optionally L2-normalised over
 // the NG groups (one key head): q, k (L2 = true) and v (L2 = false).
-template <typename T, int NG, bool L2>
+template <typename T, int NG, bool L2, bool CONV>
 __device__ __forceinline__ void conv_task(const ProParams& p, const T* raw, int64_t ld, int C, const float* taps,
                                           const float* cin, float* cout, T* out, int bb, int t0, int t1,
                                           const int (&c)[NG], const bool (&on)[NG]) {
@@ -168,18 +192,21 @@ __device__ __forceinline__ void conv_task(const ProParams& p, const T* raw, int6
         w[gi][i][j] = 0.f;
         if (i < 3) h[gi][i][j] = 0.f;
       }
-    if (on[gi] && p.use_conv) {
+    if (on[gi] && CONV) {
       load_taps(taps, c[gi], w[gi]);
       load_halo<T>(raw, ld, cin, C, bb, p.T, t0, c[gi], h[gi]);
     }
   }
+  const T* src = raw + ((int64_t)bb * p.T + t0) * ld;  // row t0
+  T* dst_row = out + ((int64_t)bb * p.T + t0) * C;       // row t0
   Raw4<T> cur[PRO_BATCH][NG], nxt[PRO_BATCH][NG];
   auto fetch = [&](int tb, Raw4<T> (&dst)[PRO_BATCH][NG]) {
+    const T* rp = src + (int64_t)(tb - t0) * ld;
     #pragma unroll
     for (int r = 0; r < PRO_BATCH; ++r)
       #pragma unroll
       for (int gi = 0; gi < NG; ++gi)
-        if (on[gi] && tb + r < t1) dst[r][gi] = ld_raw4(raw + ((int64_t)bb * p.T + tb + r) * ld + c[gi]);
+        if (on[gi] && tb + r < t1) dst[r][gi] = ld_raw4(rp + r * ld + c[gi]);
   };
   fetch(t0, cur);
   #pragma unroll 1
@@ -195,7 +222,7 @@ __device__ __forceinline__ void conv_task(const ProParams& p, const T* raw, int6
       for (int gi = 0; gi < NG; ++gi) {
         float x[4] = {0.f, 0.f, 0.f, 0.f};  // lanes past the head: taps, window and x are zero, so y = 0
         if (on[gi]) unpack(cur[r][gi], x);
-        conv_silu(p.use_conv, w[gi], h[gi], x, y[gi]);
+        conv_silu<CONV>(w[gi], h[gi], x, y[gi]);
         #pragma unroll
         for (int j = 0; j < 4; ++j) ss += y[gi][j] * y[gi][j];
       }
@@ -207,7 +234,7 @@ __device__ __forceinline__ void conv_task(const ProParams& p, const T* raw, int6
         float o[4];
         #pragma unroll
         for (int j = 0; j < 4; ++j) o[j] = y[gi][j] * inv;
-        store4(out + ((int64_t)bb * p.T + t) * C + c[gi], o);
+        store4(dst_row + (int64_t)(t - t0) * C + c[gi], o);
       }
     }
     #pragma unroll
@@ -215,7 +242,7 @@ __device__ __forceinline__ void conv_task(const ProParams& p, const T* raw, int6
       #pragma unroll
       for (int gi = 0; gi < NG; ++gi) cur[r][gi] = nxt[r][gi];
   }
-  if (p.use_conv && cout && t1 == p.T) {
+  if (CONV && cout && t1 == p.T) {
     #pragma unroll
     for (int gi = 0; gi < NG; ++gi)
       if (on[gi]) store_cache(cout, C, bb, c[gi], h[gi]);
@@ -238,11 +265,14 @@ __device__ __forceinline__ void gate_task(const ProParams& p, const T* raw, int6
     }
   }
   const float sc = (KIND == 3 && p.negeig) ? 2.f : 1.f;
+  const T* src = raw + ((int64_t)bb * p.T + t0) * ld + c;  // row t0
+  const int64_t out0 = ((int64_t)bb * p.T + t0) * C + c;
   Raw4<T> cur[PRO_BATCH], nxt[PRO_BATCH];
   auto fetch = [&](int tb, Raw4<T> (&dst)[PRO_BATCH]) {
+    const T* rp = src + (int64_t)(tb - t0) * ld;
     #pragma unroll
     for (int r = 0; r < PRO_BATCH; ++r)
-      if (on && tb + r < t1) dst[r] = ld_raw4(raw + ((int64_t)bb * p.T + tb + r) * ld + c);
+      if (on && tb + r < t1) dst[r] = ld_raw4(rp + r * ld);
   };
   fetch(t0, cur);
   #pragma unroll 1
@@ -264,7 +294,7 @@ __device__ __forceinline__ void gate_task(const ProParams& p, const T* raw, int6
           o[j] = sigmoid_f(x[j]) * sc;
         }
       }
-      const int64_t off = ((int64_t)bb * p.T + t) * C + c;
+      const int64_t off = out0 + (int64_t)(t - t0) * C;
       if (KIND == 5) store4(static_cast<float*>(out) + off, o);
       else store4(static_cast<T*>(out) + off, o);
     }
@@ -275,7 +305,7 @@ __device__ __forceinline__ void gate_task(const ProParams& p, const T* raw, int6
 
 // Conv streams, per (batch, token block): H q heads, H k heads, then the
 // 128-channel slices of v.
-template <typename T, int NGK>
+template <typename T, int NGK, bool CONV>
 __global__ void __launch_bounds__(PRO_WARPS * 32, 2) k_prologue_conv(const ProParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t task = (int64_t)blockIdx.x * PRO_WARPS + (threadIdx.x >> 5);
@@ -298,7 +328,7 @@ __global__ void __launch_bounds__(PRO_WARPS * 32, 2) k_prologue_conv(const ProPa
       on[gi] = cc < p.K;
       c[gi] = h * p.K + (on[gi] ? cc : 0);
     }
-    conv_task<T, NGK, true>(p, static_cast<const T*>(isk ? p.kr : p.qr), isk ? p.ldk : p.ldq, KD,
+    conv_task<T, NGK, true, CONV>(p, static_cast<const T*>(isk ? p.kr : p.qr), isk ? p.ldk : p.ldq, KD,
                             isk ? p.cwk : p.cwq, isk ? p.cik : p.ciq, isk ? p.cok : p.coq,
                             static_cast<T*>(isk ? p.k : p.q), bb, t0, t1, c, on);
     return;
@@ -307,7 +337,7 @@ __global__ void __launch_bounds__(PRO_WARPS * 32, 2) k_prologue_conv(const ProPa
   const int cc = 128 * u + 4 * lane;
   const int c[1] = {cc < VD ? cc : 0};
   const bool on[1] = {cc < VD};
-  conv_task<T, 1, false>(p, static_cast<const T*>(p.vr), p.ldv, VD, p.cwv, p.civ, p.cov, static_cast<T*>(p.v), bb,
+  conv_task<T, 1, false, CONV>(p, static_cast<const T*>(p.vr), p.ldv, VD, p.cwv, p.civ, p.cov, static_cast<T*>(p.v), bb,
                          t0, t1, c, on);
 }
 
@@ -346,7 +376,11 @@ int launch_t(const ProParams& p, cudaStream_t st) {
   const int SK = (KD + 127) / 128, SV = (VD + 127) / 128;
   const int64_t conv_tasks = (int64_t)p.B * p.ntb * (2 * p.H + SV);
   const int64_t gate_tasks = (int64_t)p.B * p.ntb * (2 * SK + SV);
-  k_prologue_conv<T, NGK><<<(unsigned)((conv_tasks + PRO_WARPS - 1) / PRO_WARPS), PRO_WARPS * 32, 0, st>>>(p);
+  const unsigned conv_blocks = (unsigned)((conv_tasks + PRO_WARPS - 1) / PRO_WARPS);
+  if (p.use_conv)
+    k_prologue_conv<T, NGK, true><<<conv_blocks, PRO_WARPS * 32, 0, st>>>(p);
+  else
+    k_prologue_conv<T, NGK, false><<<conv_blocks, PRO_WARPS * 32, 0, st>>>(p);
   int rc = check_cuda(cudaGetLastError(), "project activations (conv) launch");
   if (rc) return rc;
   k_prologue_gate<T><<<(unsigned)((gate_tasks + PRO_WARPS - 1) / PRO_WARPS), PRO_WARPS * 32, 0, st>>>(p);

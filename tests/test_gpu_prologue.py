@@ -90,3 +90,21 @@ def _run(case, dtype, seed):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_project_activations_matches_oracle(case, dtype):
     _run(case, dtype, seed=101 + CASES.index(case))
+
+
+def test_decay_softplus_accuracy():
+    """g = -exp(A_log) softplus(f + dt_bias) over f from -40 to 40 (both
+    branches of the kernel's softplus, the series for e^x < 1/8 and the
+    base-2 logarithm above, and the x > 20 cut) within 1e-5 relative of
+    numpy's log(1 + e^x)."""
+    import burn_gdn2 as bg
+
+    H, K = 1, 128
+    f = np.linspace(-40.0, 40.0, 64 * K).astype(np.float32).reshape(64, K)
+    dev = lambda a: torch.tensor(a, device=DEV)
+    raw = dev(np.zeros((64, K), np.float32))
+    (_, _, _, _, _, g), _ = bg.project_activations(
+        raw, raw, raw, raw, raw, dev(f), batch=1, num_heads=H, head_k_dim=K, num_v_heads=H, head_v_dim=K,
+        a_log=dev(np.zeros(H, np.float32)), dt_bias=dev(np.zeros(K, np.float32)))
+    want = -np.logaddexp(0.0, f.astype(np.float64))
+    assert_close(g.cpu().numpy(), want, rtol=1e-5, atol=1e-30, what="softplus")
