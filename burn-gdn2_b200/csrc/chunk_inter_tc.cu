@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     // v_new = U - W S  (rows 0..63 of D: sub-partitions 0, 1)
     if (sp < 2) {
       const int r = 32 * sp + lane;
-      const __nv_bfloat16* urow = reinterpret_cast<const __nv_bfloat16*>(stg + ST_U) + (size_t)r * V + col0;
+      const uint4* urow = reinterpret_cast<const uint4*>(stg + ST_U + (size_t)r * V * 2);  // chunks swizzled by r & 7
       for (int b32 = 0; b32 < HALF; b32 += 32) {
         float v[2][16];
         #pragma unroll
@@ -251,8 +251,8 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
         #pragma unroll
         for (int c16 = 0; c16 < 2; ++c16) {
           const int col = col0 + b32 + 16 * c16;
-          const uint4 u0 = reinterpret_cast<const uint4*>(urow + b32 + 16 * c16)[0];
-          const uint4 u1 = reinterpret_cast<const uint4*>(urow + b32 + 16 * c16)[1];
+          const uint4 u0 = urow[(col / 8) ^ (r & 7)];
+          const uint4 u1 = urow[(col / 8 + 1) ^ (r & 7)];
           const __nv_bfloat162* uh0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
           const __nv_bfloat162* uh1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
           float vn[16];

@@ -460,9 +460,10 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
         lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
         hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
         hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
-        uint4* dst = reinterpret_cast<uint4*>(rec + L.u + ((size_t)sl * 64 * p.vt + (size_t)r * p.vt + cc) * 2);
-        dst[0] = lo;
-        dst[1] = hi;
+        // 16-byte chunk j of a U row is stored at chunk j ^ (row & 7)
+        uint4* urow = reinterpret_cast<uint4*>(rec + L.u + ((size_t)sl * 64 * p.vt + (size_t)r * p.vt) * 2);
+        urow[(cc / 8) ^ (r & 7)] = lo;
+        urow[(cc / 8 + 1) ^ (r & 7)] = hi;
       }
     }
   }

@@ -9,7 +9,10 @@
 //                            rows 64..127 Qg = scale q gamma
 //   AQK [64][64]   K-major : scale * causal(q k^T decay)       (forward.rs:159-187)
 //   KD  [64][128]  MN-major: k exp(G_last - G)  (A operand of Kd^T v_new)
-//   U   [VS][64][VT] bf16 row-major per column slice: (I+Akk)^-1 (w v)
+//   U   [VS][64][VT] bf16 row-major per column slice: (I+Akk)^-1 (w v);
+//                            16-byte chunk j of row r sits at chunk j ^ (r & 7),
+//                            so the inter kernel's per-lane row reads are free
+//                            of shared-memory bank conflicts
 //   GL  [128] f32          : gamma_last = exp(G_last)
 #pragma once
 
