@@ -310,15 +310,17 @@ def run_ours(args):
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": args.dtype, "data": "synthetic (seeded, module value laws)",
-            "config": {"workload": "BASELINE config 2 chunked forward core: B=8 (per rank), T=4096, HV=16, "
+            "config": {"workload": f"BASELINE config 2 chunked forward core: B={B} (per rank), T=4096, HV=16, "
                                    "K=V=128, chunk 64, fused gated RMS-norm epilogue",
                        "global_batch": B * world, "seq_len": T, "parallelism": f"chains x{world} (no collective)",
-                       "l2": "inputs 1.2 GB/step > L2, no flush"},
+                       "l2": f"inputs {alg_bytes / 1e9:.2f} GB/step > 126 MB L2, no flush"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
             "roofline": {"bound": "hbm", "kernel": "chunk core (intra + inter + epilogue) per step",
                          "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic("chunk_core_bf16_cfg2"),
+                         "frac": achieved / peaks["hbm_gbs"],
+                         # per-step DRAM bytes of the B = 8 capture, scaled by the batch (traffic is linear in B)
+                         "traffic": (lambda t: None if t is None else t * B / 8)(ncu_traffic("chunk_core_bf16_cfg2")),
                          "peak_src": peaks["src"], "alg_bytes_per_step": alg_bytes,
                          "tc_frac": flops / (core_ms / 1e3) / (peaks["bf16_tflops"] * 1e12)},
             "kernels_ms": {"chunk_intra": intra_ms, "chunk_inter_plus_epilogue": inter_ms, "dominant": dom_name},
@@ -375,7 +377,7 @@ def run_layer(torch, bg, dev, stream, args, max_over_ranks, world):
     peaks = load_peaks()
     flops = proj_flops + core_flops
     return {"value": tokens * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
-            "workload": "GatedDeltaNet2.forward_train, BASELINE config 2 (D=2048, 16x128 heads, B=8, T=4096, bf16)",
+            "workload": f"GatedDeltaNet2.forward_train, BASELINE config 2 (D=2048, 16x128 heads, B={c['B']}, T=4096, bf16)",
             "tflops": flops / (ms / 1e3) / 1e12, "tc_frac": flops / (ms / 1e3) / (peaks["bf16_tflops"] * 1e12),
             "flops_per_step": flops}
 
@@ -566,7 +568,11 @@ def main():
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--core-only", action="store_true", help="skip the layer and f32 side measurements")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="batch of config 2 (default 8, the BASELINE value); smaller for profiling captures")
     args = ap.parse_args()
+    if args.batch:
+        CFG2["B"] = args.batch
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         res = run_reference(args)
