@@ -202,12 +202,24 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     }
   }
   {
-    unsigned char* xt = sm + X + tp * 8192;
+    // Every store of row r0 + i lands at (lane base of its tile) + i * 128 + ((cx ^ i) << 4): rows r0 .. r0 + 7
+    // form one 8-row group of every 128-byte-swizzled tile (r0 is a multiple of 8), and the lane's channel
+    // group fixes the rest.
+    const int cx = (ch & 63) >> 3, kb = ch >> 6, eb = (ch & 7) * 2, rg = r0 >> 3;
+    unsigned char* const xq = sm + X + tp * 8192 + kb * 32 * 128 + hh * 1024 + eb;
+    unsigned char* const xb = sm + X + tp * 8192 + kb * 32 * 128 + (2 + hh) * 1024 + eb;
+    unsigned char* const wqr = rec + L.wq + kb * 128 * 128 + (8 + rg) * 1024 + eb;
+    unsigned char* const kdr = rec + L.kd + kb * 64 * 128 + rg * 1024 + eb;
+    unsigned char* const rkr = sm + RK + kb * 64 * 128 + rg * 1024 + eb;
+    unsigned char* const rvr = sm + RV + kb * 64 * 128 + rg * 1024 + eb;
+    unsigned char* ksr[4];
+    #pragma unroll
+    for (int pp = 0; pp < 4; ++pp) ksr[pp] = sm + KSV + 4096 * (pp * (pp + 1) / 2) + kb * 16 * (pp + 1) * 128 + rg * 1024 + eb;
     float gl[4] = {off[0], off[1], off[2], off[3]};  // tile-local cumsum of g at row r
     // row i + 1 is loaded while row i is computed and stored
     #pragma unroll 2
     for (int i = 0; i < 8; ++i) {
-      const int r = r0 + i, ti = hh * 8 + i;
+      const int r = r0 + i;
       const uint2 cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw;
       if (r < cv) {
         gl[0] += ng.x; gl[1] += ng.y; gl[2] += ng.z; gl[3] += ng.w;
@@ -231,19 +243,17 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
         kinv[j] = k[j] * ei;
         kd[j] = kinv[j] * edk[j];
       }
-      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(ti, ch, 32)) = pack4(qs[0], qs[1], qs[2], qs[3]);
-      *reinterpret_cast<uint2*>(xt + umma::kmaj_off(16 + ti, ch, 32)) = pack4(bks[0], bks[1], bks[2], bks[3]);
-      *reinterpret_cast<uint2*>(rec + L.wq + umma::kmaj_off(64 + r, ch, 128)) = pack4(qg[0], qg[1], qg[2], qg[3]);
-      *reinterpret_cast<uint2*>(rec + L.kd + umma::mnmaj_off(r, ch, 64)) = pack4(kd[0], kd[1], kd[2], kd[3]);
-      *reinterpret_cast<uint2*>(sm + RK + umma::mnmaj_off(r, ch, 64)) = pack4(rk[0], rk[1], rk[2], rk[3]);
-      if (ch < V)
-        *reinterpret_cast<uint2*>(sm + RV + umma::mnmaj_off(r, ch, 64)) =
-            pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
+      const uint32_t ro = i * 128 + ((cx ^ i) << 4);
+      *reinterpret_cast<uint2*>(xq + ro) = pack4(qs[0], qs[1], qs[2], qs[3]);
+      *reinterpret_cast<uint2*>(xb + ro) = pack4(bks[0], bks[1], bks[2], bks[3]);
+      *reinterpret_cast<uint2*>(wqr + ro) = pack4(qg[0], qg[1], qg[2], qg[3]);
+      *reinterpret_cast<uint2*>(kdr + ro) = pack4(kd[0], kd[1], kd[2], kd[3]);
+      *reinterpret_cast<uint2*>(rkr + ro) = pack4(rk[0], rk[1], rk[2], rk[3]);
+      if (ch < V) *reinterpret_cast<uint2*>(rvr + ro) = pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
       #pragma unroll
       for (int pp = 0; pp < 4; ++pp) {
         if (pp < tp) continue;
-        unsigned char* kt = sm + KSV + 4096 * (pp * (pp + 1) / 2);
-        *reinterpret_cast<uint2*>(kt + umma::kmaj_off(r, ch, 16 * (pp + 1))) =
+        *reinterpret_cast<uint2*>(ksr[pp] + ro) =
             pack4(kinv[0] * cks[pp][0], kinv[1] * cks[pp][1], kinv[2] * cks[pp][2], kinv[3] * cks[pp][3]);
       }
     }
