@@ -1,4 +1,4 @@
-"""CPU, world_size 2 over gloo: head sharding of one layer.  Each rank runs
+"""CPU, world_size 2 and 4 over gloo: head sharding of one layer.  Each rank runs
 the oracle layer on its shard of the weights; the all-reduce (sum) of the
 row-parallel o_proj partials must equal the unsharded layer (forward_train
 and a stateful forward), including GVA groups."""
@@ -50,16 +50,17 @@ def _worker(rank, world, port, cfgd, seed, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfgd", [
-    dict(hidden_size=64, num_heads=4, head_dim=16, mode="chunk"),
-    dict(hidden_size=64, num_heads=2, head_dim=16, num_v_heads=4, expand_v=2.0, mode="chunk", min_decay=0.9,
-         allow_neg_eigval=True),
+@pytest.mark.parametrize("cfgd,world", [
+    (dict(hidden_size=64, num_heads=4, head_dim=16, mode="chunk"), 2),
+    (dict(hidden_size=64, num_heads=2, head_dim=16, num_v_heads=4, expand_v=2.0, mode="chunk", min_decay=0.9,
+          allow_neg_eigval=True), 2),
+    (dict(hidden_size=64, num_heads=4, head_dim=16, mode="chunk"), 4),
 ])
-def test_head_sharded_layer_matches_unsharded(cfgd):
+def test_head_sharded_layer_matches_unsharded(cfgd, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, cfgd, 3, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfgd, 3, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
