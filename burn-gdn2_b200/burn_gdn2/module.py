@@ -21,16 +21,15 @@ from __future__ import annotations
 import ctypes
 import dataclasses
 import math
-from typing import Optional, Tuple
+from typing import Optional
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from ._lib import LIB, check
 from .config import Gdn2Config, Gdn2Mode
 from .ops import (SHORT_CONV_CACHE, chunk_args, chunk_workspace, project_activations, recurrent_args,
-                  rms_norm_gate_per_head, stream_handle, view4)
+                  rms_norm_gate_per_head, stream_handle)
 
 FUSED_RECURRENT_MAX_SEQ = 64  # src/module.rs:17
 
@@ -161,24 +160,6 @@ class GatedDeltaNet2:
         if not x.is_cuda:
             raise RuntimeError("GatedDeltaNet2 runs on the B200 CUDA kernels only; got a CPU tensor")
 
-    def _gates(self, x):
-        """g (f32 log decay, [B,T,KD]), b, w (sigmoid, b*2 if neg-eig), gate
-        (src/module.rs:417-443, :470-476)."""
-        c = self.config
-        h, hk, hv, vh = self._dims
-        f_out = self.f_proj_1.forward(self.f_proj_0.forward(x)).float()
-        a_exp = torch.exp(self.a_log).repeat_interleave(hk)
-        g = -a_exp * F.softplus(f_out + self.dt_bias)
-        if self.decay_factors is not None:
-            factor = torch.sigmoid(self.decay_factors).reshape(-1) * (1.0 - c.min_decay)
-            g = torch.log(factor * torch.exp(g) + c.min_decay)
-        b = torch.sigmoid(self.b_proj.forward(x))
-        if c.allow_neg_eigval:
-            b = b * 2.0
-        w = torch.sigmoid(self.w_proj.forward(x))
-        gate = self.g_proj_1.forward(self.g_proj_0.forward(x))
-        return g.contiguous(), b, w, gate
-
     # -- src/module.rs:381-498 ----------------------------------------------
     def _proj_weight(self):
         """[D, 3*KD + 2*VD + 2*vh] concatenation of the q, k, v, b, w,
@@ -190,6 +171,21 @@ class GatedDeltaNet2:
             self._wcat = torch.cat([l.weight for l in parts], dim=1).contiguous()
             self._wcat_key = key
         return self._wcat
+
+    def _projections(self, x):
+        """The layer's GEMMs before the core: one GEMM of x against the
+        concatenated q, k, v, b, w, f_proj_0 and g_proj_0 weights, then the
+        f_proj_1 / g_proj_1 up-projections.  Returns the raw [B*T, C] column
+        slices (q, k, v, b, w, f) of that output and the gate [B*T, VD]."""
+        h, hk, hv, vh = self._dims
+        B, T, _ = x.shape
+        kd, vd = h * hk, hv * vh
+        y = x.to(self.dtype).reshape(B * T, -1) @ self._proj_weight()
+        o = [0, kd, 2 * kd, 2 * kd + vd, 3 * kd + vd, 3 * kd + 2 * vd, 3 * kd + 2 * vd + vh]
+        cols = lambda i, n: y[:, o[i]:o[i] + n]
+        f_raw = cols(5, vh) @ self.f_proj_1.weight
+        gate = torch.addmm(self.g_proj_1.bias, cols(6, vh), self.g_proj_1.weight)
+        return (cols(0, kd), cols(1, kd), cols(2, vd), cols(3, kd), cols(4, vd), f_raw), gate
 
     def project(self, x, conv_cache=None, grouped=None):
         """Projection pipeline.  Returns (ProjectedInputs, conv_out or None).
@@ -203,16 +199,11 @@ class GatedDeltaNet2:
         h, hk, hv, vh = self._dims
         B, T, _ = x.shape
         kd, vd = h * hk, hv * vh
-        x2 = x.to(self.dtype).reshape(B * T, -1)
         grouped = (self.gva_mode == "grouped") if grouped is None else grouped
-        y = x2 @ self._proj_weight()
-        o = [0, kd, 2 * kd, 2 * kd + vd, 3 * kd + vd, 3 * kd + 2 * vd, 3 * kd + 2 * vd + vh]
-        cols = lambda i, n: y[:, o[i]:o[i] + n]
-        f_raw = cols(5, vh) @ self.f_proj_1.weight
-        gate = torch.addmm(self.g_proj_1.bias, cols(6, vh), self.g_proj_1.weight)
+        raws, gate = self._projections(x)
         conv_w = (self.q_conv_w, self.k_conv_w, self.v_conv_w) if c.use_short_conv else None
         (q, k, v, b, w, g), conv_out = project_activations(
-            cols(0, kd), cols(1, kd), cols(2, vd), cols(3, kd), cols(4, vd), f_raw, batch=B, num_heads=h,
+            *raws, batch=B, num_heads=h,
             head_k_dim=hk, num_v_heads=hv, head_v_dim=vh, a_log=self.a_log, dt_bias=self.dt_bias, conv_w=conv_w,
             conv_in=conv_cache if c.use_short_conv else None, allow_neg_eigval=c.allow_neg_eigval,
             min_decay=c.min_decay, decay_factors=self.decay_factors)
@@ -250,9 +241,13 @@ class GatedDeltaNet2:
         c = self.config
         h, hk, hv, vh = self._dims
         B, T, _ = x.shape
-        x = x.to(self.dtype)
-        q_raw, k_raw, v_raw = self.q_proj.forward(x), self.k_proj.forward(x), self.v_proj.forward(x)
-        g, b, w, gate = self._gates(x)
+        raws, gate = self._projections(x)
+        q_raw, k_raw, v_raw = raws[:3]  # convolved in the recurrent kernel's own prologue
+        # b, w, g from the activations pass (its q/k/v outputs, SiLU only, are not used here)
+        (_, _, _, b, w, g), _ = project_activations(
+            *raws, batch=B, num_heads=h, head_k_dim=hk, num_v_heads=hv, head_v_dim=vh, a_log=self.a_log,
+            dt_bias=self.dt_bias, conv_w=None, allow_neg_eigval=c.allow_neg_eigval, min_decay=c.min_decay,
+            decay_factors=self.decay_factors)
         to4 = lambda t, n, d: t.reshape(B, T, n, d).permute(0, 2, 1, 3)
         kd, vd = h * hk, hv * vh
         if c.use_short_conv:

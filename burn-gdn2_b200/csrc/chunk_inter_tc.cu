@@ -141,16 +141,11 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     const int t0 = c * TC_C;
     const int cv = min(TC_C, p.T - t0);
     const uint32_t tD = tD0 + (c & 1) * V;
-    float ov[64];
+    float ov[64];  // TMEM loads land straight in ov: registers are valid only after the wait
     #pragma unroll
-    for (int c16 = 0; c16 < 4; ++c16) {
-      float v[16];
-      if (16 * c16 < HALF) {
-        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), v);
-        #pragma unroll
-        for (int j = 0; j < 16; ++j) ov[16 * c16 + j] = v[j];
-      }
-    }
+    for (int c16 = 0; c16 < 4; ++c16)
+      if (16 * c16 < HALF)
+        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), *reinterpret_cast<float(*)[16]>(ov + 16 * c16));
     umma::wait_ld();
     float s4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
     #pragma unroll
