@@ -25,7 +25,7 @@ constexpr int SIMT_THREADS = 256;
 // chunk-intra: one CTA per (chunk, hv, b)
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(SIMT_THREADS) k_intra_simt(const ChunkParams p) {
+__global__ void __launch_bounds__(SIMT_THREADS, 2) k_intra_simt(const ChunkParams p) {
   extern __shared__ float sm[];
   float* sQs = sm;                  // [KS][CP]  q E
   float* sKx = sQs + KS * CP;       // [KS][CP]  k / E
@@ -377,9 +377,14 @@ static int launch_inter_vt(const ChunkParams& p, cudaStream_t st) {
   return check_cuda(cudaGetLastError(), "chunk inter launch");
 }
 
+// Column slice per CTA.  Every CTA walks the whole chunk chain of its (b, hv),
+// so the grid must fit in one wave: 64-column slices (256 CTAs for 128
+// chains of V = 128, two per SM) beat 32-column ones (512 CTAs, more than
+// the 444 that fit) and read each chain's W / Qg / Kd / Aqk half as often.
 int launch_inter_simt(const ChunkParams& p, cudaStream_t st) {
   if (p.V <= 16) return launch_inter_vt<16>(p, st);
   if (p.V <= 64 && p.V % 32 != 0) return launch_inter_vt<16>(p, st);
+  if (p.V % 64 == 0) return launch_inter_vt<64>(p, st);
   return launch_inter_vt<32>(p, st);
 }
 
