@@ -208,6 +208,22 @@ __global__ void __launch_bounds__(SIMT_THREADS) k_inter_simt(const ChunkParams p
     const float* gKd = p.ws_kd + n * CP * K;
     const float* gGl = p.ws_gl + n * K;
 
+    // the next chunk's blocks on their way to L2 while this one computes: the
+    // plain loads below sit between barriers, on the chain's critical path
+    if (c + 1 < p.NC) {
+      const int64_t n1 = n + 1;
+      const int lw = CP * K * 4 / 128, la = CP * CP * 4 / 128, lu = CP * V * 4 / 128;
+      for (int l = tid; l < 3 * lw + la + lu; l += SIMT_THREADS) {
+        const char* a;
+        if (l < lw) a = reinterpret_cast<const char*>(p.ws_w + n1 * CP * K) + 128 * l;
+        else if (l < 2 * lw) a = reinterpret_cast<const char*>(p.ws_qg + n1 * CP * K) + 128 * (l - lw);
+        else if (l < 3 * lw) a = reinterpret_cast<const char*>(p.ws_kd + n1 * CP * K) + 128 * (l - 2 * lw);
+        else if (l < 3 * lw + la) a = reinterpret_cast<const char*>(p.ws_aqk + n1 * CP * CP) + 128 * (l - 3 * lw);
+        else a = reinterpret_cast<const char*>(p.ws_u + n1 * CP * V) + 128 * (l - 3 * lw - la);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+      }
+    }
+
     for (int idx = tid; idx < CP * CP; idx += SIMT_THREADS) sAq[(idx / CP) * (CP + 1) + idx % CP] = gAqk[idx];
 
     float avn[RT][4], ao[RT][4];
