@@ -451,10 +451,23 @@ def run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    # the same step as its two C-ABI phases, for the per-kernel split
+    wsp = ctypes.c_void_p(ws.data_ptr())
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+    for ea, eb, ec in ev:
+        state.zero_()
+        ea.record(stream)
+        bg._lib.check(bg.LIB.gdn2_chunk_intra(ctypes.byref(a), wsp, ws.numel(), sh))
+        eb.record(stream)
+        bg._lib.check(bg.LIB.gdn2_chunk_inter(ctypes.byref(a), wsp, ws.numel(), sh))
+        ec.record(stream)
+    torch.cuda.synchronize()
+    split = {"chunk_intra": sum(ea.elapsed_time(eb) for ea, eb, _ in ev) / n,
+             "chunk_inter_plus_epilogue": sum(eb.elapsed_time(ec) for _, eb, ec in ev) / n}
     del ws
     alg = core_bytes_per_token_head(K, V, 4) * B * T * HV
     peaks = load_peaks()
-    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "kernels_ms": split,
             "workload": "BASELINE config 2 chunked forward core in f32 (CUDA-core path, exact f32)",
             "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
