@@ -359,6 +359,47 @@ __device__ __forceinline__ void dec_load_v(const RecParams& p, int bb, int hv, D
   }
 }
 
+// Block sums with one barrier: each warp's partial goes to red, then every
+// thread adds the NT / 32 partials itself.  The caller must pass another
+// barrier before red is written again.
+template <int NT>
+__device__ __forceinline__ void block_sum3_1bar(float& a, float& b, float& c, float* red) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+    c += __shfl_xor_sync(0xffffffffu, c, o);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NW = NT / 32;
+  if (lane == 0) {
+    red[warp] = a;
+    red[NW + warp] = b;
+    red[2 * NW + warp] = c;
+  }
+  __syncthreads();
+  a = b = c = 0.f;
+  #pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    a += red[w];
+    b += red[NW + w];
+    c += red[2 * NW + w];
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum_1bar(float x, float* red) {
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = x;
+  __syncthreads();
+  float s = 0.f;
+  #pragma unroll
+  for (int w = 0; w < NT / 32; ++w) s += red[w];
+  return s;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(DEC_THREADS) k_decode(const RecParams p) {
   extern __shared__ __align__(128) unsigned char smraw[];
@@ -429,12 +470,15 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const RecParams p) {
     }
     const float gv = r.g, bv = r.b;
     if (next_item < n_items) dec_load_qk<T>(p, next_item, r);  // prefetch, lands during this item
+    // |q|^2, |k|^2 and q.k in one reduction; (q / |q|).(k / |k|) = q.k / (|q| |k|)
+    float sqq = qv * qv, skk = kv * kv, sqk = qv * kv;
+    block_sum3_1bar<DEC_THREADS>(sqq, skk, sqk, misc);
     float nq = 1.f, nk = 1.f;
     if (p.prologue != 0) {
-      nq = sqrtf(block_sum<DEC_THREADS>(qv * qv, misc) + 1e-6f);
-      nk = sqrtf(block_sum<DEC_THREADS>(kv * kv, misc) + 1e-6f);
+      nq = sqrtf(sqq + 1e-6f);
+      nk = sqrtf(skk + 1e-6f);
     }
-    float pqk = 0.f;
+    const float qk = sqk / (nq * nk);
     if (tid < K) {
       qv /= nq;
       kv /= nk;
@@ -443,9 +487,8 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const RecParams p) {
       seg[tid] = e;
       sbk[tid] = bv * kv * e;
       sqg[tid] = qv * e;
-      pqk = qv * kv;
     }
-    const float qk = block_sum<DEC_THREADS>(pqk, misc);  // publishes sk/seg/sbk/sqg
+    __syncthreads();  // publishes sk/seg/sbk/sqg; misc reusable
 
     for (int j = 0; j < p.rep; ++j) {
       const int hv = kh * p.rep + j;
@@ -536,7 +579,8 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const RecParams p) {
       __syncthreads();  // so[] complete
       float ss = 0.f;
       for (int c = tid; c < V; c += DEC_THREADS) ss += so[c] * so[c];
-      const float rms = p.fuse_epilogue ? sqrtf(block_sum<DEC_THREADS>(ss, misc) / (float)V + p.eps) : 1.f;
+      // misc is free: the barrier after the previous reduction's readers ("so[] complete") has passed
+      const float rms = p.fuse_epilogue ? sqrtf(block_sum_1bar<DEC_THREADS>(ss, misc) / (float)V + p.eps) : 1.f;
       #pragma unroll
       for (int u = 0; u < DEC_VCH; ++u) {
         const int c = tid + u * DEC_THREADS;
