@@ -14,6 +14,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace gdn2 {
 
@@ -38,6 +39,7 @@ struct ProParams {
   void *q, *k, *v, *b, *w;
   float* g;
   int ntb;  // token blocks per sequence
+  int tb0;  // first token block this launch covers (the generic kernels take the blocks the wide one does not)
 };
 
 // 4 consecutive elements of a row
@@ -312,10 +314,11 @@ __global__ void __launch_bounds__(PRO_WARPS * 32, 2) k_prologue_conv(const ProPa
   const int KD = p.H * p.K, VD = p.HV * p.V;
   const int SV = (VD + 127) / 128;
   const int per = 2 * p.H + SV;
-  if (task >= (int64_t)p.B * p.ntb * per) return;
+  const int nblk = p.ntb - p.tb0;
+  if (task >= (int64_t)p.B * nblk * per) return;
   int u = (int)(task % per);
   const int64_t bt = task / per;
-  const int tb = (int)(bt % p.ntb), bb = (int)(bt / p.ntb);
+  const int tb = p.tb0 + (int)(bt % nblk), bb = (int)(bt / nblk);
   const int t0 = tb * PRO_ROWS, t1 = min(p.T, t0 + PRO_ROWS);
   if (u < 2 * p.H) {  // q or k of one key head
     const bool isk = u >= p.H;
@@ -349,10 +352,11 @@ __global__ void __launch_bounds__(PRO_WARPS * 32, 4) k_prologue_gate(const ProPa
   const int KD = p.H * p.K, VD = p.HV * p.V;
   const int SK = (KD + 127) / 128, SV = (VD + 127) / 128;
   const int per = 2 * SK + SV;
-  if (task >= (int64_t)p.B * p.ntb * per) return;
+  const int nblk = p.ntb - p.tb0;
+  if (task >= (int64_t)p.B * nblk * per) return;
   int u = (int)(task % per);
   const int64_t bt = task / per;
-  const int tb = (int)(bt % p.ntb), bb = (int)(bt / p.ntb);
+  const int tb = p.tb0 + (int)(bt % nblk), bb = (int)(bt / nblk);
   const int t0 = tb * PRO_ROWS, t1 = min(p.T, t0 + PRO_ROWS);
   if (u < SK) {
     const int cc = 128 * u + 4 * lane;
@@ -370,12 +374,350 @@ __global__ void __launch_bounds__(PRO_WARPS * 32, 4) k_prologue_gate(const ProPa
   gate_task<T, 5>(p, static_cast<const T*>(p.fr), p.ldf, KD, p.g, bb, t0, t1, cc < KD ? cc : 0, cc < KD);
 }
 
+// ---------------------------------------------------------------------------
+// Wide path: full PRO_ROWS token blocks, every stream a whole number of
+// 256-channel slices, K a power of two in [32, 256], rows 16-byte aligned.
+// One warp per (batch, token block, stream, 256-channel slice); lane l owns
+// channels 8l..8l+7, so a token's slice is one 512-byte (bf16) access per
+// warp and the per-row overheads (addresses, loop, reductions) are shared by
+// 8 channels.  Conv and gate streams share one persistent launch.  Each lane
+// copies its own 16-byte pieces of the next WIDE_DEPTH - 1 rows into a private
+// shared-memory ring with cp.async and reads them back itself, so no barrier
+// is needed and the bytes in flight hold no registers.  The q/k L2 norm
+// reduces four rows at once over the K/8 lanes of a head: two exchange steps
+// leave every lane with a partial sum of one of the four rows
+// (reduce-scatter), the remaining steps complete it, one rsqrt per lane, and
+// four shuffles hand each lane the four factors.
+
+constexpr int WIDE_DEPTH = 8;  // ring slots per lane: rows in flight + the row being read
+constexpr int WIDE_WARPS = 8;
+
+__device__ __forceinline__ void cp16(uint32_t sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sdst), "l"(gsrc) : "memory");
+}
+
+__device__ __forceinline__ void unpack2(uint32_t u, float& lo, float& hi) {
+  lo = __uint_as_float(u << 16);
+  hi = __uint_as_float(u & 0xffff0000u);
+}
+
+// A lane's 8 consecutive elements of one row: ring copies (16-byte pieces,
+// piece i of all 32 lanes adjacent so the read-back is conflict-free), direct
+// non-coherent loads (conv halo) and stores.
+template <typename T>
+struct Wide;
+template <>
+struct Wide<__nv_bfloat16> {
+  static constexpr int PIECES = 1;
+  static __device__ __forceinline__ void fetch(uint32_t s, const __nv_bfloat16* g) { cp16(s, g); }
+  static __device__ __forceinline__ void read(const unsigned char* s, float (&x)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(s);
+    unpack2(u.x, x[0], x[1]);
+    unpack2(u.y, x[2], x[3]);
+    unpack2(u.z, x[4], x[5]);
+    unpack2(u.w, x[6], x[7]);
+  }
+  static __device__ __forceinline__ void ldg(const __nv_bfloat16* g, float (&x)[8]) {
+    uint4 u;
+    asm("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w) : "l"(g));
+    unpack2(u.x, x[0], x[1]);
+    unpack2(u.y, x[2], x[3]);
+    unpack2(u.z, x[4], x[5]);
+    unpack2(u.w, x[6], x[7]);
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* g, const float (&y)[8]) {
+    __nv_bfloat162 h[4];
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+    *reinterpret_cast<uint4*>(g) = *reinterpret_cast<const uint4*>(h);
+  }
+};
+template <>
+struct Wide<float> {
+  static constexpr int PIECES = 2;
+  static __device__ __forceinline__ void fetch(uint32_t s, const float* g) {
+    cp16(s, g);
+    cp16(s + 512, g + 4);
+  }
+  static __device__ __forceinline__ void read(const unsigned char* s, float (&x)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(s);
+    const float4 b = *reinterpret_cast<const float4*>(s + 512);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  }
+  static __device__ __forceinline__ void ldg(const float* g, float (&x)[8]) {
+    Raw4<float> a = ld_raw4(g), b = ld_raw4(g + 4);
+    x[0] = a.r.x; x[1] = a.r.y; x[2] = a.r.z; x[3] = a.r.w;
+    x[4] = b.r.x; x[5] = b.r.y; x[6] = b.r.z; x[7] = b.r.w;
+  }
+  static __device__ __forceinline__ void store(float* g, const float (&y)[8]) {
+    reinterpret_cast<float4*>(g)[0] = make_float4(y[0], y[1], y[2], y[3]);
+    reinterpret_cast<float4*>(g)[1] = make_float4(y[4], y[5], y[6], y[7]);
+  }
+};
+
+__device__ __forceinline__ void store8_f32(float* g, const float (&y)[8]) { Wide<float>::store(g, y); }
+
+// The ring of one lane: slot s starts at sring + s * SLOT (shared-window
+// address for cp.async) and at rring + s * SLOT (generic pointer for reads).
+template <typename T>
+struct Ring {
+  static constexpr int SLOT = Wide<T>::PIECES * 512;
+  uint32_t s;
+  const unsigned char* r;
+};
+
+// Starts the ring on rows src, src + ld, ... (WIDE_DEPTH - 1 of them, row i
+// in slot i) and returns the pointer of the next row to fetch.
+template <typename T>
+__device__ __forceinline__ const T* ring_start(const Ring<T>& rg, const T* src, int64_t ld) {
+  #pragma unroll
+  for (int r = 0; r < WIDE_DEPTH - 1; ++r) {
+    Wide<T>::fetch(rg.s + r * Ring<T>::SLOT, src);
+    cp_async_commit();
+    src += ld;
+  }
+  return src;
+}
+
+// Row t of the block (slot t % WIDE_DEPTH): first refills the slot of row
+// t - 1 with row t + WIDE_DEPTH - 1 (an empty group past the block, so the
+// wait count stays uniform), then waits for row t and reads it.
+template <typename T>
+__device__ __forceinline__ void ring_next(const Ring<T>& rg, int t, const T*& fp, int64_t ld, float (&x)[8]) {
+  if (t + WIDE_DEPTH - 1 < PRO_ROWS) {
+    Wide<T>::fetch(rg.s + ((t + WIDE_DEPTH - 1) % WIDE_DEPTH) * Ring<T>::SLOT, fp);
+    fp += ld;
+  }
+  cp_async_commit();
+  cp_async_wait<WIDE_DEPTH - 1>();
+  Wide<T>::read(rg.r + (t % WIDE_DEPTH) * Ring<T>::SLOT, x);
+}
+
+// conv4 + SiLU of channels c..c+7 over tokens [t0, t0 + PRO_ROWS), with the
+// per-head L2 norm when lph (lanes per head, K / 8) is nonzero (q, k).  One
+// loop body serves all three streams and handles four rows, the L2 group;
+// the ring slots are runtime indices, so the body stays small enough for
+// the instruction cache next to the gate bodies.
+template <typename T, bool CONV>
+__device__ __forceinline__ void wide_conv(const ProParams& p, const Ring<T>& rg, const T* raw, int64_t ld, int C,
+                                          const float* taps, const float* cin, float* cout, T* out, int bb, int t0,
+                                          int c, int lane, int lph) {
+  const T* src = raw + ((int64_t)bb * p.T + t0) * ld + c;
+  const T* fp = ring_start<T>(rg, src, ld);
+  float w[8][4], h[3][8];
+  if (CONV) {
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 tp = *reinterpret_cast<const float4*>(taps + (int64_t)(c + j) * 4);
+      w[j][0] = tp.x; w[j][1] = tp.y; w[j][2] = tp.z; w[j][3] = tp.w;
+    }
+    if (t0 > 0) {
+      #pragma unroll
+      for (int i = 0; i < 3; ++i) Wide<T>::ldg(src + (int64_t)(i - 3) * ld, h[i]);
+    } else if (cin) {
+      #pragma unroll
+      for (int i = 0; i < 3; ++i) Wide<float>::ldg(cin + ((int64_t)bb * 3 + i) * C + c, h[i]);
+    } else {
+      Wide<T>::ldg(src, h[0]);
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) h[1][j] = h[2][j] = h[0][j];
+    }
+  }
+  // L2 lane pattern (uniform per task): after the exchanges at o1 and o2 the
+  // lane holds row (hi1 ? 2 : 0) + (hi2 ? 1 : 0) of the group; row r's sum
+  // ends on lane hb + (r & 2 ? o1 : 0) + (r & 1 ? o2 : 0).
+  const int o1 = lph >> 1, o2 = lph >> 2;
+  const bool hi1 = (lane & o1) != 0, hi2 = (lane & o2) != 0;
+  const int hb = lane & ~(lph - 1);
+  T* dp = out + ((int64_t)bb * p.T + t0) * C + c;
+  #pragma unroll 1
+  for (int t4 = 0; t4 < PRO_ROWS; t4 += 4) {
+    float y[4][8], ss[4];
+    #pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float x[8];
+      ring_next<T>(rg, t4 + r, fp, ld, x);
+      ss[r] = 0.f;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float s = CONV ? (w[j][0] * h[0][j] + w[j][1] * h[1][j] + w[j][2] * h[2][j] + w[j][3] * x[j]) : x[j];
+        y[r][j] = silu_fast(s);
+        ss[r] += y[r][j] * y[r][j];
+        if (CONV) {
+          h[0][j] = h[1][j];
+          h[1][j] = h[2][j];
+          h[2][j] = x[j];
+        }
+      }
+    }
+    if (lph) {
+      float a0 = hi1 ? ss[2] : ss[0], a1 = hi1 ? ss[3] : ss[1];
+      const float s0 = hi1 ? ss[0] : ss[2], s1 = hi1 ? ss[1] : ss[3];
+      a0 += __shfl_xor_sync(0xffffffffu, s0, o1);
+      a1 += __shfl_xor_sync(0xffffffffu, s1, o1);
+      float kp = hi2 ? a1 : a0;
+      kp += __shfl_xor_sync(0xffffffffu, hi2 ? a0 : a1, o2);
+      for (int o = lph >> 3; o > 0; o >>= 1) kp += __shfl_xor_sync(0xffffffffu, kp, o);
+      const float iv = rsqrtf(kp + 1e-6f);
+      #pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float f = __shfl_sync(0xffffffffu, iv, hb + ((r & 2) ? o1 : 0) + ((r & 1) ? o2 : 0));
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) y[r][j] *= f;
+      }
+    }
+    #pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      Wide<T>::store(dp, y[r]);
+      dp += C;
+    }
+  }
+  if (CONV && cout && t0 + PRO_ROWS == p.T) {
+    #pragma unroll
+    for (int i = 0; i < 3; ++i) store8_f32(cout + ((int64_t)bb * 3 + i) * C + c, h[i]);
+  }
+}
+
+// Gate stream of channels c..c+7 over tokens [t0, t0 + PRO_ROWS), the same
+// formulas as gate_task: G = false: sigmoid x sc (b with sc = 2 under
+// neg-eig, w with sc = 1), out T; G = true: the decay g, out f32.
+template <typename T, bool G>
+__device__ __forceinline__ void wide_gate(const ProParams& p, const Ring<T>& rg, const T* raw, int64_t ld, int C,
+                                          void* out, int bb, int t0, int c, float sc) {
+  const T* src = raw + ((int64_t)bb * p.T + t0) * ld + c;
+  const T* fp = ring_start<T>(rg, src, ld);
+  float dtb[8], fac[8], a = 0.f;
+  const bool remap = p.min_decay >= 0.f;
+  if (G) {
+    a = expf(p.a_log[c / p.K]);  // the 8 channels lie in one head (K % 8 == 0)
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      dtb[j] = p.dt_bias[c + j];
+      fac[j] = 0.f;
+      if (remap) fac[j] = sigmoid_f(p.decay[c + j]) * (1.0f - p.min_decay);  // decay may be null otherwise
+    }
+  }
+  const int64_t o0 = ((int64_t)bb * p.T + t0) * C + c;
+  #pragma unroll 2
+  for (int t = 0; t < PRO_ROWS; ++t) {
+    float x[8], o[8];
+    ring_next<T>(rg, t, fp, ld, x);
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (G) {
+        float gv = -a * softplus_f(x[j] + dtb[j]);
+        if (remap) gv = logf(fac[j] * expf(gv) + p.min_decay);
+        o[j] = gv;
+      } else {
+        o[j] = sigmoid_f(x[j]) * sc;
+      }
+    }
+    if (G)
+      store8_f32(static_cast<float*>(out) + o0 + (int64_t)t * C, o);
+    else
+      Wide<T>::store(static_cast<T*>(out) + o0 + (int64_t)t * C, o);
+  }
+}
+
+// Persistent: warps take (batch, full token block, stream slice) tasks in
+// order of task id, the slices of one (batch, block) adjacent: q and k
+// (KD / 256 each, L2-normalised), v (VD / 256), b (KD / 256), w (VD / 256),
+// g (KD / 256).
+template <typename T, bool CONV>
+__global__ void __launch_bounds__(WIDE_WARPS * 32, 2) k_prologue_wide(const ProParams p, int nfull, int64_t ntask) {
+  extern __shared__ __align__(16) unsigned char wring[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int off = (warp * WIDE_DEPTH * Wide<T>::PIECES * 32 + lane) * 16;
+  Ring<T> rg;
+  rg.s = smem_u32(wring) + off;
+  rg.r = wring + off;
+  const int KD = p.H * p.K, VD = p.HV * p.V, NQ = KD / 256, NV = VD / 256;
+  const int per = 4 * NQ + 2 * NV;
+  const int64_t nw = (int64_t)gridDim.x * WIDE_WARPS;
+  for (int64_t task = (int64_t)blockIdx.x * WIDE_WARPS + warp; task < ntask; task += nw) {
+    int u = (int)(task % per);
+    const int64_t bt = task / per;
+    const int t0 = (int)(bt % nfull) * PRO_ROWS, bb = (int)(bt / nfull);
+    if (u < 2 * NQ + NV) {  // q, k, v
+      const int s = u < NQ ? 0 : u < 2 * NQ ? 1 : 2;
+      const int c = 256 * (u - s * NQ) + 8 * lane;
+      const T* raw = static_cast<const T*>(s == 0 ? p.qr : s == 1 ? p.kr : p.vr);
+      const int64_t ld = s == 0 ? p.ldq : s == 1 ? p.ldk : p.ldv;
+      const float* taps = s == 0 ? p.cwq : s == 1 ? p.cwk : p.cwv;
+      const float* cin = s == 0 ? p.ciq : s == 1 ? p.cik : p.civ;
+      float* cout = s == 0 ? p.coq : s == 1 ? p.cok : p.cov;
+      T* out = static_cast<T*>(s == 0 ? p.q : s == 1 ? p.k : p.v);
+      wide_conv<T, CONV>(p, rg, raw, ld, s == 2 ? VD : KD, taps, cin, cout, out, bb, t0, c, lane,
+                         s == 2 ? 0 : p.K / 8);
+      continue;
+    }
+    u -= 2 * NQ + NV;
+    if (u < NQ + NV) {  // b, w
+      const bool isw = u >= NQ;
+      wide_gate<T, false>(p, rg, static_cast<const T*>(isw ? p.wr : p.br), isw ? p.ldw : p.ldb, isw ? VD : KD,
+                          isw ? p.w : p.b, bb, t0, 256 * (isw ? u - NQ : u) + 8 * lane,
+                          (!isw && p.negeig) ? 2.f : 1.f);
+      continue;
+    }
+    u -= NQ + NV;
+    wide_gate<T, true>(p, rg, static_cast<const T*>(p.fr), p.ldf, KD, p.g, bb, t0, 256 * u + 8 * lane, 1.f);
+  }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p % 16) == 0; }
+
+// Whether the wide kernel can take the full token blocks of this call.
+template <typename T>
+bool wide_ok(const ProParams& p) {
+  const int KD = p.H * p.K, VD = p.HV * p.V;
+  if (KD % 256 || VD % 256 || (p.K != 32 && p.K != 64 && p.K != 128 && p.K != 256)) return false;
+  const void* raws[6] = {p.qr, p.kr, p.vr, p.br, p.wr, p.fr};
+  const int64_t lds[6] = {p.ldq, p.ldk, p.ldv, p.ldb, p.ldw, p.ldf};
+  for (int i = 0; i < 6; ++i)
+    if (!aligned16(raws[i]) || (lds[i] * (int64_t)sizeof(T)) % 16) return false;
+  const void* outs[6] = {p.q, p.k, p.v, p.b, p.w, p.g};
+  for (int i = 0; i < 6; ++i)
+    if (!aligned16(outs[i])) return false;
+  return true;
+}
+
+template <typename T, bool CONV>
+int launch_wide(const ProParams& p, int nfull, cudaStream_t st) {
+  const int KD = p.H * p.K, VD = p.HV * p.V;
+  const int64_t ntask = (int64_t)p.B * nfull * (4 * (KD / 256) + 2 * (VD / 256));
+  const int smem = WIDE_WARPS * WIDE_DEPTH * Wide<T>::PIECES * 512;
+  void (*fn)(const ProParams, int, int64_t) = k_prologue_wide<T, CONV>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return check_cuda(e, "project activations (wide): smem attribute");
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, WIDE_WARPS * 32, smem);
+  if (e != cudaSuccess) return check_cuda(e, "project activations (wide): occupancy");
+  int64_t grid = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+  const int64_t need = (ntask + WIDE_WARPS - 1) / WIDE_WARPS;
+  if (grid > need) grid = need;
+  fn<<<(unsigned)grid, WIDE_WARPS * 32, smem, st>>>(p, nfull, ntask);
+  return check_cuda(cudaGetLastError(), "project activations (wide) launch");
+}
+
 template <typename T, int NGK>
-int launch_t(const ProParams& p, cudaStream_t st) {
+int launch_t(const ProParams& p0, cudaStream_t st) {
+  ProParams p = p0;
+  // Full token blocks through the wide kernel when the shapes allow; the
+  // generic kernels take the rest (a ragged last block, or everything).
+  const int nfull = wide_ok<T>(p) ? p.T / PRO_ROWS : 0;
+  if (nfull > 0) {
+    const int rc = p.use_conv ? launch_wide<T, true>(p, nfull, st) : launch_wide<T, false>(p, nfull, st);
+    if (rc) return rc;
+  }
+  p.tb0 = nfull;
+  if (p.tb0 == p.ntb) return 0;
   const int KD = p.H * p.K, VD = p.HV * p.V;
   const int SK = (KD + 127) / 128, SV = (VD + 127) / 128;
-  const int64_t conv_tasks = (int64_t)p.B * p.ntb * (2 * p.H + SV);
-  const int64_t gate_tasks = (int64_t)p.B * p.ntb * (2 * SK + SV);
+  const int64_t conv_tasks = (int64_t)p.B * (p.ntb - p.tb0) * (2 * p.H + SV);
+  const int64_t gate_tasks = (int64_t)p.B * (p.ntb - p.tb0) * (2 * SK + SV);
   const unsigned conv_blocks = (unsigned)((conv_tasks + PRO_WARPS - 1) / PRO_WARPS);
   if (p.use_conv)
     k_prologue_conv<T, NGK, true><<<conv_blocks, PRO_WARPS * 32, 0, st>>>(p);
@@ -451,6 +793,7 @@ int launch_project_activations(const gdn2_prologue_args* a, cudaStream_t st) {
   p.a_log = a->a_log; p.dt_bias = a->dt_bias; p.decay = a->decay_factors;
   p.q = a->q; p.k = a->k; p.v = a->v; p.b = a->b; p.w = a->w; p.g = a->g;
   p.ntb = (d.seq_len + PRO_ROWS - 1) / PRO_ROWS;
+  p.tb0 = 0;
   return a->dtype == GDN2_DTYPE_BF16 ? launch_dt<__nv_bfloat16>(p, st) : launch_dt<float>(p, st);
 }
 

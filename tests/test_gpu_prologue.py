@@ -26,6 +26,14 @@ CASES = [
     (1, 65, 1, 256, 1, 128, True, False, False, None),
     (1, 40, 3, 32, 3, 48, False, False, True, None),
     (1, 2, 2, 128, 2, 128, True, True, False, None),
+    # full 64-token blocks of 256-channel slices: the wide kernel (K = 32 .. 256),
+    # with and without conv / cache; the T = 100 and 70 cases above split into a
+    # wide block and a generic ragged tail
+    (1, 128, 4, 64, 2, 128, True, True, True, 0.9),
+    (2, 192, 2, 128, 2, 256, True, False, False, None),
+    (1, 64, 2, 256, 2, 128, True, True, False, None),
+    (1, 64, 8, 32, 4, 64, True, False, True, None),
+    (1, 128, 2, 128, 2, 128, False, False, False, 0.5),
 ]
 
 
