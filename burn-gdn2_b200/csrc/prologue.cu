@@ -1,7 +1,13 @@
 // Projection activations (gdn2_project_activations): the elementwise part of
 // GatedDeltaNet2::project (src/module.rs:381-498) in one memory-bound pass.
 //
-// Work unit: one warp per (batch, block of PRO_ROWS tokens, stream, head or
+// Two paths.  Full 64-token blocks of the common shapes (every stream a
+// whole number of 256-channel slices, K a power of two in [32, 256], rows
+// 16-byte aligned) go through the wide persistent kernel further down
+// (8 channels per lane, cp.async row rings).  Everything else (a ragged last
+// block, odd shapes) goes through the generic kernels described here.
+//
+// Generic work unit: one warp per (batch, block of PRO_ROWS tokens, stream, head or
 // 128-channel slice), walking its tokens in order.  Lane l owns channels
 // 4l..4l+3 of each 128-channel group, so a token's row is one coalesced
 // 256-byte (bf16) access per group.  q and k tasks cover one key head (one
