@@ -290,6 +290,13 @@ def run_ours(args):
     layer_tp = run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world) if world > 1 else None
     # ---- the f32 configuration of BASELINE config 2 (CUDA-core path) ----
     f32 = run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world) if not args.core_only else None
+    # ---- BASELINE configs 4 and 5, chunk core ----
+    others = None
+    if not args.core_only:
+        others = {"cfg4_core": run_core_cfg(torch, bg, ops, dev, stream, CFG4, "config 4", max_over_ranks, world,
+                                            seed=4000 + 10 * rank),
+                  "cfg5_core": run_core_cfg(torch, bg, ops, dev, stream, CFG5, "config 5", max_over_ranks, world,
+                                            seed=5000 + 10 * rank)}
 
     # ---- roofline of the dominant kernel ----
     peaks = load_peaks()
@@ -328,6 +335,7 @@ def run_ours(args):
             "layer": layer,
             "layer_head_sharded": layer_tp,
             "f32": f32,
+            "other_configs": others,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
@@ -469,6 +477,60 @@ def run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world):
     peaks = load_peaks()
     return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "kernels_ms": split,
             "workload": "BASELINE config 2 chunked forward core in f32 (CUDA-core path, exact f32)",
+            "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
+
+
+# BASELINE configs 4 (GVA: 8 key heads grouped over 16 value heads, V = 256, neg-eig b in [0, 2], min_decay 0.9)
+# and 5 (long context, 32 heads), chunk core only (bf16), measured beside the headline so the path each one
+# takes and its roofline fraction are on record.
+CFG4 = dict(B=4, H=8, HV=16, T=8192, K=128, V=256, chunk=64, negeig=True, min_decay=0.9)
+CFG5 = dict(B=2, H=32, HV=32, T=65536, K=128, V=128, chunk=64, negeig=False, min_decay=None)
+
+
+def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, seed):
+    """Chunk core (intra + inter + fused epilogue) at one BASELINE config:
+    tokens/s, ms/step and the fraction of the measured HBM copy bandwidth
+    its algorithmic bytes reach.  Key-side inputs (q, k, g, b) have H heads
+    and are read grouped (value head hv uses key head hv // (HV / H))."""
+    B, H, HV, T, K, V = c["B"], c["H"], c["HV"], c["T"], c["K"], c["V"]
+    xk = make_inputs(torch, B, H, T, K, K, torch.bfloat16, dev, seed=seed)
+    xv = make_inputs(torch, B, HV, T, V, V, torch.bfloat16, dev, seed=seed + 1)
+    b = xk["b"]
+    if c["negeig"]:
+        b = (b.float() * 2.0).to(torch.bfloat16)
+    g = xk["g"]
+    if c["min_decay"] is not None:  # the module's remap with decay factors 2: log(sigmoid(2) (1 - m) e^g + m)
+        g = torch.log((1.0 / (1.0 + math.exp(-2.0))) * (1.0 - c["min_decay"]) * torch.exp(g) + c["min_decay"])
+    view = lambda t: t.permute(0, 2, 1, 3)
+    state = torch.zeros(B, HV, K, V, dtype=torch.float32, device=dev)
+    out = torch.empty(B, T, HV, V, dtype=torch.bfloat16, device=dev)
+    onw = torch.ones(V, dtype=torch.float32, device=dev)
+    a = ops.chunk_args(view(xk["q"]), view(xk["k"]), view(xv["v"]), view(g.contiguous()), view(b), view(xv["w"]),
+                       state, view(out), K ** -0.5, c["chunk"], num_heads=H, grouped=H < HV, gate=view(xv["gate"]),
+                       o_norm_weight=onw, norm_eps=1e-5)
+    ws = ops.chunk_workspace(a, dev)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    run = lambda: bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ws.numel(), sh))
+    run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 3
+    e0.record(stream)
+    for _ in range(n):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    del ws, xk, xv
+    # algorithmic bytes per value head: the key-side reads count once per value head, as the kernels read them
+    alg = core_bytes_per_token_head(K, V, 2) * B * T * HV
+    tc = K == 128 and V in (64, 128) and c["chunk"] == 64
+    peaks = load_peaks()
+    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "workload": f"BASELINE {name} chunk core: B={B} (per rank), T={T}, H={H}, HV={HV}, K={K}, V={V}, bf16",
+            "path": "tensor cores (k_intra_tc + k_inter_tc)" if tc else
+                    "CUDA cores, f32 arithmetic (k_intra_simt + k_inter_simt + k_chunk_out): V > 128",
             "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
 

@@ -276,3 +276,64 @@ def test_chunk_tensor_core_grouped_heads_and_epilogue():
     assert np.abs(y - y_ref).max() <= 0.05 * np.abs(y_ref).max()
     assert_close_bf16(st.cpu().numpy(), s_ref, what="state")
     assert bg._lib.read_device_errors() == 0
+
+
+def test_chunk_config4_features_bf16():
+    """BASELINE config-4 core features at small size: 2 key heads grouped
+    over 4 value heads (value head hv reads key head hv // 2), K = 128,
+    V = 256 (outside the tcgen05 path: the CUDA-core kernels with the
+    separate gated RMS-norm epilogue), neg-eig b in [0, 2], g after the
+    min_decay 0.9 remap, a partial last chunk; bf16 vs the f64 oracle."""
+    import ctypes
+    import burn_gdn2 as bg
+    from burn_gdn2 import ops
+
+    B, H, HV, T, K, V = 2, 2, 4, 150, 128, 256
+    rng = np.random.default_rng(96)
+    kq = O.make_core_inputs(B, H, T, K, V, seed=97, dtype=np.float32)
+    kv = O.make_core_inputs(B, HV, T, K, V, seed=98, dtype=np.float32)
+    gate = rng.standard_normal((B, T, HV, V)).astype(np.float32)
+    onw = rng.uniform(0.5, 1.5, V).astype(np.float32)
+    fac = (1.0 / (1.0 + np.exp(-2.0))) * (1.0 - 0.9)
+    g_remap = np.log(fac * np.exp(kq["g"].astype(np.float64)) + 0.9).astype(np.float32)
+    t = lambda a, dt=torch.bfloat16: torch.tensor(a, device=DEV, dtype=dt)
+    q, k, b = t(kq["q"]), t(kq["k"]), t(2.0 * kq["b"])
+    g = t(g_remap, torch.float32)
+    v, w = t(kv["v"]), t(kv["w"])
+    gt = t(gate)
+    st = torch.zeros(B, HV, K, V, device=DEV)
+    out = torch.empty(B, T, HV, V, device=DEV, dtype=torch.bfloat16)
+    a = ops.chunk_args(q, k, v, g, b, w, st, out.permute(0, 2, 1, 3), K ** -0.5, 64, num_heads=H, grouped=True,
+                       gate=gt.permute(0, 2, 1, 3), o_norm_weight=t(onw, torch.float32), norm_eps=1e-5)
+    ws = ops.chunk_workspace(a, DEV)
+    bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a), ops.ptr(ws), ws.numel(), ops.stream_handle()))
+    torch.cuda.synchronize()
+    r = lambda x: x.float().cpu().numpy().astype(np.float64)
+    rep = lambda x: np.repeat(x, HV // H, axis=1)
+    o_ref, s_ref = O.chunk_wy_forward(rep(r(q)), rep(r(k)), r(v), rep(r(g)), rep(r(b)), r(w),
+                                      np.zeros((B, HV, K, V)), K ** -0.5, 64)
+    y_ref = O.rms_norm_gate_per_head(o_ref.transpose(0, 2, 1, 3), r(gt), onw.astype(np.float64), 1e-5)
+    y = out.float().cpu().numpy()
+    assert np.linalg.norm(y - y_ref) / np.linalg.norm(y_ref) <= BF16_NORMWISE
+    assert np.abs(y - y_ref).max() <= 0.05 * np.abs(y_ref).max()
+    assert_close_bf16(st.cpu().numpy(), s_ref, what="state")
+    assert bg._lib.read_device_errors() == 0
+
+
+def test_chunk_long_sequence_config5_bf16():
+    """BASELINE config-5 sequence length (T = 65536, 1024 chunks per chain)
+    on the tcgen05 path at B * HV = 2, against the token-by-token recurrent
+    kernel on the same inputs (a size-independent property: the f64 oracle
+    would take minutes here); output and final state."""
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = 1, 2, 65536, 128, 128
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=99, dtype=np.float32)
+    d = _to_dev({k: arrs[k] for k in "qkvgbw"}, torch.bfloat16)
+    s0 = torch.tensor(np.random.default_rng(100).standard_normal((B, HV, K, V)).astype(np.float32) * 0.5,
+                      device=DEV)
+    oc, sc = bg.chunk_wy_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], s0, K ** -0.5, 64)
+    orr, sr = bg.fused_recurrent_forward(d["q"], d["k"], d["v"], d["g"], d["b"], d["w"], s0, K ** -0.5)
+    assert_close_bf16(oc.float().cpu().numpy(), orr.float().cpu().numpy(), what="out")
+    assert_close_bf16(sc.cpu().numpy(), sr.cpu().numpy(), what="state")
+    assert bg._lib.read_device_errors() == 0
