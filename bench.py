@@ -525,12 +525,12 @@ def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, se
     del ws, xk, xv
     # algorithmic bytes per value head: the key-side reads count once per value head, as the kernels read them
     alg = core_bytes_per_token_head(K, V, 2) * B * T * HV
-    tc = K == 128 and V in (64, 128) and c["chunk"] == 64
     peaks = load_peaks()
     return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
             "workload": f"BASELINE {name} chunk core: B={B} (per rank), T={T}, H={H}, HV={HV}, K={K}, V={V}, bf16",
-            "path": "tensor cores (k_intra_tc + k_inter_tc)" if tc else
-                    "CUDA cores, f32 arithmetic (k_intra_simt + k_inter_simt + k_chunk_out): V > 128",
+            "path": "tensor cores (k_intra_tc + k_inter_tc)" if V <= 128 else
+                    "tensor cores (k_intra_tc, k_inter_tc over two 128-column slices per chain, raw o in f32) "
+                    "+ k_chunk_out (gated RMS norm over whole rows)",
             "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
 

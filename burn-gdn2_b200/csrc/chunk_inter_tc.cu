@@ -3,14 +3,19 @@
 //
 // Replaces gdn2_chunk_inter_kernel (src/kernel/chunk_cube.rs:300-610); math
 // of src/forward.rs:263-274 with the epilogue of src/module.rs:501-517.
-// One CTA (8 warps) per (value head, batch) walks the chunks in order.  The
-// state S [K][V] stays in TMEM in f32 for the whole sequence; a bf16 image
-// of it in shared memory is the MMA operand.  Per chunk:
+// One CTA (8 warps) per (value-column slice, value head, batch) walks the
+// chunks in order; V <= 128 is one slice, V = 256 two slices of 128 columns
+// (the value columns of the recurrence are independent: each slice reads the
+// shared W, Qg, Kd, Aqk parts of the record and its own U columns).  The
+// state S [K][V] slice stays in TMEM in f32 for the whole sequence; a bf16
+// image of it in shared memory is the MMA operand.  Per chunk:
 //   MMA1  D = [W; Qg] S                    (M=128, N=V, K=128)
 //   v_new = U - (W S)                      (rows 0..63 of D, to smem, bf16)
 //   MMA2  D += [0; Aqk] v_new              (rows 64..127 become o)
 //   MMA3  S = diag(gamma_last) S + Kd^T v_new   (S pre-scaled in TMEM)
 //   o -> gated RMS norm -> out; S -> bf16 image for the next chunk.
+// With two slices the RMS norm needs both halves of a row, so o goes to an
+// f32 workspace instead and the gated norm runs as a separate pass.
 // The per-chunk record written by the intra kernel (operand-tile images)
 // arrives by bulk copies into one of two stages while the previous chunk
 // computes.
@@ -48,20 +53,22 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
 
   const int hv = blockIdx.y, bb = blockIdx.z;
-  const int V = p.V, HALF = V / 2;
+  const int V = p.vt, HALF = V / 2;                 // columns of this CTA's slice
+  const int VF = p.V, cbase = blockIdx.x * p.vt;   // full row width, first column of the slice
+  const bool raw_o = p.vsplit > 1;                 // o to the f32 workspace (norm runs separately)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sp = warp & 3, half = warp >> 2;
   const int col0 = half * HALF;
-  const TcRecord L = tc_record_layout(V);
+  const TcRecord L = tc_record_layout(VF);
   const unsigned char* recs = p.rec + ((size_t)bb * p.HV + hv) * p.NC * p.rec_bytes;
-  float* st = p.state + ((size_t)bb * p.HV + hv) * (size_t)TC_K * V;
+  float* st = p.state + ((size_t)bb * p.HV + hv) * (size_t)TC_K * VF + cbase;
   const uint32_t sbase = smem_u32(sm);
 
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
     umma::tmem_relinquish();
   }
-  if (p.fuse_epilogue)
+  if (p.fuse_epilogue && !raw_o)
     for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[i];
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
@@ -89,7 +96,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     bulk_g2s(d + ST_WQ, r + L.wq, 32768u, &bars[s]);
     bulk_g2s(d + ST_TA + 8192, r + L.aqk, 8192u, &bars[s]);
     bulk_g2s(d + ST_KD, r + L.kd, 16384u, &bars[s]);
-    bulk_g2s(d + ST_U, r + L.u, ub, &bars[s]);
+    bulk_g2s(d + ST_U, r + L.u + (size_t)blockIdx.x * ub, ub, &bars[s]);
     bulk_g2s(d + ST_GL, r + L.gl, 512u, &bars[s]);
   };
   if (tid == 0) issue(0);
@@ -99,7 +106,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   for (int c16 = 0; c16 < HALF / 16; ++c16) {
     const int col = col0 + 16 * c16;
     float v[16];
-    const float4* src = reinterpret_cast<const float4*>(st + (size_t)kk * V + col);
+    const float4* src = reinterpret_cast<const float4*>(st + (size_t)kk * VF + col);
     #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 f = src[j];
@@ -129,7 +136,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   const int orow = 32 * (sp - 2) + lane;
   auto load_gate = [&](int c) {
     const int t0 = c * TC_C;
-    if (p.fuse_epilogue && orow < min(TC_C, p.T - t0)) {
+    if (p.fuse_epilogue && !raw_o && orow < min(TC_C, p.T - t0)) {
       const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
                                 (int64_t)(t0 + orow) * p.gate.s2 + col0;
       #pragma unroll
@@ -147,6 +154,16 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       if (16 * c16 < HALF)
         umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), *reinterpret_cast<float(*)[16]>(ov + 16 * c16));
     umma::wait_ld();
+    if (raw_o) {  // f32 o [B,HV,T,V] for the separate gated-norm pass (uniform branch: no named barrier skipped)
+      if (orow < cv) {
+        float4* op = reinterpret_cast<float4*>(p.o_ws + (((size_t)bb * p.HV + hv) * p.T + t0 + orow) * VF + cbase +
+                                               col0);
+        #pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (4 * j < HALF) op[j] = make_float4(ov[4 * j], ov[4 * j + 1], ov[4 * j + 2], ov[4 * j + 3]);
+      }
+      return;
+    }
     float s4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
     #pragma unroll
     for (int j = 0; j < 64; ++j)
@@ -322,7 +339,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     float v[16];
     umma::ld16(umma::taddr(tS, 32 * sp, col), v);
     umma::wait_ld();
-    float4* dst = reinterpret_cast<float4*>(st + (size_t)kk * V + col);
+    float4* dst = reinterpret_cast<float4*>(st + (size_t)kk * VF + col);
     #pragma unroll
     for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
@@ -335,13 +352,13 @@ int launch_inter_tc(const TcParams& p, cudaStream_t st) {
   const size_t smem = inter_smem::TOTAL + 1024;
   cudaError_t e = cudaFuncSetAttribute((const void*)k_inter_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "chunk inter (tc) smem attribute");
-  dim3 grid(1, p.HV, p.B);
+  dim3 grid(p.vsplit, p.HV, p.B);
   k_inter_tc<<<grid, 256, smem, st>>>(p);
   return check_cuda(cudaGetLastError(), "chunk inter (tc) launch");
 }
 
 bool tc_supported(int K, int V, int C, int dtype) {
-  return dtype == GDN2_DTYPE_BF16 && K == TC_K && C == TC_C && (V == 64 || V == 128);
+  return dtype == GDN2_DTYPE_BF16 && K == TC_K && C == TC_C && (V == 64 || V == 128 || V == 256);
 }
 
 GDN2_DEVICE_ERROR_READER(read_device_errors_inter_tc)

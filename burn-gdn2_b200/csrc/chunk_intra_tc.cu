@@ -38,9 +38,12 @@ constexpr uint32_t AQK_IMG = 36864;     // bf16 K-major [64][64]
 constexpr uint32_t TINV_IMG = 45056;    // bf16 K-major [64][64]
 constexpr uint32_t SCRATCH = 53248;     // 6 x f32 [16][20] blocks of the inverse
 constexpr uint32_t RK = R1_END;         // bf16 MN-major [64][128]
-constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][V], V <= 128
-constexpr uint32_t MISC = RV + 16384;   // half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem base
-constexpr uint32_t TOTAL = MISC + 4096 + 512 + 64;
+constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][VMAX]
+// after RV: half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem base
+template <int VMAX>
+constexpr uint32_t MISC = RV + 128 * VMAX;
+template <int VMAX>
+constexpr uint32_t TOTAL = MISC<VMAX> + 4096 + 512 + 64;
 }  // namespace intra_smem
 
 // Loads of the kernel's read-only inputs.  Written as non-volatile asm
@@ -63,7 +66,8 @@ __device__ __forceinline__ float4 ld_f4_nc(const float* ptr) {
 
 __device__ __forceinline__ void l2_prefetch(const void* a) { asm volatile("prefetch.global.L2 [%0];" ::"l"(a)); }
 
-// Line j (0..13) of token t's inputs: q k b v w (two 128-byte lines each), g (four).
+// Line j of token t's inputs: q k b v w (two 128-byte lines each), g (four),
+// then for V = 256 the second 256 bytes of v (j = 14, 15) and w (16, 17).
 __device__ __forceinline__ void prefetch_line(const TcParams& p, int bb, int kh, int hv, int t, int j) {
   if (j < 10) {
     if (j >= 6 && (j & 1) && p.V <= 64) return;
@@ -71,9 +75,13 @@ __device__ __forceinline__ void prefetch_line(const TcParams& p, int bb, int kh,
     const int h = j < 6 ? kh : hv;
     l2_prefetch(reinterpret_cast<const char*>(static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + h * v.s1 +
                                               (int64_t)t * v.s2) + (j & 1) * 128);
-  } else {
+  } else if (j < 14) {
     l2_prefetch(reinterpret_cast<const char*>(static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 +
                                               (int64_t)t * p.g.s2) + (j - 10) * 128);
+  } else {
+    const DView& v = j < 16 ? p.v : p.w;
+    l2_prefetch(reinterpret_cast<const char*>(static_cast<const __nv_bfloat16*>(v.p) + bb * v.s0 + hv * v.s1 +
+                                              (int64_t)t * v.s2) + 256 + (j & 1) * 128);
   }
 }
 
@@ -88,11 +96,17 @@ __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
   return make_uint2(umma::pack_bf16x2(a, b), umma::pack_bf16x2(c, d));
 }
 
-__global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
+// VMAX = 128: V in {64, 128}, two CTAs per SM (256 TMEM columns each).
+// VMAX = 256: V = 256, one CTA per SM (rhs_v is 32 KB, U takes 256 TMEM
+// columns next to W's 128); lane l also owns value channels 128 + 4l .. +3.
+template <int VMAX>
+__global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcParams p) {
   using namespace intra_smem;
+  constexpr uint32_t TCOLS = VMAX > 128 ? 512 : 256;  // TMEM columns: W [0, 128), U [128, 128 + V)
+  constexpr int NL = VMAX > 128 ? 18 : 14;            // 128-byte input lines per token
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
-  float* sHalf = reinterpret_cast<float*>(sm + MISC);  // [8][128] g sums of each 8-row half tile
+  float* sHalf = reinterpret_cast<float*>(sm + MISC<VMAX>);  // [8][128] g sums of each 8-row half tile
   float* sGlast = sHalf + 8 * 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGlast + 128);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
@@ -110,7 +124,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   const TcRecord L = tc_record_layout(V);
 
   if (warp == 0) {
-    umma::tmem_alloc(tslot, 256);
+    umma::tmem_alloc(tslot, TCOLS);
     umma::tmem_relinquish();
   }
   if (tid == 0) {
@@ -120,15 +134,16 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   }
 
   // every input line of this warp's 8 rows on its way to L2 before the first use
-  for (int idx = lane; idx < 8 * 14; idx += 32) {
-    const int r = r0 + idx / 14;
-    if (r < cv) prefetch_line(p, bb, kh, hv, t0 + r, idx % 14);
+  for (int idx = lane; idx < 8 * NL; idx += 32) {
+    const int r = r0 + idx / NL;
+    if (r < cv) prefetch_line(p, bb, kh, hv, t0 + r, idx % NL);
   }
 
   // ---- 1. sums of g over each half tile (the per-row cumsum is rebuilt below) ----
   const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
   // inputs of row r0 + i, fetched one row ahead of their use in step 2
   uint2 nq, nk, nb, nv = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
+  uint2 nv2 = make_uint2(0u, 0u), nw2 = make_uint2(0u, 0u);  // value channels 128 + ch (VMAX = 256)
   float4 ng = make_float4(0.f, 0.f, 0.f, 0.f);
   auto fetch = [&](int i) {
     const int r = r0 + i;
@@ -140,6 +155,10 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     if (ch < V) {
       nv = ld4_raw(p.v, bb, hv, t0 + r, ch, ok);
       nw = ld4_raw(p.w, bb, hv, t0 + r, ch, ok);
+    }
+    if (VMAX > 128) {
+      nv2 = ld4_raw(p.v, bb, hv, t0 + r, ch + 128, ok);
+      nw2 = ld4_raw(p.w, bb, hv, t0 + r, ch + 128, ok);
     }
   };
   fetch(0);
@@ -220,7 +239,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     #pragma unroll 2
     for (int i = 0; i < 8; ++i) {
       const int r = r0 + i;
-      const uint2 cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw;
+      const uint2 cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw, cvv2 = nv2, cw2 = nw2;
       if (r < cv) {
         gl[0] += ng.x; gl[1] += ng.y; gl[2] += ng.z; gl[3] += ng.w;
       }
@@ -250,6 +269,12 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
       *reinterpret_cast<uint2*>(kdr + ro) = pack4(kd[0], kd[1], kd[2], kd[3]);
       *reinterpret_cast<uint2*>(rkr + ro) = pack4(rk[0], rk[1], rk[2], rk[3]);
       if (ch < V) *reinterpret_cast<uint2*>(rvr + ro) = pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
+      if (VMAX > 128) {  // channels 128 + ch: MN-major groups 2, 3 (two groups of 64 K rows x 128 bytes further)
+        float v2[4], w2[4];
+        unpack4(cvv2, v2);
+        unpack4(cw2, w2);
+        *reinterpret_cast<uint2*>(rvr + 2 * 64 * 128 + ro) = pack4(w2[0] * v2[0], w2[1] * v2[1], w2[2] * v2[2], w2[3] * v2[3]);
+      }
       #pragma unroll
       for (int pp = 0; pp < 4; ++pp) {
         if (pp < tp) continue;
@@ -479,16 +504,22 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   }
   umma::fence_before_sync();
   __syncthreads();
-  if (warp == 0) umma::tmem_dealloc(tA, 256);
+  if (warp == 0) umma::tmem_dealloc(tA, TCOLS);
+}
+
+template <int VMAX>
+static int launch_intra_tc_v(const TcParams& p, cudaStream_t st) {
+  const size_t smem = intra_smem::TOTAL<VMAX> + 1024;
+  cudaError_t e =
+      cudaFuncSetAttribute((const void*)k_intra_tc<VMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "chunk intra (tc) smem attribute");
+  dim3 grid(p.NC, p.HV, p.B);
+  k_intra_tc<VMAX><<<grid, 256, smem, st>>>(p);
+  return check_cuda(cudaGetLastError(), "chunk intra (tc) launch");
 }
 
 int launch_intra_tc(const TcParams& p, cudaStream_t st) {
-  const size_t smem = intra_smem::TOTAL + 1024;
-  cudaError_t e = cudaFuncSetAttribute((const void*)k_intra_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return check_cuda(e, "chunk intra (tc) smem attribute");
-  dim3 grid(p.NC, p.HV, p.B);
-  k_intra_tc<<<grid, 256, smem, st>>>(p);
-  return check_cuda(cudaGetLastError(), "chunk intra (tc) launch");
+  return p.V > 128 ? launch_intra_tc_v<256>(p, st) : launch_intra_tc_v<128>(p, st);
 }
 
 GDN2_DEVICE_ERROR_READER(read_device_errors_intra_tc)
