@@ -529,8 +529,8 @@ def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, se
     return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
             "workload": f"BASELINE {name} chunk core: B={B} (per rank), T={T}, H={H}, HV={HV}, K={K}, V={V}, bf16",
             "path": "tensor cores (k_intra_tc + k_inter_tc)" if V <= 128 else
-                    "tensor cores (k_intra_tc, k_inter_tc over two 128-column slices per chain, raw o in f32) "
-                    "+ k_chunk_out (gated RMS norm over whole rows)",
+                    "tensor cores (k_intra_tc; k_inter_tc over two 128-column slices per chain, a 2-CTA cluster "
+                    "exchanging the gated RMS norm's row sums)",
             "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
 

@@ -76,18 +76,9 @@ static bool use_tc(const gdn2_chunk_args* a) {
 // Value columns per inter CTA: V <= 128 in one slice, V = 256 in two.
 static int tc_vt(int V) { return V > 128 ? 128 : V; }
 
-// The chunk records, then (V = 256 only) the f32 o [B,HV,T,V] that the
-// separate gated-norm pass reads.
-static size_t tc_records_bytes(const gdn2_dims& d) {
+static size_t tc_workspace_bytes(const gdn2_dims& d) {
   const size_t nch = (size_t)d.batch * d.num_v_heads * ((d.seq_len + TC_C - 1) / TC_C);
   return nch * tc_record_layout(d.head_v_dim).bytes;
-}
-
-static size_t tc_workspace_bytes(const gdn2_dims& d) {
-  size_t n = tc_records_bytes(d);
-  if (tc_vt(d.head_v_dim) < d.head_v_dim)
-    n += (size_t)d.batch * d.num_v_heads * d.seq_len * d.head_v_dim * sizeof(float);
-  return n;
 }
 
 static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, const char* fn) {
@@ -108,8 +99,7 @@ static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, 
   p.state = a->state;
   p.rec = static_cast<unsigned char*>(ws);
   p.rec_bytes = tc_record_layout(d.head_v_dim).bytes;
-  // records are whole KB, so the o workspace behind them is 16-byte aligned
-  p.o_ws = p.vsplit > 1 ? reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + tc_records_bytes(d)) : nullptr;
+  p.o_ws = nullptr;
   return GDN2_OK;
 }
 
@@ -231,10 +221,7 @@ int gdn2_chunk_inter(const gdn2_chunk_args* a, void* ws, size_t wsb, void* strea
     TcParams t;
     rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_inter");
     if (rc) return rc;
-    rc = launch_inter_tc(t, (cudaStream_t)stream);
-    if (rc || t.vsplit == 1) return rc;
-    p.ws_o = t.o_ws;  // column slices: the gated RMS norm over whole rows as its own pass
-    return launch_chunk_out(p, a->dtype, (cudaStream_t)stream);
+    return launch_inter_tc(t, (cudaStream_t)stream);
   }
   rc = launch_inter_simt(p, (cudaStream_t)stream);
   if (rc) return rc;
@@ -251,10 +238,7 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream)
     if (rc) return rc;
     rc = launch_intra_tc(t, (cudaStream_t)stream);
     if (rc) return rc;
-    rc = launch_inter_tc(t, (cudaStream_t)stream);
-    if (rc || t.vsplit == 1) return rc;
-    p.ws_o = t.o_ws;  // column slices: the gated RMS norm over whole rows as its own pass
-    return launch_chunk_out(p, a->dtype, (cudaStream_t)stream);
+    return launch_inter_tc(t, (cudaStream_t)stream);
   }
   rc = launch_intra_simt(p, a->dtype, (cudaStream_t)stream);
   if (rc) return rc;

@@ -14,8 +14,11 @@
 //   MMA2  D += [0; Aqk] v_new              (rows 64..127 become o)
 //   MMA3  S = diag(gamma_last) S + Kd^T v_new   (S pre-scaled in TMEM)
 //   o -> gated RMS norm -> out; S -> bf16 image for the next chunk.
-// With two slices the RMS norm needs both halves of a row, so o goes to an
-// f32 workspace instead and the gated norm runs as a separate pass.
+// With two slices the RMS norm needs both halves of a row: the two CTAs of a
+// chain form a cluster, and each epilogue thread writes its slice's row sum
+// of squares into the other CTA's shared memory and arrives on that CTA's
+// exchange mbarrier (release, cluster scope), then waits on its own (bounded,
+// acquire) for the other half.
 // The per-chunk record written by the intra kernel (operand-tile images)
 // arrives by bulk copies into one of two stages while the previous chunk
 // computes.
@@ -36,13 +39,51 @@ constexpr uint32_t VN_IMG = S_IMG + 32768;      // MN-major [64][V]
 constexpr uint32_t MISC = VN_IMG + 16384;       // rms partials [64][2], o-norm weight [V], barriers, tmem slot
 constexpr uint32_t ONW = MISC + 512;
 constexpr uint32_t BARS = ONW + 512;
-constexpr uint32_t TOTAL = BARS + 64;
+constexpr uint32_t XSUM = BARS + 64;    // f32 [2][64]: the peer slice's row sums, by chunk parity
+constexpr uint32_t XBARS = XSUM + 512;  // 2 mbarriers: the peer's 128 epilogue threads arrived, by chunk parity
+constexpr uint32_t TOTAL = XBARS + 64;
 }  // namespace inter_smem
 
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// Bounded wait with cluster-scope acquire (the arrivals come from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, unsigned parity) {
+  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  atomicOr(&g_device_errors, DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// XCHG: the two value-column slices of a chain (a 2-CTA cluster) exchange
+// the RMS norm's row sums; a separate instantiation keeps the one-slice
+// kernel free of that code.
+template <bool XCHG>
 __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   using namespace inter_smem;
   extern __shared__ __align__(1024) unsigned char smraw[];
@@ -51,11 +92,14 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   float* sOnw = reinterpret_cast<float*>(sm + ONW);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);  // full[2], mma1, mma2/3, operands ready
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
+  float* sXsum = reinterpret_cast<float*>(sm + XSUM);
+  uint64_t* xbars = reinterpret_cast<uint64_t*>(sm + XBARS);
 
   const int hv = blockIdx.y, bb = blockIdx.z;
   const int V = p.vt, HALF = V / 2;                 // columns of this CTA's slice
   const int VF = p.V, cbase = blockIdx.x * p.vt;   // full row width, first column of the slice
-  const bool raw_o = p.vsplit > 1;                 // o to the f32 workspace (norm runs separately)
+  constexpr bool xchg = XCHG;                          // row sums exchanged with the other slice's CTA
+  const uint32_t peer = blockIdx.x ^ 1u;               // cluster rank of that CTA (cluster = the vsplit slices)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sp = warp & 3, half = warp >> 2;
   const int col0 = half * HALF;
@@ -68,11 +112,13 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     umma::tmem_alloc(tslot, 512);
     umma::tmem_relinquish();
   }
-  if (p.fuse_epilogue && !raw_o)
-    for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[i];
+  if (p.fuse_epilogue)
+    for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[cbase + i];
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
     mbar_init(&bars[4], 256);  // every thread: its v_new rows / S rescale done
+    mbar_init(&xbars[0], 128);
+    mbar_init(&xbars[1], 128);
     fence_mbar_init();
   }
   // zero halves of the [0; Aqk] tiles (never written by the copies)
@@ -82,6 +128,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   }
   umma::fence_before_sync();
   __syncthreads();
+  if (xchg) cluster_sync_all();  // the peer's exchange barriers are initialised before anyone arrives on them
   umma::fence_after_sync();
   const uint32_t tD0 = *tslot;   // D of even chunks: cols [0, V); odd chunks: [V, 2V)
   const uint32_t tS = tD0 + 2 * V;  // S master: cols [2V, 3V)
@@ -136,9 +183,9 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   const int orow = 32 * (sp - 2) + lane;
   auto load_gate = [&](int c) {
     const int t0 = c * TC_C;
-    if (p.fuse_epilogue && !raw_o && orow < min(TC_C, p.T - t0)) {
+    if (p.fuse_epilogue && orow < min(TC_C, p.T - t0)) {
       const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
-                                (int64_t)(t0 + orow) * p.gate.s2 + col0;
+                                (int64_t)(t0 + orow) * p.gate.s2 + cbase + col0;
       #pragma unroll
       for (int j = 0; j < 8; ++j)
         if (8 * j < HALF) graw[j] = reinterpret_cast<const uint4*>(gp)[j];
@@ -154,16 +201,6 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       if (16 * c16 < HALF)
         umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), *reinterpret_cast<float(*)[16]>(ov + 16 * c16));
     umma::wait_ld();
-    if (raw_o) {  // f32 o [B,HV,T,V] for the separate gated-norm pass (uniform branch: no named barrier skipped)
-      if (orow < cv) {
-        float4* op = reinterpret_cast<float4*>(p.o_ws + (((size_t)bb * p.HV + hv) * p.T + t0 + orow) * VF + cbase +
-                                               col0);
-        #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (4 * j < HALF) op[j] = make_float4(ov[4 * j], ov[4 * j + 1], ov[4 * j + 2], ov[4 * j + 3]);
-      }
-      return;
-    }
     float s4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
     #pragma unroll
     for (int j = 0; j < 64; ++j)
@@ -171,11 +208,19 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
     sRms[orow * 2 + half] = ss;
     named_bar(1, 128);
-    const float inv = rsqrtf((sRms[orow * 2] + sRms[orow * 2 + 1]) / (float)V + p.eps);
+    float tot = sRms[orow * 2] + sRms[orow * 2 + 1];
+    if (xchg) {  // add the other slice's sum of this row (both halves of a row send the same value)
+      const int par = c & 1;
+      st_cluster_f32(cluster_addr(sXsum + par * 64 + orow, peer), tot);
+      mbar_arrive_cluster(cluster_addr(&xbars[par], peer));
+      mbar_wait_cluster_bounded(&xbars[par], (c >> 1) & 1);
+      tot += sXsum[par * 64 + orow];
+    }
+    const float inv = rsqrtf(tot / (float)VF + p.eps);
     named_bar(1, 128);  // sRms reusable
     if (orow < cv) {
       __nv_bfloat16* op = static_cast<__nv_bfloat16*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
-                          (int64_t)(t0 + orow) * p.out.s2 + col0;
+                          (int64_t)(t0 + orow) * p.out.s2 + cbase + col0;
       #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if (8 * j >= HALF) break;
@@ -345,16 +390,31 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
   }
   umma::fence_before_sync();
   __syncthreads();
+  if (xchg) cluster_sync_all();  // no CTA leaves while its peer may still reach its shared memory
   if (warp == 0) umma::tmem_dealloc(tD0, 512);
 }
 
 int launch_inter_tc(const TcParams& p, cudaStream_t st) {
   const size_t smem = inter_smem::TOTAL + 1024;
-  cudaError_t e = cudaFuncSetAttribute((const void*)k_inter_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const bool xchg = p.vsplit > 1 && p.fuse_epilogue;  // the slices of a chain exchange row sums: one cluster per chain
+  void (*fn)(const TcParams) = xchg ? k_inter_tc<true> : k_inter_tc<false>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "chunk inter (tc) smem attribute");
-  dim3 grid(p.vsplit, p.HV, p.B);
-  k_inter_tc<<<grid, 256, smem, st>>>(p);
-  return check_cuda(cudaGetLastError(), "chunk inter (tc) launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.vsplit, p.HV, p.B);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (xchg) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.vsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return check_cuda(cudaLaunchKernelEx(&cfg, fn, p), "chunk inter (tc) launch");
 }
 
 bool tc_supported(int K, int V, int C, int dtype) {
