@@ -225,20 +225,23 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       for (int j = 0; j < 8; ++j) {
         if (8 * j >= HALF) break;
         float y[8];
-        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&graw[j]);
-        #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float o = ov[8 * j + e];
-          if (p.fuse_epilogue) {
-            const float gt = (e & 1) ? __high2float(gh[e >> 1]) : __low2float(gh[e >> 1]);
-            // SiLU(g) = g (1 + tanh(g / 2)) / 2: one MUFU op instead of ex2 + rcp.  tanh.approx
-            // (relative error ~2^-11) keeps the output within half a bf16 ulp of the row's RMS.
-            float th;
-            asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(0.5f * gt));
-            y[e] = o * inv * sOnw[col0 + 8 * j + e] * (0.5f * gt) * (1.f + th);
-          } else {
-            y[e] = o;
+        if (p.fuse_epilogue) {
+          // SiLU(g) = h + h tanh(h), h = g / 2, on bf16 pairs (the gate is bf16 and the product is rounded to
+          // bf16): three packed ops per pair; the norm and the weight stay in f32.
+          #pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            uint32_t hh, th, sl;
+            const uint32_t g2 = reinterpret_cast<const uint32_t*>(&graw[j])[e2];
+            asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hh) : "r"(g2), "r"(0x3f003f00u));
+            asm("tanh.approx.bf16x2 %0, %1;" : "=r"(th) : "r"(hh));
+            asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(sl) : "r"(hh), "r"(th), "r"(hh));
+            const float s0 = __uint_as_float(sl << 16), s1 = __uint_as_float(sl & 0xffff0000u);
+            y[2 * e2] = ov[8 * j + 2 * e2] * inv * sOnw[col0 + 8 * j + 2 * e2] * s0;
+            y[2 * e2 + 1] = ov[8 * j + 2 * e2 + 1] * inv * sOnw[col0 + 8 * j + 2 * e2 + 1] * s1;
           }
+        } else {
+          #pragma unroll
+          for (int e = 0; e < 8; ++e) y[e] = ov[8 * j + e];
         }
         uint4 pk;
         pk.x = umma::pack_bf16x2(y[0], y[1]); pk.y = umma::pack_bf16x2(y[2], y[3]);
