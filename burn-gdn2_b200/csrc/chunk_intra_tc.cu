@@ -38,12 +38,9 @@ constexpr uint32_t AQK_IMG = 36864;     // bf16 K-major [64][64]
 constexpr uint32_t TINV_IMG = 45056;    // bf16 K-major [64][64]
 constexpr uint32_t SCRATCH = 53248;     // 6 x f32 [16][20] blocks of the inverse
 constexpr uint32_t RK = R1_END;         // bf16 MN-major [64][128]
-constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][VMAX]
-// after RV: half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem base
-template <int VMAX>
-constexpr uint32_t MISC = RV + 128 * VMAX;
-template <int VMAX>
-constexpr uint32_t TOTAL = MISC<VMAX> + 4096 + 512 + 64;
+constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][128]: rhs_v of (up to) 128 value channels
+constexpr uint32_t MISC = RV + 16384;   // half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem base
+constexpr uint32_t TOTAL = MISC + 4096 + 512 + 64;
 }  // namespace intra_smem
 
 // Loads of the kernel's read-only inputs.  Written as non-volatile asm
@@ -96,17 +93,20 @@ __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
   return make_uint2(umma::pack_bf16x2(a, b), umma::pack_bf16x2(c, d));
 }
 
-// VMAX = 128: V in {64, 128}, two CTAs per SM (256 TMEM columns each).
-// VMAX = 256: V = 256, one CTA per SM (rhs_v is 32 KB, U takes 256 TMEM
-// columns next to W's 128); lane l also owns value channels 128 + 4l .. +3.
+// VMAX = 128: V in {64, 128}.  VMAX = 256: V = 256 in the same footprint (two
+// CTAs per SM, 256 TMEM columns): U's first 128 columns come out of the
+// W / U MMA pair as for V = 128; then rhs_v of channels 128..255 is rebuilt
+// in the same shared tile from a second read of v and w (prefetched to L2
+// with the CTA's other inputs) and a second MMA writes U's upper half into
+// W's TMEM columns once W has been read out.
 template <int VMAX>
-__global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcParams p) {
+__global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   using namespace intra_smem;
-  constexpr uint32_t TCOLS = VMAX > 128 ? 512 : 256;  // TMEM columns: W [0, 128), U [128, 128 + V)
+  constexpr uint32_t TCOLS = 256;                     // TMEM columns: W [0, 128), U [128, 256)
   constexpr int NL = VMAX > 128 ? 18 : 14;            // 128-byte input lines per token
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
-  float* sHalf = reinterpret_cast<float*>(sm + MISC<VMAX>);  // [8][128] g sums of each 8-row half tile
+  float* sHalf = reinterpret_cast<float*>(sm + MISC);  // [8][128] g sums of each 8-row half tile
   float* sGlast = sHalf + 8 * 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGlast + 128);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
@@ -143,7 +143,6 @@ __global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcPa
   const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
   // inputs of row r0 + i, fetched one row ahead of their use in step 2
   uint2 nq, nk, nb, nv = make_uint2(0u, 0u), nw = make_uint2(0u, 0u);
-  uint2 nv2 = make_uint2(0u, 0u), nw2 = make_uint2(0u, 0u);  // value channels 128 + ch (VMAX = 256)
   float4 ng = make_float4(0.f, 0.f, 0.f, 0.f);
   auto fetch = [&](int i) {
     const int r = r0 + i;
@@ -155,10 +154,6 @@ __global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcPa
     if (ch < V) {
       nv = ld4_raw(p.v, bb, hv, t0 + r, ch, ok);
       nw = ld4_raw(p.w, bb, hv, t0 + r, ch, ok);
-    }
-    if (VMAX > 128) {
-      nv2 = ld4_raw(p.v, bb, hv, t0 + r, ch + 128, ok);
-      nw2 = ld4_raw(p.w, bb, hv, t0 + r, ch + 128, ok);
     }
   };
   fetch(0);
@@ -239,7 +234,7 @@ __global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcPa
     #pragma unroll 2
     for (int i = 0; i < 8; ++i) {
       const int r = r0 + i;
-      const uint2 cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw, cvv2 = nv2, cw2 = nw2;
+      const uint2 cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw;
       if (r < cv) {
         gl[0] += ng.x; gl[1] += ng.y; gl[2] += ng.z; gl[3] += ng.w;
       }
@@ -269,12 +264,6 @@ __global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcPa
       *reinterpret_cast<uint2*>(kdr + ro) = pack4(kd[0], kd[1], kd[2], kd[3]);
       *reinterpret_cast<uint2*>(rkr + ro) = pack4(rk[0], rk[1], rk[2], rk[3]);
       if (ch < V) *reinterpret_cast<uint2*>(rvr + ro) = pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
-      if (VMAX > 128) {  // channels 128 + ch: MN-major groups 2, 3 (two groups of 64 K rows x 128 bytes further)
-        float v2[4], w2[4];
-        unpack4(cvv2, v2);
-        unpack4(cw2, w2);
-        *reinterpret_cast<uint2*>(rvr + 2 * 64 * 128 + ro) = pack4(w2[0] * v2[0], w2[1] * v2[1], w2[2] * v2[2], w2[3] * v2[3]);
-      }
       #pragma unroll
       for (int pp = 0; pp < 4; ++pp) {
         if (pp < tp) continue;
@@ -447,7 +436,7 @@ __global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcPa
   if (tid == 0) {
     const uint32_t sbase = smem_u32(sm);
     const uint32_t iw = umma::idesc_bf16(64, 128, false, true);
-    const uint32_t iu = umma::idesc_bf16(64, V, false, true);
+    const uint32_t iu = umma::idesc_bf16(64, VMAX > 128 ? 128 : V, false, true);
     #pragma unroll
     for (int j = 0; j < 4; ++j)
       umma::mma_bf16(tA, umma::desc_kmaj(sbase + TINV_IMG, 64, j), umma::desc_mnmaj(sbase + RK, 64, j), iw, j > 0);
@@ -483,23 +472,65 @@ __global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcPa
         *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, col / 8 + 1, 128)) = hi;
       }
     }
-    for (int c16 = 0; c16 < V / 32; ++c16) {
-      const int col = half * (V / 2) + 16 * c16;
-      float v[16];
-      umma::ld16(umma::taddr(tA, 32 * sp, 128 + col), v);
-      umma::wait_ld();
-      if (lane < 16) {
-        const int sl = col / p.vt, cc = col % p.vt;
-        uint4 lo, hi;
-        lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
-        lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
-        hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
-        hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
-        // 16-byte chunk j of a U row is stored at chunk j ^ (row & 7)
-        uint4* urow = reinterpret_cast<uint4*>(rec + L.u + ((size_t)sl * 64 * p.vt + (size_t)r * p.vt) * 2);
-        urow[(cc / 8) ^ (r & 7)] = lo;
-        urow[(cc / 8 + 1) ^ (r & 7)] = hi;
+    // U columns [u0, u0 + n) from TMEM columns tcol .. tcol + n (this warp's column half) to the record
+    auto store_u = [&](uint32_t tcol, int u0, int n) {
+      for (int c16 = 0; c16 < n / 32; ++c16) {
+        const int lc = half * (n / 2) + 16 * c16;
+        const int col = u0 + lc;
+        float v[16];
+        umma::ld16(umma::taddr(tA, 32 * sp, tcol + lc), v);
+        umma::wait_ld();
+        if (lane < 16) {
+          const int sl = col / p.vt, cc = col % p.vt;
+          uint4 lo, hi;
+          lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
+          lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
+          hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
+          hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
+          // 16-byte chunk j of a U row is stored at chunk j ^ (row & 7)
+          uint4* urow = reinterpret_cast<uint4*>(rec + L.u + ((size_t)sl * 64 * p.vt + (size_t)r * p.vt) * 2);
+          urow[(cc / 8) ^ (r & 7)] = lo;
+          urow[(cc / 8 + 1) ^ (r & 7)] = hi;
+        }
       }
+    };
+    store_u(128, 0, VMAX > 128 ? 128 : V);  // the first U MMA's columns
+    if (VMAX > 128) {
+      // ---- 8. U columns 128..255: rhs_v of value channels 128 + ch rebuilt in RV (the first U MMA has read
+      // it), then one more MMA into W's TMEM columns, which were read out above ----
+      uint2 v8[8], w8[8];
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = r0 + i;
+        v8[i] = ld4_raw(p.v, bb, hv, t0 + rr, ch + 128, rr < cv);
+        w8[i] = ld4_raw(p.w, bb, hv, t0 + rr, ch + 128, rr < cv);
+      }
+      const int cx = (ch & 63) >> 3, kb = ch >> 6, eb = (ch & 7) * 2, rg = r0 >> 3;
+      unsigned char* const rvr = sm + RV + kb * 64 * 128 + rg * 1024 + eb;  // as in step 2
+      #pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float vv[4], ww[4];
+        unpack4(v8[i], vv);
+        unpack4(w8[i], ww);
+        *reinterpret_cast<uint2*>(rvr + i * 128 + ((cx ^ i) << 4)) =
+            pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
+      }
+      fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      umma::fence_after_sync();
+      if (tid == 0) {
+        const uint32_t sbase = smem_u32(sm);
+        const uint32_t iu = umma::idesc_bf16(64, 128, false, true);
+        #pragma unroll
+        for (int j = 0; j < 4; ++j)
+          umma::mma_bf16(tA, umma::desc_kmaj(sbase + TINV_IMG, 64, j), umma::desc_mnmaj(sbase + RV, 64, j), iu,
+                         j > 0);
+        umma::commit(&bars[1]);
+      }
+      mbar_wait_bounded(&bars[1], 1);
+      umma::fence_after_sync();
+      store_u(0, 128, 128);
     }
   }
   umma::fence_before_sync();
@@ -509,7 +540,7 @@ __global__ void __launch_bounds__(256, VMAX > 128 ? 1 : 2) k_intra_tc(const TcPa
 
 template <int VMAX>
 static int launch_intra_tc_v(const TcParams& p, cudaStream_t st) {
-  const size_t smem = intra_smem::TOTAL<VMAX> + 1024;
+  const size_t smem = intra_smem::TOTAL + 1024;
   cudaError_t e =
       cudaFuncSetAttribute((const void*)k_intra_tc<VMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "chunk intra (tc) smem attribute");
