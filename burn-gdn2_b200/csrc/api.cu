@@ -99,7 +99,6 @@ static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, 
   p.state = a->state;
   p.rec = static_cast<unsigned char*>(ws);
   p.rec_bytes = tc_record_layout(d.head_v_dim).bytes;
-  p.o_ws = nullptr;
   return GDN2_OK;
 }
 

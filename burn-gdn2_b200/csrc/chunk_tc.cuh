@@ -47,7 +47,6 @@ struct TcParams {
   float* state;
   unsigned char* rec;  // NC records per (b, hv), record bytes each
   size_t rec_bytes;
-  float* o_ws;         // raw o [B,HV,T,V] f32 when the epilogue runs separately
 };
 
 int launch_intra_tc(const TcParams& p, cudaStream_t st);
