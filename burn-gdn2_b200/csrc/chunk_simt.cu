@@ -20,6 +20,11 @@
 namespace gdn2 {
 
 constexpr int SIMT_THREADS = 256;
+// Row stride (floats) of the intra kernel's [KS][CP] operand arrays: a warp
+// writes 32 consecutive channels of one row, so a stride of CP = 64 would put
+// all 32 stores in one bank; 68 keeps rows 16-byte aligned for the float4
+// reads and leaves 4-way conflicts.
+constexpr int CPS = CP + 4;
 
 // ---------------------------------------------------------------------------
 // chunk-intra: one CTA per (chunk, hv, b)
@@ -27,10 +32,10 @@ constexpr int SIMT_THREADS = 256;
 template <typename T>
 __global__ void __launch_bounds__(SIMT_THREADS, 2) k_intra_simt(const ChunkParams p) {
   extern __shared__ float sm[];
-  float* sQs = sm;                  // [KS][CP]  q E
-  float* sKx = sQs + KS * CP;       // [KS][CP]  k / E
-  float* sBs = sKx + KS * CP;       // [KS][CP]  b k E
-  float* seb = sBs + KS * CP;       // [4][4][KS] exp(min(Gb_p - Gb_q, 0))
+  float* sQs = sm;                  // [KS][CPS]  q E
+  float* sKx = sQs + KS * CPS;      // [KS][CPS]  k / E
+  float* sBs = sKx + KS * CPS;      // [KS][CPS]  b k E
+  float* seb = sBs + KS * CPS;      // [4][4][KS] exp(min(Gb_p - Gb_q, 0))
   float* sTot = seb + 16 * KS;      // [4][KS] tile sums of g
   float* sGl = sTot + 4 * KS;       // [KS] G at the last valid row
   float* sA = sGl + KS;             // [CP][CP+1] Akk
@@ -98,9 +103,9 @@ __global__ void __launch_bounds__(SIMT_THREADS, 2) k_intra_simt(const ChunkParam
       const float E = expf(gl[i]);
       const float G = gb + gl[i];
       const float gam = expf(G);
-      sQs[kk * CP + r] = qv * E;
-      sKx[kk * CP + r] = kv / E;
-      sBs[kk * CP + r] = bv * kv * E;
+      sQs[kk * CPS + r] = qv * E;
+      sKx[kk * CPS + r] = kv / E;
+      sBs[kk * CPS + r] = bv * kv * E;
       if (kval) {
         gW[r * K + kc] = bv * kv * gam;
         gQg[r * K + kc] = qv * gam * p.scale;
@@ -112,9 +117,9 @@ __global__ void __launch_bounds__(SIMT_THREADS, 2) k_intra_simt(const ChunkParam
       const float* eb = seb + ((r0 >> 4) * 4 + (s0 >> 4)) * KS;
       #pragma unroll 4
       for (int j = 0; j < KS; ++j) {
-        const float4 a = *reinterpret_cast<const float4*>(sQs + j * CP + r0);
-        const float4 bq = *reinterpret_cast<const float4*>(sBs + j * CP + r0);
-        const float4 kx = *reinterpret_cast<const float4*>(sKx + j * CP + s0);
+        const float4 a = *reinterpret_cast<const float4*>(sQs + j * CPS + r0);
+        const float4 bq = *reinterpret_cast<const float4*>(sBs + j * CPS + r0);
+        const float4 kx = *reinterpret_cast<const float4*>(sKx + j * CPS + s0);
         const float e = eb[j];
         const float av[4] = {a.x * e, a.y * e, a.z * e, a.w * e};
         const float bv[4] = {bq.x * e, bq.y * e, bq.z * e, bq.w * e};
@@ -354,7 +359,7 @@ __global__ void __launch_bounds__(256) k_chunk_out(const ChunkParams p) {
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
-size_t simt_smem_intra() { return sizeof(float) * (3 * KS * CP + 16 * KS + 4 * KS + KS + CP * (CP + 1)); }
+size_t simt_smem_intra() { return sizeof(float) * (3 * KS * CPS + 16 * KS + 4 * KS + KS + CP * (CP + 1)); }
 
 template <int VT>
 static size_t smem_inter(int K) {
