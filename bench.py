@@ -296,7 +296,9 @@ def run_ours(args):
         others = {"cfg4_core": run_core_cfg(torch, bg, ops, dev, stream, CFG4, "config 4", max_over_ranks, world,
                                             seed=4000 + 10 * rank),
                   "cfg5_core": run_core_cfg(torch, bg, ops, dev, stream, CFG5, "config 5", max_over_ranks, world,
-                                            seed=5000 + 10 * rank)}
+                                            seed=5000 + 10 * rank),
+                  # the config-5 layer split by heads over the N ranks (strong scaling, all-reduce timed apart)
+                  "cfg5_layer_head_sharded": run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world)}
 
     # ---- roofline of the dominant kernel ----
     peaks = load_peaks()
@@ -431,6 +433,66 @@ def run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world):
             "workload": f"GatedDeltaNet2.forward_train, BASELINE config 2, 16 heads split over {world} GPUs",
             "allreduce_ms": ar_ms, "allreduce_bytes": nbytes,
             "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / (ar_ms / 1e3) / 1e9}
+
+
+def layer_flops(tokens, D, H, K, HV, V, C):
+    """Dense FLOPs of one forward_train: the seven input projections (one concatenated GEMM: q, k, b with
+    D x H.K, v, w with D x HV.V, f / gate down-projections D x V), the two up-projections (V x H.K,
+    V x HV.V), o_proj (HV.V x D), and the chunk core."""
+    kd, vd = H * K, HV * V
+    proj = 2 * tokens * (3 * D * kd + 2 * D * vd + 2 * D * V + V * kd + V * vd + vd * D)
+    return proj + core_flops_per_token_head(K, V, C) * tokens * HV
+
+
+def run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world):
+    """BASELINE config 5 (hidden 4096, 32 x 128 heads, B = 2, T = 65536, bf16) as the head-sharded layer of
+    its definition: at N = 1 the whole layer, at N > 1 the layer split by heads over the N ranks (strong
+    scaling of one layer) with the one NCCL all-reduce of the o_proj partials [B, T, 4096] timed apart."""
+    B, T, D, H, K = 2, 65536, 4096, 32, 128
+    cfg = bg.Gdn2Config(hidden_size=D, num_heads=H, head_dim=K, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
+    full = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=7)
+    if world > 1:
+        from burn_gdn2 import sharding
+        W = {n: getattr(full, n).weight.detach().float().cpu() for n in
+             ("q_proj", "k_proj", "v_proj", "f_proj_0", "f_proj_1", "b_proj", "w_proj", "g_proj_0", "o_proj")}
+        W["g_proj_1_w"] = full.g_proj_1.weight.float().cpu()
+        W["g_proj_1_b"] = full.g_proj_1.bias.float().cpu()
+        for n, a in (("A_log", "a_log"), ("dt_bias", "dt_bias"), ("o_norm_w", "o_norm_weight"),
+                     ("q_conv_w", "q_conv_w"), ("k_conv_w", "k_conv_w"), ("v_conv_w", "v_conv_w")):
+            W[n] = getattr(full, a).float().cpu()
+        del full
+        m = sharding.ShardedGatedDeltaNet2(cfg, W, device=dev, dtype=torch.bfloat16)
+        del W
+    else:
+        m = full
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(B, T, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    for _ in range(2):
+        m.forward_train(x)
+    torch.cuda.synchronize()
+    n = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ar = 0.0
+    e0.record(stream)
+    for _ in range(n):
+        m.forward_train(x)
+        if world > 1:
+            ar += m.allreduce_ms()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    flops = layer_flops(B * T, D, H, K, H, K, 64)
+    out = {"value": B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
+           "workload": f"GatedDeltaNet2.forward_train, BASELINE config 5 (D=4096, 32x128 heads, B=2, T=65536, bf16), "
+                       f"heads split over {world} GPU(s)",
+           "tc_frac_of_all_gpus": flops / (ms / 1e3) / (load_peaks()["bf16_tflops"] * 1e12 * world)}
+    if world > 1:
+        nbytes = B * T * D * 2
+        ar_ms = max_over_ranks(ar / n)
+        out.update({"allreduce_ms": ar_ms, "allreduce_bytes": nbytes,
+                    "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / (ar_ms / 1e3) / 1e9})
+    del m, x
+    return out
 
 
 def run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world):
