@@ -60,6 +60,21 @@ __global__ void __launch_bounds__(SIMT_THREADS, 2) k_intra_simt(const ChunkParam
   const bool blk = s0 <= r0 + 3;
   const int lt = (cv - 1) >> 4, lr = (cv - 1) & 15;  // tile / row of the last valid token
 
+  // the CTA's input rows on their way to L2 before the first use: q, k, b, g (key head), v, w (value head)
+  {
+    const int es = sizeof(T);
+    for (int idx = tid; idx < 6 * CP * 8; idx += SIMT_THREADS) {
+      const int j = idx / (CP * 8), rem = idx % (CP * 8), r = rem / 8, seg = rem % 8;
+      if (r >= cv) continue;
+      const DView& v = j == 0 ? p.q : j == 1 ? p.k : j == 2 ? p.b : j == 3 ? p.g : j == 4 ? p.v : p.w;
+      const int h = j < 4 ? kh : hv;
+      const int e = j == 3 ? 4 : es;
+      const int width = (j < 4 ? K : V) * e;
+      if (seg * 128 >= width) continue;
+      const char* a0 = static_cast<const char*>(v.p) + ((int64_t)bb * v.s0 + (int64_t)h * v.s1 + (int64_t)(t0 + r) * v.s2) * e;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a0 + seg * 128));
+    }
+  }
   float aq[4][4], ak[4][4];
   #pragma unroll
   for (int i = 0; i < 4; ++i)
