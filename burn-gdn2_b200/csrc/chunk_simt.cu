@@ -244,7 +244,11 @@ __global__ void __launch_bounds__(SIMT_THREADS) k_inter_simt(const ChunkParams p
       }
     }
 
-    for (int idx = tid; idx < CP * CP; idx += SIMT_THREADS) sAq[(idx / CP) * (CP + 1) + idx % CP] = gAqk[idx];
+    for (int idx = tid; idx < CP * CP / 4; idx += SIMT_THREADS) {
+      const float4 a4 = reinterpret_cast<const float4*>(gAqk)[idx];
+      float* d = sAq + (4 * idx / CP) * (CP + 1) + (4 * idx) % CP;
+      d[0] = a4.x; d[1] = a4.y; d[2] = a4.z; d[3] = a4.w;
+    }
 
     float avn[RT][4], ao[RT][4];
     #pragma unroll
@@ -253,11 +257,26 @@ __global__ void __launch_bounds__(SIMT_THREADS) k_inter_simt(const ChunkParams p
       for (int j = 0; j < 4; ++j) avn[i][j] = ao[i][j] = 0.f;
 
     for (int k0 = 0; k0 < K; k0 += KS) {
-      for (int idx = tid; idx < CP * KS; idx += SIMT_THREADS) {
-        const int r = idx / KS, j = idx % KS;
-        const bool ok = k0 + j < K;
-        sW[r * (KS + 1) + j] = ok ? gW[r * K + k0 + j] : 0.f;
-        sQ[r * (KS + 1) + j] = ok ? gQg[r * K + k0 + j] : 0.f;
+      if (K % 4 == 0) {  // 16-byte loads (rows of K floats stay 16-byte aligned)
+        for (int idx = tid; idx < CP * KS / 4; idx += SIMT_THREADS) {
+          const int r = idx / (KS / 4), j = 4 * (idx % (KS / 4));
+          float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f), q4 = w4;
+          if (k0 + j < K) {
+            w4 = *reinterpret_cast<const float4*>(gW + r * K + k0 + j);
+            q4 = *reinterpret_cast<const float4*>(gQg + r * K + k0 + j);
+          }
+          float* dw = sW + r * (KS + 1) + j;
+          float* dq = sQ + r * (KS + 1) + j;
+          dw[0] = w4.x; dw[1] = w4.y; dw[2] = w4.z; dw[3] = w4.w;
+          dq[0] = q4.x; dq[1] = q4.y; dq[2] = q4.z; dq[3] = q4.w;
+        }
+      } else {
+        for (int idx = tid; idx < CP * KS; idx += SIMT_THREADS) {
+          const int r = idx / KS, j = idx % KS;
+          const bool ok = k0 + j < K;
+          sW[r * (KS + 1) + j] = ok ? gW[r * K + k0 + j] : 0.f;
+          sQ[r * (KS + 1) + j] = ok ? gQg[r * K + k0 + j] : 0.f;
+        }
       }
       __syncthreads();
       #pragma unroll 4
@@ -303,9 +322,19 @@ __global__ void __launch_bounds__(SIMT_THREADS) k_inter_simt(const ChunkParams p
     }
     // S <- diag(gamma_last) S + Kd^T v_new
     for (int k0 = 0; k0 < K; k0 += KS) {
-      for (int idx = tid; idx < CP * KS; idx += SIMT_THREADS) {
-        const int r = idx / KS, j = idx % KS;
-        sW[r * (KS + 1) + j] = (k0 + j < K) ? gKd[r * K + k0 + j] : 0.f;
+      if (K % 4 == 0) {
+        for (int idx = tid; idx < CP * KS / 4; idx += SIMT_THREADS) {
+          const int r = idx / (KS / 4), j = 4 * (idx % (KS / 4));
+          float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (k0 + j < K) k4 = *reinterpret_cast<const float4*>(gKd + r * K + k0 + j);
+          float* d = sW + r * (KS + 1) + j;
+          d[0] = k4.x; d[1] = k4.y; d[2] = k4.z; d[3] = k4.w;
+        }
+      } else {
+        for (int idx = tid; idx < CP * KS; idx += SIMT_THREADS) {
+          const int r = idx / KS, j = idx % KS;
+          sW[r * (KS + 1) + j] = (k0 + j < K) ? gKd[r * K + k0 + j] : 0.f;
+        }
       }
       __syncthreads();
       float acc[RT][4];
