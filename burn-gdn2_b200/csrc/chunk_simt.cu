@@ -400,6 +400,62 @@ __global__ void __launch_bounds__(256) k_chunk_out(const ChunkParams p) {
   }
 }
 
+// The same with 4 consecutive columns per lane (16-byte o loads, 8- or 16-byte
+// gate / out accesses): taken when the gate and out rows are aligned for it.
+__device__ __forceinline__ void ld4(const float* p, float (&x)[4]) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+__device__ __forceinline__ void ld4(const __nv_bfloat16* p, float (&x)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  x[0] = __uint_as_float(u.x << 16); x[1] = __uint_as_float(u.x & 0xffff0000u);
+  x[2] = __uint_as_float(u.y << 16); x[3] = __uint_as_float(u.y & 0xffff0000u);
+}
+__device__ __forceinline__ void st4(float* p, const float (&y)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(y[0], y[1], y[2], y[3]);
+}
+__device__ __forceinline__ void st4(__nv_bfloat16* p, const float (&y)[4]) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(y[0], y[1]), b = __floats2bfloat162_rn(y[2], y[3]);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_chunk_out4(const ChunkParams p) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int64_t nrows = (int64_t)p.B * p.HV * p.T;
+  if (row >= nrows) return;
+  const int t = (int)(row % p.T);
+  const int hv = (int)((row / p.T) % p.HV);
+  const int bb = (int)(row / ((int64_t)p.T * p.HV));
+  const float* o = p.ws_o + row * p.V;
+  float ss = 0.f;
+  for (int c = 4 * lane; c < p.V; c += 128) {
+    float x[4];
+    ld4(o + c, x);
+    ss += x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+  }
+  #pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rms = sqrtf(ss / (float)p.V + p.eps);
+  const T* gp = static_cast<const T*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 + (int64_t)t * p.gate.s2;
+  T* op = static_cast<T*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 + (int64_t)t * p.out.s2;
+  for (int c = 4 * lane; c < p.V; c += 128) {
+    float x[4], y[4];
+    ld4(o + c, x);
+    if (p.fuse_epilogue) {
+      float g[4];
+      ld4(gp + c, g);
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = x[e] / rms * p.onw[c + e] * silu_f(g[e]);
+    } else {
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = x[e];
+    }
+    st4(op + c, y);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
@@ -456,10 +512,19 @@ int launch_inter_simt(const ChunkParams& p, cudaStream_t st) {
 int launch_chunk_out(const ChunkParams& p, int dtype, cudaStream_t st) {
   const int64_t nrows = (int64_t)p.B * p.HV * p.T;
   dim3 grid((unsigned)((nrows + 7) / 8));
-  if (dtype == GDN2_DTYPE_BF16)
-    k_chunk_out<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
-  else
-    k_chunk_out<float><<<grid, 256, 0, st>>>(p);
+  // 4-column accesses need every gate / out row start aligned to 4 elements (V % 4 == 0 already holds)
+  const int es = dtype == GDN2_DTYPE_BF16 ? 2 : 4;
+  auto rows4 = [&](const DView& v) {
+    return (uintptr_t)v.p % (4 * es) == 0 && v.s0 % 4 == 0 && v.s1 % 4 == 0 && v.s2 % 4 == 0;
+  };
+  const bool vec = rows4(p.out) && (!p.fuse_epilogue || rows4(p.gate));
+  if (dtype == GDN2_DTYPE_BF16) {
+    if (vec) k_chunk_out4<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+    else k_chunk_out<__nv_bfloat16><<<grid, 256, 0, st>>>(p);
+  } else {
+    if (vec) k_chunk_out4<float><<<grid, 256, 0, st>>>(p);
+    else k_chunk_out<float><<<grid, 256, 0, st>>>(p);
+  }
   return check_cuda(cudaGetLastError(), "chunk output launch");
 }
 
