@@ -642,8 +642,10 @@ __global__ void __launch_bounds__(WIDE_WARPS * 32, 2) k_prologue_wide(const ProP
   const int per = 4 * NQ + 2 * NV;
   const int64_t nw = (int64_t)gridDim.x * WIDE_WARPS;
   for (int64_t task = (int64_t)blockIdx.x * WIDE_WARPS + warp; task < ntask; task += nw) {
-    int u = (int)(task % per);
     const int64_t bt = task / per;
+    // the slice order rotated by the block index, so that a warp's successive tasks (task ids nw apart) do
+    // not keep landing on the same stream kinds, whose costs differ (L2-normalised conv, conv, sigmoid, softplus)
+    int u = (int)((task % per + bt) % per);
     const int t0 = (int)(bt % nfull) * PRO_ROWS, bb = (int)(bt / nfull);
     if (u < 2 * NQ + NV) {  // q, k, v
       const int s = u < NQ ? 0 : u < 2 * NQ ? 1 : 2;
