@@ -14,9 +14,12 @@ sigmoid gates, g = -A dt with A in [1,16], dt in [1e-3, 0.1]); they are
 Printed (rank 0, one JSON line): tokens/s of the device-resident core
 (`value`), the same through the C ABI from pinned host buffers (`e2e`),
 the roofline of the dominant kernel, the decode step of BASELINE config 3
-(B = 256, one token, state [256,16,128,128] f32) as `decode`, the CPU
-baseline (numpy restatement of the crate's tensor path on the host cores)
-and SM clocks sampled during the timed region.
+(B = 256, one token, state [256,16,128,128] f32) as `decode`, the config-2
+layer (`layer`: projections + core + o_proj, against the tensor-core peak),
+the config-2 core in f32 (`f32`), BASELINE configs 4 and 5 (`other_configs`:
+their chunk cores, and config 5 as its head-sharded layer over the N ranks),
+the CPU baseline (numpy restatement of the crate's tensor path on the host
+cores) and SM clocks sampled during the timed region.
 
 Multi-GPU (torchrun, one rank per GPU): (batch x value-head) chains are
 independent, so each rank runs its own partition of config-2 chains
