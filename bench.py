@@ -31,9 +31,7 @@ import ctypes
 import json
 import math
 import os
-import subprocess
 import sys
-import tempfile
 import threading
 import time
 

@@ -166,7 +166,6 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(RuntimeError):
         bg.chunk_wy_forward(q, q, v, q, q, v, torch.zeros(1, 1, 16, 16), 0.25, 64)
     cfg = bg.Gdn2Config(hidden_size=32, num_heads=2, head_dim=16)
-    import numpy as np
     import gdn2_oracle as O
     m = bg.GatedDeltaNet2(cfg, O.init_weights(O.Gdn2Config(hidden_size=32, num_heads=2, head_dim=16)), device="cpu")
     with pytest.raises(RuntimeError):

@@ -1,7 +1,6 @@
 """GPU: the tcgen05 building blocks (shared-memory descriptors for K-major
 and MN-major 128-byte-swizzled tiles, M = 64 and M = 128 TMEM accumulator
 layouts) against a host matmul of the same bf16-rounded operands."""
-import ctypes
 
 import pytest
 import torch
