@@ -262,10 +262,11 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
 
     // MMA1: D = [W; Qg] S
     if (tid == 0) {
+      const uint64_t dwq = umma::desc_kmaj_base(sbase + s * STAGE + ST_WQ);
+      const uint64_t dsi = umma::desc_mnmaj_base(sbase + S_IMG, TC_K);
       #pragma unroll
       for (int j = 0; j < 8; ++j)
-        umma::mma_bf16(tD, umma::desc_kmaj(sbase + s * STAGE + ST_WQ, 128, j),
-                       umma::desc_mnmaj(sbase + S_IMG, TC_K, j), i1, j > 0);
+        umma::mma_bf16(tD, umma::desc_kmaj_at(dwq, 128, j), umma::desc_mnmaj_at(dsi, j), i1, j > 0);
       umma::commit(&bars[2]);
     }
     // meanwhile: S <- diag(gamma_last) S in TMEM (all warps), then the
@@ -343,14 +344,15 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
     if (tid == 0) {
       mbar_wait_bounded(&bars[4], c & 1);
       umma::fence_after_sync();
+      const uint64_t dta = umma::desc_kmaj_base(sbase + s * STAGE + ST_TA);
+      const uint64_t dkd = umma::desc_mnmaj_base(sbase + s * STAGE + ST_KD, TC_C);
+      const uint64_t dvn = umma::desc_mnmaj_base(sbase + VN_IMG, TC_C);
       #pragma unroll
       for (int j = 0; j < 4; ++j)
-        umma::mma_bf16(tD, umma::desc_kmaj(sbase + s * STAGE + ST_TA, 128, j),
-                       umma::desc_mnmaj(sbase + VN_IMG, TC_C, j), i1, true);
+        umma::mma_bf16(tD, umma::desc_kmaj_at(dta, 128, j), umma::desc_mnmaj_at(dvn, j), i1, true);
       #pragma unroll
       for (int j = 0; j < 4; ++j)
-        umma::mma_bf16(tS, umma::desc_mnmaj(sbase + s * STAGE + ST_KD, TC_C, j),
-                       umma::desc_mnmaj(sbase + VN_IMG, TC_C, j), i3, true);
+        umma::mma_bf16(tS, umma::desc_mnmaj_at(dkd, j), umma::desc_mnmaj_at(dvn, j), i3, true);
       umma::commit(&bars[3]);
     }
     mbar_wait_bounded(&bars[3], c & 1);

@@ -20,7 +20,8 @@
 //  5. Aqk (scaled, causal) and Akk (strict) back from TMEM; (I + Akk)^-1 by
 //     blocked forward substitution over 16x16 tiles (forward.rs:192-261).
 //  6. Two M=64 MMAs: W = (I+Akk)^-1 rhs_k, U = (I+Akk)^-1 rhs_v.
-//  7. The record (chunk_tc.cuh) is written as operand-tile images.
+//  7. The record (chunk_tc.cuh) is written as operand-tile images; W and U
+//     are staged in shared memory and leave in bulk copies.
 #include "chunk_tc.cuh"
 #include "umma.cuh"
 
@@ -37,6 +38,10 @@ constexpr uint32_t TINV = 17408;        // f32 [64][SS]
 constexpr uint32_t AQK_IMG = 36864;     // bf16 K-major [64][64]
 constexpr uint32_t TINV_IMG = 45056;    // bf16 K-major [64][64]
 constexpr uint32_t SCRATCH = 53248;     // 6 x f32 [16][20] blocks of the inverse
+// staging of the record's W and U images (step 7), once the solve's f32 tiles are dead
+constexpr uint32_t WST = 0;             // W rows 0..63: K-major [64][128], two 8 KB column blocks
+constexpr uint32_t UST = 16384;         // U, first value-column slice: [64][vt] rows (8 or 16 KB)
+constexpr uint32_t UST2 = AQK_IMG;      // U, second slice (V = 256), once Aqk and T^-1 images are used
 constexpr uint32_t RK = R1_END;         // bf16 MN-major [64][128]
 constexpr uint32_t RV = RK + 16384;     // bf16 MN-major [64][128]: rhs_v of (up to) 128 value channels
 constexpr uint32_t MISC = RV + 16384;   // half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem base
@@ -88,6 +93,31 @@ __device__ __forceinline__ void unpack4(uint2 raw, float (&x)[4]) {
   x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
 }
 
+// Pairs of f32 in one 64-bit register for the packed sm_100 multiply
+// (mul.rn.f32x2: two IEEE round-to-nearest products per instruction, the
+// same results as two scalar multiplies).  The operand build of step 2 works
+// on the lane's channels in pairs (c, c + 1), as they arrive in bf16x2 words.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 f2pk(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ f32x2 f2mul(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// bf16 pair (lower channel in the low half) -> f32 pair, exact
+__device__ __forceinline__ f32x2 bf2f2(uint32_t u) {
+  return f2pk(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+// f32 pair -> bf16 pair, round to nearest even
+__device__ __forceinline__ uint32_t f2bf2(f32x2 r) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+  return umma::pack_bf16x2(lo, hi);
+}
 
 __device__ __forceinline__ uint2 pack4(float a, float b, float c, float d) {
   return make_uint2(umma::pack_bf16x2(a, b), umma::pack_bf16x2(c, d));
@@ -226,6 +256,16 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
       cks[pp][j] = __expf(gbpp - Gbp[j]);
     }
   }
+  // the same constants as channel pairs (2m, 2m + 1)
+  f32x2 eGbp2[2], eGbpS2[2], edk2[2], cks2[4][2];
+  #pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    eGbp2[m] = f2pk(eGbp[2 * m], eGbp[2 * m + 1]);
+    eGbpS2[m] = f2pk(eGbpS[2 * m], eGbpS[2 * m + 1]);
+    edk2[m] = f2pk(edk[2 * m], edk[2 * m + 1]);
+    #pragma unroll
+    for (int pp = 0; pp < 4; ++pp) cks2[pp][m] = f2pk(cks[pp][2 * m], cks[pp][2 * m + 1]);
+  }
   {
     // Every store of row r0 + i lands at (lane base of its tile) + i * 128 + ((cx ^ i) << 4): rows r0 .. r0 + 7
     // form one 8-row group of every 128-byte-swizzled tile (r0 is a multiple of 8), and the lane's channel
@@ -250,36 +290,38 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
         gl[0] += ng.x; gl[1] += ng.y; gl[2] += ng.z; gl[3] += ng.w;
       }
       if (i + 1 < 8) fetch(i + 1);
-      float q[4], k[4], b[4], vv[4], ww[4];
-      unpack4(cq, q);
-      unpack4(ck, k);
-      unpack4(cb, b);
-      unpack4(cvv, vv);
-      unpack4(cw, ww);
-      float qs[4], bks[4], qg[4], rk[4], kd[4], kinv[4];
+      // bf16 pairs of q e^gl, b k e^gl, Qg, Kd, rhs_k, rhs_v; k e^-gl kept in f32 for the Ks_pp of step 2
+      uint32_t oq[2], ob[2], og[2], od[2], ork[2], ov[2];
+      f32x2 kinv2s[2];
       #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float e = __expf(gl[j]);
-        const float ei = __expf(-gl[j]);
-        qs[j] = q[j] * e;
-        bks[j] = b[j] * k[j] * e;
-        qg[j] = qs[j] * eGbpS[j];
-        rk[j] = bks[j] * eGbp[j];
-        kinv[j] = k[j] * ei;
-        kd[j] = kinv[j] * edk[j];
+      for (int m = 0; m < 2; ++m) {
+        const f32x2 q2 = bf2f2(m ? cq.y : cq.x), k2 = bf2f2(m ? ck.y : ck.x), b2 = bf2f2(m ? cb.y : cb.x);
+        const f32x2 v2 = bf2f2(m ? cvv.y : cvv.x), w2 = bf2f2(m ? cw.y : cw.x);
+        const f32x2 e2 = f2pk(__expf(gl[2 * m]), __expf(gl[2 * m + 1]));
+        const f32x2 ei2 = f2pk(__expf(-gl[2 * m]), __expf(-gl[2 * m + 1]));
+        const f32x2 qs2 = f2mul(q2, e2);
+        const f32x2 bks2 = f2mul(f2mul(b2, k2), e2);
+        const f32x2 kinv2 = f2mul(k2, ei2);
+        oq[m] = f2bf2(qs2);
+        ob[m] = f2bf2(bks2);
+        og[m] = f2bf2(f2mul(qs2, eGbpS2[m]));
+        ork[m] = f2bf2(f2mul(bks2, eGbp2[m]));
+        od[m] = f2bf2(f2mul(kinv2, edk2[m]));
+        ov[m] = f2bf2(f2mul(w2, v2));
+        kinv2s[m] = kinv2;
       }
       const uint32_t ro = i * 128 + ((cx ^ i) << 4);
-      *reinterpret_cast<uint2*>(xq + ro) = pack4(qs[0], qs[1], qs[2], qs[3]);
-      *reinterpret_cast<uint2*>(xb + ro) = pack4(bks[0], bks[1], bks[2], bks[3]);
-      *reinterpret_cast<uint2*>(wqr + ro) = pack4(qg[0], qg[1], qg[2], qg[3]);
-      *reinterpret_cast<uint2*>(kdr + ro) = pack4(kd[0], kd[1], kd[2], kd[3]);
-      *reinterpret_cast<uint2*>(rkr + ro) = pack4(rk[0], rk[1], rk[2], rk[3]);
-      if (ch < V) *reinterpret_cast<uint2*>(rvr + ro) = pack4(ww[0] * vv[0], ww[1] * vv[1], ww[2] * vv[2], ww[3] * vv[3]);
+      *reinterpret_cast<uint2*>(xq + ro) = make_uint2(oq[0], oq[1]);
+      *reinterpret_cast<uint2*>(xb + ro) = make_uint2(ob[0], ob[1]);
+      *reinterpret_cast<uint2*>(wqr + ro) = make_uint2(og[0], og[1]);
+      *reinterpret_cast<uint2*>(kdr + ro) = make_uint2(od[0], od[1]);
+      *reinterpret_cast<uint2*>(rkr + ro) = make_uint2(ork[0], ork[1]);
+      if (ch < V) *reinterpret_cast<uint2*>(rvr + ro) = make_uint2(ov[0], ov[1]);
       #pragma unroll
       for (int pp = 0; pp < 4; ++pp) {
         if (pp < tp) continue;
         *reinterpret_cast<uint2*>(ksr[pp] + ro) =
-            pack4(kinv[0] * cks[pp][0], kinv[1] * cks[pp][1], kinv[2] * cks[pp][2], kinv[3] * cks[pp][3]);
+            make_uint2(f2bf2(f2mul(kinv2s[0], cks2[pp][0])), f2bf2(f2mul(kinv2s[1], cks2[pp][1])));
       }
     }
   }
@@ -296,13 +338,15 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   if (tid == 0) {
     const uint32_t idesc = umma::idesc_bf16(64, 32, false, false);
     const uint32_t sbase = smem_u32(sm);
+    const uint64_t dks = umma::desc_kmaj_base(sbase + KSV), dxs = umma::desc_kmaj_base(sbase + X);
     #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
-      const uint32_t ks = sbase + KSV + 4096 * (pp * (pp + 1) / 2);
-      const uint32_t xs = sbase + X + pp * 8192;
+      const uint64_t ks = umma::desc_add(dks, 4096 * (pp * (pp + 1) / 2));
+      const uint64_t xs = umma::desc_add(dxs, pp * 8192);
       #pragma unroll
       for (int j = 0; j < 8; ++j)
-        umma::mma_bf16(tA + 32 * pp, umma::desc_kmaj(ks, 16 * (pp + 1), j), umma::desc_kmaj(xs, 32, j), idesc, j > 0);
+        umma::mma_bf16(tA + 32 * pp, umma::desc_kmaj_at(ks, 16 * (pp + 1), j), umma::desc_kmaj_at(xs, 32, j), idesc,
+                       j > 0);
     }
     umma::commit(&bars[0]);
   }
@@ -448,13 +492,14 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     const uint32_t sbase = smem_u32(sm);
     const uint32_t iw = umma::idesc_bf16(64, 128, false, true);
     const uint32_t iu = umma::idesc_bf16(64, VMAX > 128 ? 128 : V, false, true);
+    const uint64_t dt = umma::desc_kmaj_base(sbase + TINV_IMG);
+    const uint64_t drk = umma::desc_mnmaj_base(sbase + RK, 64), drv = umma::desc_mnmaj_base(sbase + RV, 64);
     #pragma unroll
     for (int j = 0; j < 4; ++j)
-      umma::mma_bf16(tA, umma::desc_kmaj(sbase + TINV_IMG, 64, j), umma::desc_mnmaj(sbase + RK, 64, j), iw, j > 0);
+      umma::mma_bf16(tA, umma::desc_kmaj_at(dt, 64, j), umma::desc_mnmaj_at(drk, j), iw, j > 0);
     #pragma unroll
     for (int j = 0; j < 4; ++j)
-      umma::mma_bf16(tA + 128, umma::desc_kmaj(sbase + TINV_IMG, 64, j), umma::desc_mnmaj(sbase + RV, 64, j), iu,
-                     j > 0);
+      umma::mma_bf16(tA + 128, umma::desc_kmaj_at(dt, 64, j), umma::desc_mnmaj_at(drv, j), iu, j > 0);
     umma::commit(&bars[1]);
   }
   // Aqk image to the record while the MMAs run
@@ -463,7 +508,9 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
   mbar_wait_bounded(&bars[1], 0);
   umma::fence_after_sync();
 
-  // ---- 7. W and U to the record (warp w: sub-partition w % 4, column half w / 4) ----
+  // ---- 7. W and U to the record (warp w: sub-partition w % 4, column half w / 4): TMEM -> bf16 images in
+  // shared memory -> bulk copies, so the record is written in 8-16 KB runs (a direct store from the TMEM
+  // layout writes 16 bytes into each of 16 rows per instruction) ----
   {
     const int sp = warp & 3, half = warp >> 2;
     const int r = 16 * sp + lane;  // valid for lane < 16
@@ -479,33 +526,41 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
         lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
         hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
         hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
-        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, col / 8, 128)) = lo;
-        *reinterpret_cast<uint4*>(rec + L.wq + umma::kmaj_chunk(r, col / 8 + 1, 128)) = hi;
+        *reinterpret_cast<uint4*>(sm + WST + umma::kmaj_chunk(r, col / 8, 64)) = lo;
+        *reinterpret_cast<uint4*>(sm + WST + umma::kmaj_chunk(r, col / 8 + 1, 64)) = hi;
       }
     }
-    // U columns [u0, u0 + n) from TMEM columns tcol .. tcol + n (this warp's column half) to the record
-    auto store_u = [&](uint32_t tcol, int u0, int n) {
+    // n columns of one value-column slice from TMEM columns tcol .. tcol + n (this warp's half of them) to
+    // the slice image at `ust`: rows of n bf16, 16-byte chunk j of row r at chunk j ^ (r & 7)
+    auto stage_u = [&](uint32_t ust, uint32_t tcol, int n) {
       for (int c16 = 0; c16 < n / 32; ++c16) {
         const int lc = half * (n / 2) + 16 * c16;
-        const int col = u0 + lc;
         float v[16];
         umma::ld16(umma::taddr(tA, 32 * sp, tcol + lc), v);
         umma::wait_ld();
         if (lane < 16) {
-          const int sl = col / p.vt, cc = col % p.vt;
           uint4 lo, hi;
           lo.x = umma::pack_bf16x2(v[0], v[1]); lo.y = umma::pack_bf16x2(v[2], v[3]);
           lo.z = umma::pack_bf16x2(v[4], v[5]); lo.w = umma::pack_bf16x2(v[6], v[7]);
           hi.x = umma::pack_bf16x2(v[8], v[9]); hi.y = umma::pack_bf16x2(v[10], v[11]);
           hi.z = umma::pack_bf16x2(v[12], v[13]); hi.w = umma::pack_bf16x2(v[14], v[15]);
-          // 16-byte chunk j of a U row is stored at chunk j ^ (row & 7)
-          uint4* urow = reinterpret_cast<uint4*>(rec + L.u + ((size_t)sl * 64 * p.vt + (size_t)r * p.vt) * 2);
-          urow[(cc / 8) ^ (r & 7)] = lo;
-          urow[(cc / 8 + 1) ^ (r & 7)] = hi;
+          uint4* urow = reinterpret_cast<uint4*>(sm + ust + (size_t)r * n * 2);
+          urow[(lc / 8) ^ (r & 7)] = lo;
+          urow[(lc / 8 + 1) ^ (r & 7)] = hi;
         }
       }
     };
-    store_u(128, 0, VMAX > 128 ? 128 : V);  // the first U MMA's columns
+    constexpr int NU = VMAX > 128 ? 128 : 0;  // first slice width (V for VMAX = 128)
+    const int nu = NU ? NU : V;
+    stage_u(UST, 128, nu);  // the first U MMA's columns
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      bulk_s2g(rec + L.wq, sm + WST, 8192u);
+      bulk_s2g(rec + L.wq + 16384, sm + WST + 8192, 8192u);
+      bulk_s2g(rec + L.u, sm + UST, (unsigned)(64 * nu * 2));
+      bulk_commit();
+    }
     if (VMAX > 128) {
       // ---- 8. U columns 128..255: rhs_v of value channels 128 + ch rebuilt in RV (the first U MMA has read
       // it), then one more MMA into W's TMEM columns, which were read out above ----
@@ -533,19 +588,27 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
       if (tid == 0) {
         const uint32_t sbase = smem_u32(sm);
         const uint32_t iu = umma::idesc_bf16(64, 128, false, true);
+        const uint64_t dt = umma::desc_kmaj_base(sbase + TINV_IMG), drv = umma::desc_mnmaj_base(sbase + RV, 64);
         #pragma unroll
         for (int j = 0; j < 4; ++j)
-          umma::mma_bf16(tA, umma::desc_kmaj(sbase + TINV_IMG, 64, j), umma::desc_mnmaj(sbase + RV, 64, j), iu,
-                         j > 0);
+          umma::mma_bf16(tA, umma::desc_kmaj_at(dt, 64, j), umma::desc_mnmaj_at(drv, j), iu, j > 0);
         umma::commit(&bars[1]);
       }
       mbar_wait_bounded(&bars[1], 1);
       umma::fence_after_sync();
-      store_u(0, 128, 128);
+      stage_u(UST2, 0, 128);  // U columns 128..255: the second slice
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        bulk_s2g(rec + L.u + 64 * 128 * 2, sm + UST2, 64u * 128u * 2u);
+        bulk_commit();
+      }
     }
   }
   umma::fence_before_sync();
   __syncthreads();
+  if (tid == 0) bulk_wait_read_all();  // the staged images stay in place until the bulk copies have read them
+  __syncwarp();
   if (warp == 0) umma::tmem_dealloc(tA, TCOLS);
 }
 

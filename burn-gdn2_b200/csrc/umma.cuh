@@ -69,6 +69,22 @@ __device__ __forceinline__ uint64_t desc_mnmaj(uint32_t tile_saddr, int KD, int 
   return desc_sw128(tile_saddr + (uint32_t)(j * 2048), (uint32_t)(KD * 128), 1024);
 }
 
+// The descriptor of the same layout `off_bytes` further on: only the start-address field (address >> 4, the low
+// 14 bits) changes, and shared-memory addresses stay below 2^18 bytes, so the sum never carries out of that field.
+// One add per MMA instead of rebuilding every field.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t off_bytes) {
+  return (d & 0xFFFFFFFF00000000ull) | (uint64_t)((uint32_t)d + (off_bytes >> 4));
+}
+__device__ __forceinline__ uint64_t desc_kmaj_base(uint32_t tile_saddr) { return desc_sw128(tile_saddr, 16, 1024); }
+__device__ __forceinline__ uint64_t desc_mnmaj_base(uint32_t tile_saddr, int KD) {
+  return desc_sw128(tile_saddr, (uint32_t)(KD * 128), 1024);
+}
+// k-step j of a K-major [R][KD] tile / an MN-major [KD][N] tile, from its base descriptor
+__device__ __forceinline__ uint64_t desc_kmaj_at(uint64_t base, int R, int j) {
+  return desc_add(base, (uint32_t)((j >> 2) * R * 128 + (j & 3) * 32));
+}
+__device__ __forceinline__ uint64_t desc_mnmaj_at(uint64_t base, int j) { return desc_add(base, (uint32_t)(j * 2048)); }
+
 // kind::f16 instruction descriptor: bf16 x bf16 -> f32
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                       // D format f32
