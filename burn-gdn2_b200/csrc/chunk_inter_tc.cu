@@ -201,10 +201,16 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       if (16 * c16 < HALF)
         umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), *reinterpret_cast<float(*)[16]>(ov + 16 * c16));
     umma::wait_ld();
-    float s4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
+    f32x2 s2[2] = {0ull, 0ull};  // four independent chains, as two pairs
     #pragma unroll
-    for (int j = 0; j < 64; ++j)
-      if (j < HALF) s4[j & 3] += ov[j] * ov[j];
+    for (int j = 0; j < 64; j += 2)
+      if (j < HALF) {
+        const f32x2 o2 = f2pk(ov[j], ov[j + 1]);
+        s2[(j >> 1) & 1] = f2fma(o2, o2, s2[(j >> 1) & 1]);
+      }
+    float s4[4];
+    f2un(s2[0], s4[0], s4[1]);
+    f2un(s2[1], s4[2], s4[3]);
     const float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
     sRms[orow * 2 + half] = ss;
     named_bar(1, 128);
@@ -217,6 +223,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
       tot += sXsum[par * 64 + orow];
     }
     const float inv = rsqrtf(tot / (float)VF + p.eps);
+    const f32x2 inv2 = f2pk(inv, inv);
     named_bar(1, 128);  // sRms reusable
     if (orow < cv) {
       __nv_bfloat16* op = static_cast<__nv_bfloat16*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
@@ -235,9 +242,10 @@ __global__ void __launch_bounds__(256, 1) k_inter_tc(const TcParams p) {
             asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hh) : "r"(g2), "r"(0x3f003f00u));
             asm("tanh.approx.bf16x2 %0, %1;" : "=r"(th) : "r"(hh));
             asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(sl) : "r"(hh), "r"(th), "r"(hh));
-            const float s0 = __uint_as_float(sl << 16), s1 = __uint_as_float(sl & 0xffff0000u);
-            y[2 * e2] = ov[8 * j + 2 * e2] * inv * sOnw[col0 + 8 * j + 2 * e2] * s0;
-            y[2 * e2 + 1] = ov[8 * j + 2 * e2 + 1] * inv * sOnw[col0 + 8 * j + 2 * e2 + 1] * s1;
+            const f32x2 s01 = f2pk(__uint_as_float(sl << 16), __uint_as_float(sl & 0xffff0000u));
+            const f32x2 w01 = *reinterpret_cast<const f32x2*>(sOnw + col0 + 8 * j + 2 * e2);
+            const f32x2 o01 = f2pk(ov[8 * j + 2 * e2], ov[8 * j + 2 * e2 + 1]);
+            f2un(f2mul(f2mul(f2mul(o01, inv2), w01), s01), y[2 * e2], y[2 * e2 + 1]);
           }
         } else {
           #pragma unroll

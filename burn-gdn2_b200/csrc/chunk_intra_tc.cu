@@ -93,21 +93,8 @@ __device__ __forceinline__ void unpack4(uint2 raw, float (&x)[4]) {
   x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
 }
 
-// Pairs of f32 in one 64-bit register for the packed sm_100 multiply
-// (mul.rn.f32x2: two IEEE round-to-nearest products per instruction, the
-// same results as two scalar multiplies).  The operand build of step 2 works
-// on the lane's channels in pairs (c, c + 1), as they arrive in bf16x2 words.
-typedef unsigned long long f32x2;
-__device__ __forceinline__ f32x2 f2pk(float lo, float hi) {
-  f32x2 r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ f32x2 f2mul(f32x2 a, f32x2 b) {
-  f32x2 r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
+// The operand build of step 2 works on the lane's channels in pairs (c, c + 1), as they arrive in bf16x2
+// words, with the packed f32x2 multiply (ptx.cuh).
 // bf16 pair (lower channel in the low half) -> f32 pair, exact
 __device__ __forceinline__ f32x2 bf2f2(uint32_t u) {
   return f2pk(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
@@ -115,7 +102,7 @@ __device__ __forceinline__ f32x2 bf2f2(uint32_t u) {
 // f32 pair -> bf16 pair, round to nearest even
 __device__ __forceinline__ uint32_t f2bf2(f32x2 r) {
   float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+  f2un(r, lo, hi);
   return umma::pack_bf16x2(lo, hi);
 }
 
