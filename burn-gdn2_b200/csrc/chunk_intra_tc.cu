@@ -393,12 +393,17 @@ __global__ void __launch_bounds__(256, 2) k_intra_tc(const TcParams p) {
     auto XS = [&](int k) { return scr + k * 16 * 20; };
     // acc += a_block[row][:] * b_block[:][c0 .. c0 + 3]
     auto mac = [&](float (&acc)[4], const float* a, int as, const float* b, int bs) {
+      f32x2 a01 = f2pk(acc[0], acc[1]), a23 = f2pk(acc[2], acc[3]);
       #pragma unroll
       for (int m = 0; m < 16; ++m) {
         const float x = a[row * as + m];
-        const float4 y = *reinterpret_cast<const float4*>(b + m * bs + c0);
-        acc[0] += x * y.x; acc[1] += x * y.y; acc[2] += x * y.z; acc[3] += x * y.w;
+        const f32x2* y = reinterpret_cast<const f32x2*>(b + m * bs + c0);
+        const f32x2 x2 = f2pk(x, x);
+        a01 = f2fma(x2, y[0], a01);
+        a23 = f2fma(x2, y[1], a23);
       }
+      f2un(a01, acc[0], acc[1]);
+      f2un(a23, acc[2], acc[3]);
     };
     auto put = [&](float* d, int ds, const float (&acc)[4], float sg) {
       *reinterpret_cast<float4*>(d + row * ds + c0) = make_float4(sg * acc[0], sg * acc[1], sg * acc[2], sg * acc[3]);
