@@ -1,4 +1,4 @@
-"""CPU, world_size 2 and 4 over gloo: head sharding of one layer.  Each rank runs
+"""CPU, world_size 2, 4 and 8 over gloo: head sharding of one layer.  Each rank runs
 the oracle layer on its shard of the weights; the all-reduce (sum) of the
 row-parallel o_proj partials must equal the unsharded layer (forward_train
 and a stateful forward), including GVA groups."""
@@ -55,6 +55,7 @@ def _worker(rank, world, port, cfgd, seed, q):
     (dict(hidden_size=64, num_heads=2, head_dim=16, num_v_heads=4, expand_v=2.0, mode="chunk", min_decay=0.9,
           allow_neg_eigval=True), 2),
     (dict(hidden_size=64, num_heads=4, head_dim=16, mode="chunk"), 4),
+    (dict(hidden_size=128, num_heads=8, head_dim=16, mode="chunk"), 8),  # the bench's widest split (N = 8)
 ])
 def test_head_sharded_layer_matches_unsharded(cfgd, world):
     ctx = mp.get_context("spawn")
