@@ -65,8 +65,11 @@ class ShardedGatedDeltaNet2:
     Each rank holds a GatedDeltaNet2 of H/N key heads (and HV/N value heads)
     built from `shard_weights`; `forward_train` / `forward` return the full
     output after one all-reduce (sum) of the row-parallel o_proj partials.
-    `last_allreduce_ms` records the all-reduce alone (CUDA events on the
-    current stream), so it can be reported separately.
+    Every all-reduce is bracketed by CUDA events on the current stream and
+    nothing waits on them here, so a timed loop of layer calls never stalls
+    the host; `pop_allreduce_ms()` (after the caller has synchronised) returns
+    the all-reduce time of each call since the last pop, so it can be
+    reported separately.
     """
 
     def __init__(self, cfg, weights: dict, group=None, device="cuda", dtype=None, **kw):
@@ -82,7 +85,7 @@ class ShardedGatedDeltaNet2:
         self.config = cfg
         self.local = GatedDeltaNet2(shard_config(cfg, self.world), shard_weights(weights, cfg, self.rank, self.world),
                                     device=device, dtype=dtype or torch.float32, **kw)
-        self.last_allreduce_ms = None
+        self._events = []
 
     def _reduce(self, y):
         import torch
@@ -91,13 +94,16 @@ class ShardedGatedDeltaNet2:
         e0.record()
         self.dist.all_reduce(y, op=self.dist.ReduceOp.SUM, group=self.group)
         e1.record()
-        self._events = (e0, e1)
+        self._events.append((e0, e1))
         return y
 
-    def allreduce_ms(self):
-        e0, e1 = self._events
-        e1.synchronize()
-        return e0.elapsed_time(e1)
+    def pop_allreduce_ms(self):
+        """All-reduce times (ms) of the calls since the last pop, oldest
+        first.  Call after the work has completed (e.g. after
+        torch.cuda.synchronize()); it does not wait itself."""
+        out = [e0.elapsed_time(e1) for e0, e1 in self._events]
+        self._events = []
+        return out
 
     def forward_train(self, x):
         return self._reduce(self.local.forward_train(x))

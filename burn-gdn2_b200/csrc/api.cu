@@ -190,7 +190,11 @@ int gdn2_read_device_errors(uint32_t* flags) {
 }
 
 size_t gdn2_chunk_fwd_workspace_bytes(const gdn2_chunk_args* a) {
-  if (!a || a->chunk_size <= 0 || a->dims.batch <= 0 || a->dims.seq_len <= 0) return 0;
+  if (!a || a->chunk_size <= 0) return 0;
+  const gdn2_dims& d = a->dims;
+  if (d.batch <= 0 || d.seq_len <= 0 || d.num_heads <= 0 || d.num_v_heads <= 0 || d.head_k_dim <= 0 ||
+      d.head_v_dim <= 0)
+    return 0;
   if (use_tc(a)) return tc_workspace_bytes(a->dims);
   const int C = a->chunk_size < CP ? a->chunk_size : CP;
   return chunk_workspace_layout(a->dims.batch, a->dims.num_v_heads, a->dims.seq_len, a->dims.head_k_dim,
@@ -249,6 +253,13 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream)
 int gdn2_chunk_fwd_noalloc(const gdn2_chunk_args* a, void* stream) {
   const char* fn = "gdn2_chunk_fwd_noalloc";
   if (!a) return set_error(GDN2_EINVAL, "%s: null args", fn);
+  // argument errors are reported as such before the size check (a bad dim
+  // must not read as "scratch too small")
+  int rc = check_dims(a->dims, fn);
+  if (rc) return rc;
+  if (a->dtype != GDN2_DTYPE_F32 && a->dtype != GDN2_DTYPE_BF16)
+    return set_error(GDN2_EINVAL, "%s: unknown dtype %d", fn, a->dtype);
+  if (a->chunk_size <= 0) return set_error(GDN2_EINVAL, "%s: chunk_size must be > 0, got %d", fn, a->chunk_size);
   const size_t need = gdn2_chunk_fwd_workspace_bytes(a);
   if (need > GDN2_NOALLOC_SCRATCH_BYTES)
     return set_error(GDN2_EWORKSPACE,
@@ -256,7 +267,7 @@ int gdn2_chunk_fwd_noalloc(const gdn2_chunk_args* a, void* stream) {
                      "call gdn2_chunk_fwd with a workspace",
                      fn, need, (size_t)GDN2_NOALLOC_SCRATCH_BYTES);
   void* ws = nullptr;
-  int rc = noalloc_scratch(&ws, fn);
+  rc = noalloc_scratch(&ws, fn);
   if (rc) return rc;
   return gdn2_chunk_fwd(a, ws, GDN2_NOALLOC_SCRATCH_BYTES, stream);
 }

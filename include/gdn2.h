@@ -131,12 +131,21 @@ GDN2_API int gdn2_chunk_inter(const gdn2_chunk_args* args, void* workspace, size
  * the device.
  *
  * The workspace is one file-scope device array of
- * GDN2_NOALLOC_SCRATCH_BYTES, a separate copy on each device.  The first
- * call on a device looks up that copy's address (cudaGetSymbolAddress, with
- * the device current) and caches it; make that first call before any
- * stream capture on the device.  A call that needs more scratch than the
- * array holds (gdn2_chunk_fwd_workspace_bytes > GDN2_NOALLOC_SCRATCH_BYTES)
- * returns GDN2_EWORKSPACE and launches nothing.
+ * GDN2_NOALLOC_SCRATCH_BYTES, a separate copy on each device.  Like any
+ * module-scope device variable it is reserved on a device whenever the
+ * library's code is loaded there (at the first launch of any of its
+ * kernels with lazy module loading, at context creation with
+ * CUDA_MODULE_LOADING=EAGER), whether or not this entry point is ever
+ * called, and held until the process exits.  The first call on a device
+ * looks up that copy's address (cudaGetSymbolAddress, with the device
+ * current) and caches it per device number; make that first call before
+ * any stream capture on the device.  The cache assumes the runtime's
+ * primary context: after cudaDeviceReset, or when the caller switches to
+ * another context of the same device, the cached address is stale.  A
+ * call that needs more scratch than the array holds
+ * (gdn2_chunk_fwd_workspace_bytes > GDN2_NOALLOC_SCRATCH_BYTES) returns
+ * GDN2_EWORKSPACE and launches nothing; argument errors (a dim <= 0, an
+ * unknown dtype) return GDN2_EINVAL before that size check.
  *
  * Every call on a device shares the one array, and it keeps the last
  * call's contents: no byte of it needs to start at zero, since each call

@@ -452,8 +452,8 @@ class Gdn2Layer:
             if conv_out is not None:
                 state.conv_q, state.conv_k, state.conv_v = conv_out
         else:
-            # read-only: o_t = scale * q_t^T S (state untouched); see DESIGN.md
-            # for the reference's double permute at src/module.rs:307/:310.
+            # read-only: o_t = scale * q_t^T S (state untouched), the evident intent
+            # of src/module.rs:297-308, whose output is permuted twice (:307, :310).
             o = p["q"] @ rec * scale
         return self._epilogue(o, p["gate"]), state
 

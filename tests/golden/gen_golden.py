@@ -15,7 +15,7 @@ first N (x, y) pairs as ``.npz``.  Two extra fixture sets patch the module
 constants before building the layer (allow_neg_eigval on; a K=64 head
 config with longer sequences that reach the crate's chunk path).
 
-Usage: python tests/golden/gen_golden.py [/path/to/reference]
+Usage: python tests/golden/gen_golden.py <reference checkout>   (or GDN2_REFERENCE_ROOT=<checkout>)
 Runs on CPU in a few seconds.  The GPU box never runs it.
 """
 import importlib.util
@@ -82,7 +82,9 @@ def dump(mod, name, n_cases, seq_fn, patch):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GDN2_REFERENCE_ROOT")
+    if not ref_root:
+        sys.exit("usage: gen_golden.py <reference checkout> (or set GDN2_REFERENCE_ROOT)")
     base = dict(D=64, H=4, HK=16, HV=4, EXPAND_V=1.5, USE_SHORT_CONV=True, ALLOW_NEG_EIGVAL=False)
     # 1) the reference's own fixture stream (first 42 of its 1000 cases:
     #    every combination of i % 6 and i % 7, T in 2..70)

@@ -135,6 +135,12 @@ def test_chunk_fwd_noalloc_size_limit():
     assert LIB.gdn2_chunk_fwd_noalloc(ctypes.byref(a), None) == _lib.GDN2_EWORKSPACE
     msg = LIB.gdn2_last_error().decode()
     assert msg.startswith("gdn2_chunk_fwd_noalloc") and str(32 << 20) in msg
+    # a negative dim is an argument error, not a scratch-size one
+    a.dims = _lib.Dims(1, 64, 1, -16, 16, 16)
+    assert LIB.gdn2_chunk_fwd_workspace_bytes(ctypes.byref(a)) == 0
+    assert LIB.gdn2_chunk_fwd_noalloc(ctypes.byref(a), None) == _lib.GDN2_EINVAL
+    a.dims = _lib.Dims(1, 64, 1, 1, -128, 16)
+    assert LIB.gdn2_chunk_fwd_noalloc(ctypes.byref(a), None) == _lib.GDN2_EINVAL
 
 
 def test_recurrent_argument_errors():
