@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, "libgdn2_b200.so")
 
 GDN2_OK, GDN2_EINVAL, GDN2_EUNSUPPORTED, GDN2_ECUDA, GDN2_EWORKSPACE = range(5)
 GDN2_DTYPE_F32, GDN2_DTYPE_BF16 = 0, 1
+GDN2_PRECISION_F32, GDN2_PRECISION_BF16 = 0, 1
 
 _STATUS = {1: "EINVAL", 2: "EUNSUPPORTED", 3: "ECUDA", 4: "EWORKSPACE"}
 
@@ -42,7 +43,8 @@ class ChunkArgs(ctypes.Structure):
                 ("key_heads_grouped", ctypes.c_int32), ("fuse_epilogue", ctypes.c_int32),
                 ("scale", ctypes.c_float), ("norm_eps", ctypes.c_float),
                 ("q", View), ("k", View), ("v", View), ("g", View), ("b", View), ("w", View),
-                ("gate", View), ("o_norm_weight", ctypes.c_void_p), ("state", ctypes.c_void_p), ("out", View)]
+                ("gate", View), ("o_norm_weight", ctypes.c_void_p), ("state", ctypes.c_void_p), ("out", View),
+                ("precision", ctypes.c_int32)]
 
 
 class RecurrentArgs(ctypes.Structure):

@@ -28,8 +28,8 @@ import torch
 from . import _lib
 from ._lib import LIB, check
 from .config import Gdn2Config, Gdn2Mode
-from .ops import (SHORT_CONV_CACHE, chunk_args, chunk_workspace, project_activations, recurrent_args,
-                  rms_norm_gate_per_head, stream_handle)
+from .ops import (SHORT_CONV_CACHE, chunk_args, chunk_workspace, precision_code, project_activations,
+                  recurrent_args, rms_norm_gate_per_head, stream_handle)
 
 FUSED_RECURRENT_MAX_SEQ = 64  # src/module.rs:17
 
@@ -90,10 +90,13 @@ class GatedDeltaNet2:
     NAMES = ("q_proj", "k_proj", "v_proj", "f_proj_0", "f_proj_1", "b_proj", "w_proj", "g_proj_0", "g_proj_1_w",
              "g_proj_1_b", "A_log", "dt_bias", "o_norm_w", "o_proj", "q_conv_w", "k_conv_w", "v_conv_w")
 
-    def __init__(self, cfg: Gdn2Config, weights: dict, device="cuda", dtype=torch.float32, gva_mode="reference"):
+    def __init__(self, cfg: Gdn2Config, weights: dict, device="cuda", dtype=torch.float32, gva_mode="reference",
+                 precision="f32"):
         cfg.validate()
         if gva_mode not in ("reference", "grouped"):
             raise ValueError("gva_mode must be 'reference' or 'grouped'")
+        precision_code(precision)
+        self.precision = precision
         self.config = cfg
         self.device = torch.device(device)
         self.dtype = dtype
@@ -228,7 +231,7 @@ class GatedDeltaNet2:
         out = torch.empty(B, T, hv, V, dtype=p.v.dtype, device=p.v.device)
         a = chunk_args(p.q, p.k, p.v, p.g, p.b, p.w, state, out.permute(0, 2, 1, 3), K ** -0.5,
                        self.config.chunk_size, num_heads=h, grouped=p.grouped, gate=p.gate.permute(0, 2, 1, 3),
-                       o_norm_weight=p.o_norm, norm_eps=p.eps)
+                       o_norm_weight=p.o_norm, norm_eps=p.eps, precision=self.precision)
         ws = chunk_workspace(a, p.v.device)
         check(LIB.gdn2_chunk_fwd(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ws.numel(),
                                  stream_handle(p.v.device)))

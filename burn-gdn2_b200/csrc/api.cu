@@ -9,6 +9,7 @@
 
 #include "chunk.cuh"
 #include "chunk_tc.cuh"
+#include "chunk_x3.cuh"
 #include "common.cuh"
 
 namespace gdn2 {
@@ -35,6 +36,8 @@ unsigned read_device_errors_recurrent();
 unsigned read_device_errors_selftest();
 unsigned read_device_errors_intra_tc();
 unsigned read_device_errors_inter_tc();
+unsigned read_device_errors_intra_x3();
+unsigned read_device_errors_inter_x3();
 int selftest_umma(int test, const float* A, const float* B, float* D, cudaStream_t st);
 int launch_short_conv(int B, int Tn, int C, int dtype, const void* x, const float* w, const float* cin, float* cout,
                       void* y, cudaStream_t st);
@@ -56,34 +59,59 @@ static int check_dims(const gdn2_dims& d, const char* fn) {
 static bool mult(int64_t x, int m) { return x % m == 0; }
 static bool align_ok(const void* ptr, int bytes) { return ((uintptr_t)ptr % bytes) == 0; }
 
-// The tensor-core path: bf16, K = 128, V in {64, 128, 256}, 64-token chunks, and
-// views whose rows allow its vector accesses (8-byte q/k/b/v/w, 16-byte g,
-// gate and out).  Everything else runs on the CUDA-core path.
-static bool use_tc(const gdn2_chunk_args* a) {
-  const gdn2_dims& d = a->dims;
-  const int C = a->chunk_size < CP ? a->chunk_size : CP;
-  if (!tc_supported(d.head_k_dim, d.head_v_dim, C, a->dtype)) return false;
+// Views whose rows allow the tensor-core kernels' vector accesses: four
+// q/k/b/v/w elements per load (8 bytes bf16, 16 bytes f32), 16-byte g,
+// gate and out pieces.
+static bool tc_views_ok(const gdn2_chunk_args* a) {
   auto v_ok = [&](const gdn2_view& v, int elems, int bytes) {
     return align_ok(v.data, bytes) && mult(v.stride0, elems) && mult(v.stride1, elems) && mult(v.stride2, elems);
   };
-  if (!v_ok(a->q, 4, 8) || !v_ok(a->k, 4, 8) || !v_ok(a->b, 4, 8) || !v_ok(a->v, 4, 8) || !v_ok(a->w, 4, 8))
+  const int in_b = a->dtype == GDN2_DTYPE_BF16 ? 8 : 16;   // bytes of four input elements
+  const int row_e = a->dtype == GDN2_DTYPE_BF16 ? 8 : 4;   // elements of 16 bytes
+  if (!v_ok(a->q, 4, in_b) || !v_ok(a->k, 4, in_b) || !v_ok(a->b, 4, in_b) || !v_ok(a->v, 4, in_b) ||
+      !v_ok(a->w, 4, in_b))
     return false;
-  if (!v_ok(a->g, 4, 16) || !v_ok(a->out, 8, 16)) return false;
-  if (a->fuse_epilogue && !v_ok(a->gate, 8, 16)) return false;
+  if (!v_ok(a->g, 4, 16) || !v_ok(a->out, row_e, 16)) return false;
+  if (a->fuse_epilogue && !v_ok(a->gate, row_e, 16)) return false;
   return true;
+}
+
+// The bf16-intermediate tensor-core path (GDN2_PRECISION_BF16): bf16 inputs,
+// K = 128, V in {64, 128, 256}, 64-token chunks.
+static bool use_tc(const gdn2_chunk_args* a) {
+  const gdn2_dims& d = a->dims;
+  const int C = a->chunk_size < CP ? a->chunk_size : CP;
+  if (a->precision != GDN2_PRECISION_BF16) return false;
+  if (!tc_supported(d.head_k_dim, d.head_v_dim, C, a->dtype)) return false;
+  return tc_views_ok(a);
+}
+
+// The split-operand tensor-core path (f32-grade intermediates): bf16 or f32
+// inputs, K = 128, V in {64, 128}, 64-token chunks.  Every other shape runs
+// on the exact-f32 CUDA-core path.
+static bool use_x3(const gdn2_chunk_args* a) {
+  const gdn2_dims& d = a->dims;
+  const int C = a->chunk_size < CP ? a->chunk_size : CP;
+  if (use_tc(a)) return false;
+  if (!x3_supported(d.head_k_dim, d.head_v_dim, C)) return false;
+  return tc_views_ok(a);
 }
 
 // Value columns per inter CTA: V <= 128 in one slice, V = 256 in two.
 static int tc_vt(int V) { return V > 128 ? 128 : V; }
 
-static size_t tc_workspace_bytes(const gdn2_dims& d) {
-  const size_t nch = (size_t)d.batch * d.num_v_heads * ((d.seq_len + TC_C - 1) / TC_C);
-  return nch * tc_record_layout(d.head_v_dim).bytes;
+static size_t rec_bytes(const gdn2_dims& d, bool x3) {
+  return x3 ? x3_record_layout(d.head_v_dim).bytes : tc_record_layout(d.head_v_dim).bytes;
 }
 
-static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, const char* fn) {
+static size_t tc_workspace_bytes(const gdn2_dims& d, bool x3) {
+  const size_t nch = (size_t)d.batch * d.num_v_heads * ((d.seq_len + TC_C - 1) / TC_C);
+  return nch * rec_bytes(d, x3);
+}
+
+static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, const char* fn, bool x3) {
   const gdn2_dims& d = a->dims;
-  const size_t need = tc_workspace_bytes(d);
+  const size_t need = tc_workspace_bytes(d, x3);
   if (wsb < need) return set_error(GDN2_EWORKSPACE, "%s: workspace %zu bytes < required %zu", fn, wsb, need);
   p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.V = d.head_v_dim;
   p.NC = (d.seq_len + TC_C - 1) / TC_C;
@@ -98,7 +126,7 @@ static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, 
   p.onw = a->o_norm_weight;
   p.state = a->state;
   p.rec = static_cast<unsigned char*>(ws);
-  p.rec_bytes = tc_record_layout(d.head_v_dim).bytes;
+  p.rec_bytes = rec_bytes(d, x3);
   return GDN2_OK;
 }
 
@@ -110,6 +138,8 @@ static int prep_chunk(const gdn2_chunk_args* a, void* ws, size_t wsb, ChunkParam
   if (a->dtype != GDN2_DTYPE_F32 && a->dtype != GDN2_DTYPE_BF16)
     return set_error(GDN2_EINVAL, "%s: unknown dtype %d", fn, a->dtype);
   if (a->chunk_size <= 0) return set_error(GDN2_EINVAL, "%s: chunk_size must be > 0, got %d", fn, a->chunk_size);
+  if (a->precision != GDN2_PRECISION_F32 && a->precision != GDN2_PRECISION_BF16)
+    return set_error(GDN2_EINVAL, "%s: unknown precision %d", fn, a->precision);
   if (!a->q.data || !a->k.data || !a->v.data || !a->g.data || !a->b.data || !a->w.data || !a->state ||
       !a->out.data)
     return set_error(GDN2_EINVAL, "%s: null tensor pointer", fn);
@@ -120,7 +150,7 @@ static int prep_chunk(const gdn2_chunk_args* a, void* ws, size_t wsb, ChunkParam
   const int C = a->chunk_size < CP ? a->chunk_size : CP;
   const ChunkWorkspace L = chunk_workspace_layout(d.batch, d.num_v_heads, d.seq_len, d.head_k_dim, d.head_v_dim, C);
   if (!ws) return set_error(GDN2_EINVAL, "%s: null workspace", fn);
-  if (!use_tc(a) && wsb < L.total * sizeof(float))
+  if (!use_tc(a) && !use_x3(a) && wsb < L.total * sizeof(float))
     return set_error(GDN2_EWORKSPACE, "%s: workspace %zu bytes < required %zu", fn, wsb, L.total * sizeof(float));
   if (((uintptr_t)ws & 255u) != 0) return set_error(GDN2_EINVAL, "%s: workspace must be 256-byte aligned", fn);
   p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.K = d.head_k_dim; p.V = d.head_v_dim;
@@ -185,7 +215,7 @@ int gdn2_read_device_errors(uint32_t* flags) {
   int rc = check_cuda(cudaDeviceSynchronize(), "gdn2_read_device_errors");
   if (rc) return rc;
   *flags = read_device_errors_recurrent() | read_device_errors_selftest() | read_device_errors_intra_tc() |
-           read_device_errors_inter_tc();
+           read_device_errors_inter_tc() | read_device_errors_intra_x3() | read_device_errors_inter_x3();
   return GDN2_OK;
 }
 
@@ -195,7 +225,9 @@ size_t gdn2_chunk_fwd_workspace_bytes(const gdn2_chunk_args* a) {
   if (d.batch <= 0 || d.seq_len <= 0 || d.num_heads <= 0 || d.num_v_heads <= 0 || d.head_k_dim <= 0 ||
       d.head_v_dim <= 0)
     return 0;
-  if (use_tc(a)) return tc_workspace_bytes(a->dims);
+  if (a->precision != GDN2_PRECISION_F32 && a->precision != GDN2_PRECISION_BF16) return 0;
+  if (use_tc(a)) return tc_workspace_bytes(a->dims, false);
+  if (use_x3(a)) return tc_workspace_bytes(a->dims, true);
   const int C = a->chunk_size < CP ? a->chunk_size : CP;
   return chunk_workspace_layout(a->dims.batch, a->dims.num_v_heads, a->dims.seq_len, a->dims.head_k_dim,
                                 a->dims.head_v_dim, C)
@@ -207,11 +239,12 @@ int gdn2_chunk_intra(const gdn2_chunk_args* a, void* ws, size_t wsb, void* strea
   ChunkParams p;
   int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_intra");
   if (rc) return rc;
-  if (use_tc(a)) {
+  const bool x3 = use_x3(a);
+  if (x3 || use_tc(a)) {
     TcParams t;
-    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_intra");
+    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_intra", x3);
     if (rc) return rc;
-    return launch_intra_tc(t, (cudaStream_t)stream);
+    return x3 ? launch_intra_x3(t, a->dtype, (cudaStream_t)stream) : launch_intra_tc(t, (cudaStream_t)stream);
   }
   return launch_intra_simt(p, a->dtype, (cudaStream_t)stream);
 }
@@ -220,11 +253,12 @@ int gdn2_chunk_inter(const gdn2_chunk_args* a, void* ws, size_t wsb, void* strea
   ChunkParams p;
   int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_inter");
   if (rc) return rc;
-  if (use_tc(a)) {
+  const bool x3 = use_x3(a);
+  if (x3 || use_tc(a)) {
     TcParams t;
-    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_inter");
+    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_inter", x3);
     if (rc) return rc;
-    return launch_inter_tc(t, (cudaStream_t)stream);
+    return x3 ? launch_inter_x3(t, a->dtype, (cudaStream_t)stream) : launch_inter_tc(t, (cudaStream_t)stream);
   }
   rc = launch_inter_simt(p, (cudaStream_t)stream);
   if (rc) return rc;
@@ -235,13 +269,14 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* ws, size_t wsb, void* stream)
   ChunkParams p;
   int rc = prep_chunk(a, ws, wsb, p, "gdn2_chunk_fwd");
   if (rc) return rc;
-  if (use_tc(a)) {
+  const bool x3 = use_x3(a);
+  if (x3 || use_tc(a)) {
     TcParams t;
-    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_fwd");
+    rc = prep_tc(a, ws, wsb, t, "gdn2_chunk_fwd", x3);
     if (rc) return rc;
-    rc = launch_intra_tc(t, (cudaStream_t)stream);
+    rc = x3 ? launch_intra_x3(t, a->dtype, (cudaStream_t)stream) : launch_intra_tc(t, (cudaStream_t)stream);
     if (rc) return rc;
-    return launch_inter_tc(t, (cudaStream_t)stream);
+    return x3 ? launch_inter_x3(t, a->dtype, (cudaStream_t)stream) : launch_inter_tc(t, (cudaStream_t)stream);
   }
   rc = launch_intra_simt(p, a->dtype, (cudaStream_t)stream);
   if (rc) return rc;

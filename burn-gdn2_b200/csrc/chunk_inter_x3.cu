@@ -1,0 +1,410 @@
+// Kernel (2), split-operand form: chunk-inter for bf16 or f32 inputs,
+// K = 128, C = 64, V in {64, 128}, with the SiLU-gated RMS-norm epilogue
+// fused, f32-grade intermediates (chunk_x3.cuh).
+//
+// Replaces gdn2_chunk_inter_kernel (src/kernel/chunk_cube.rs:300-610); math
+// of src/forward.rs:263-274 with the epilogue of src/module.rs:501-517.
+// One CTA (8 warps, one per SM) per (value head, batch) walks the chunks in
+// order.  The state S [K][V] stays in TMEM in f32 for the whole sequence;
+// its hi and lo bf16 images in shared memory are the MMA operands.  Per
+// chunk (every product as three MMAs: hi.hi + lo.hi + hi.lo):
+//   MMA1  D = [W; Qg] S                      (M=128, N=V, K=128)
+//   v_new = U - (W S)                        (rows 0..63 of D; U read from
+//                                             the record into registers)
+//   MMA2  D += [*; Aqk] v_new                (rows 64..127 become o; rows
+//                                             0..63 are dead and take
+//                                             whatever the 8 KB in front of
+//                                             the Aqk image hold)
+//   MMA3  S = diag(gamma_last) S + Kd^T v_new   (S pre-scaled in TMEM)
+//   o -> gated RMS norm -> out; S -> hi / lo images for the next chunk.
+// The record parts sit in one stage and are refilled as soon as they are
+// consumed: [W; Qg] (and gamma_last) once MMA1 completed, Aqk and Kd once
+// MMA2 and MMA3 completed, so each copy has the rest of a chunk to land.
+#include "chunk_x3.cuh"
+
+namespace gdn2 {
+
+namespace nx3 {
+constexpr uint32_t WQ = 0;          // WQ_HI, WQ_LO: K-major [128][128] each (the record's first 64 KB)
+constexpr uint32_t AQK = 65536;     // AQK_HI, AQK_LO [64][64], KD_HI, KD_LO MN-major [64][128]: 48 KB
+constexpr uint32_t AQK_LO = AQK + 8192;
+constexpr uint32_t KD_HI = AQK + 16384;
+constexpr uint32_t KD_LO = AQK + 32768;
+constexpr uint32_t GL = 114688;     // f32 [2][128], by chunk parity
+constexpr uint32_t S_HI = 115712;   // MN-major [128][V]
+constexpr uint32_t S_LO = S_HI + 32768;
+constexpr uint32_t VN_HI = S_LO + 32768;  // MN-major [64][V]
+constexpr uint32_t VN_LO = VN_HI + 16384;
+constexpr uint32_t RMS = VN_LO + 16384;   // f32 [64][2]
+constexpr uint32_t ONW = RMS + 512;       // f32 [V]
+constexpr uint32_t BARS = ONW + 512;
+constexpr uint32_t TOTAL = BARS + 128;
+}  // namespace nx3
+
+__device__ __forceinline__ void named_bar_x3(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// SiLU in f32: g sigma(g) with the MUFU exponential and a fast divide (a few ulp)
+__device__ __forceinline__ float silu_acc(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+template <typename TIN>
+__global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
+  using namespace nx3;
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
+  float* sRms = reinterpret_cast<float*>(sm + RMS);
+  float* sOnw = reinterpret_cast<float*>(sm + ONW);
+  const float* sGl = reinterpret_cast<const float*>(sm + GL);
+  // fullA (W, Qg, gamma_last), fullB (Aqk, Kd), mma1, mma2/3, operands ready
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
+
+  const int hv = blockIdx.y, bb = blockIdx.z;
+  const int V = p.V, HALF = V / 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sp = warp & 3, half = warp >> 2;
+  const int col0 = half * HALF;
+  const X3Record L = x3_record_layout(V);
+  const unsigned char* recs = p.rec + ((size_t)bb * p.HV + hv) * p.NC * p.rec_bytes;
+  float* st = p.state + ((size_t)bb * p.HV + hv) * (size_t)TC_K * V;
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) {
+    umma::tmem_alloc(tslot, 512);
+    umma::tmem_relinquish();
+  }
+  if (p.fuse_epilogue)
+    for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[i];
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&bars[4], 256);
+    fence_mbar_init();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tD0 = *tslot;       // D of even chunks: cols [0, V); odd chunks: [V, 2V)
+  const uint32_t tS = tD0 + 2 * V;   // S master: cols [2V, 3V)
+
+  auto issueA = [&](int c) {  // thread 0: [W; Qg] hi / lo and gamma_last of chunk c
+    const unsigned char* r = recs + (size_t)c * p.rec_bytes;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&bars[0], 65536u + 512u);
+    bulk_g2s(sm + WQ, r + L.wq_hi, 65536u, &bars[0]);
+    bulk_g2s(sm + GL + (c & 1) * 512, r + L.gl, 512u, &bars[0]);
+  };
+  auto issueB = [&](int c) {  // thread 0: Aqk and Kd hi / lo of chunk c
+    const unsigned char* r = recs + (size_t)c * p.rec_bytes;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&bars[1], 49152u);
+    bulk_g2s(sm + AQK, r + L.aqk_hi, 49152u, &bars[1]);
+  };
+  if (tid == 0) {
+    issueA(0);
+    issueB(0);
+  }
+
+  // ---- initial state: f32 master in TMEM, hi / lo images in smem ----
+  const int kk = 32 * sp + lane;  // key channel = TMEM lane of this thread
+  for (int c16 = 0; c16 < HALF / 16; ++c16) {
+    const int col = col0 + 16 * c16;
+    float v[16];
+    const float4* src = reinterpret_cast<const float4*>(st + (size_t)kk * V + col);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 f = src[j];
+      v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+    }
+    umma::st16(umma::taddr(tS, 32 * sp, col), v);
+    uint4 h0, l0, h1, l1;
+    split8(v, h0, l0);
+    split8(v + 8, h1, l1);
+    const uint32_t o0 = umma::mnmaj_chunk(kk, col / 8, TC_K), o1 = umma::mnmaj_chunk(kk, col / 8 + 1, TC_K);
+    *reinterpret_cast<uint4*>(sm + S_HI + o0) = h0;
+    *reinterpret_cast<uint4*>(sm + S_HI + o1) = h1;
+    *reinterpret_cast<uint4*>(sm + S_LO + o0) = l0;
+    *reinterpret_cast<uint4*>(sm + S_LO + o1) = l1;
+  }
+  umma::wait_st();
+  fence_proxy_async_smem();
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+
+  const uint32_t i1 = umma::idesc_bf16(128, V, false, true);  // [W;Qg] . S and [*;Aqk] . v_new
+  const uint32_t i3 = umma::idesc_bf16(128, V, true, true);   // Kd^T . v_new
+
+  // U row of this thread (sub-partitions 0, 1: row 32 sp + lane, this half's columns) in the record of chunk c;
+  // prefetched to L2 one chunk ahead, read into registers while MMA1 runs
+  auto u_row = [&](int c) {
+    return reinterpret_cast<const float4*>(recs + (size_t)c * p.rec_bytes + L.u +
+                                           ((size_t)(32 * sp + lane) * V + col0) * 4);
+  };
+  auto prefetch_u = [&](int c) {
+    const char* g = reinterpret_cast<const char*>(u_row(c));
+    for (int b = 0; b < HALF * 4; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + b));
+  };
+
+  // o rows of chunk c live in rows 64..127 of D[c & 1] (sub-partitions 2, 3);
+  // their epilogue runs while the tensor core does MMA1 of chunk c + 1.  The
+  // gate rows of a chunk are prefetched to L2 one chunk ahead and read into
+  // registers when its epilogue starts.
+  constexpr int GW = 64 * (int)sizeof(TIN) / 16;  // 16-byte gate words per row half
+  const int orow = 32 * (sp - 2) + lane;
+  auto gate_row = [&](int c) {
+    return reinterpret_cast<const uint4*>(static_cast<const TIN*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
+                                          (int64_t)(c * TC_C + orow) * p.gate.s2 + col0);
+  };
+  auto prefetch_gate = [&](int c) {
+    if (p.fuse_epilogue && orow < min(TC_C, p.T - c * TC_C)) {
+      const char* g = reinterpret_cast<const char*>(gate_row(c));
+      for (int b = 0; b < HALF * (int)sizeof(TIN); b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + b));
+    }
+  };
+  auto epilogue = [&](int c) {
+    const int t0 = c * TC_C;
+    const int cv = min(TC_C, p.T - t0);
+    const uint32_t tD = tD0 + (c & 1) * V;
+    uint4 graw[GW];
+    if (p.fuse_epilogue && orow < cv) {
+      const uint4* gp = gate_row(c);
+      #pragma unroll
+      for (int j = 0; j < GW; ++j)
+        if (j * 16 < HALF * (int)sizeof(TIN)) graw[j] = gp[j];
+    }
+    auto gate_at = [&](int j) -> float {  // gate element j of this row half
+      if constexpr (sizeof(TIN) == 2) {
+        const uint32_t w32 = reinterpret_cast<const uint32_t*>(graw)[j >> 1];
+        return __uint_as_float((j & 1) ? (w32 & 0xffff0000u) : (w32 << 16));
+      } else {
+        return reinterpret_cast<const float*>(graw)[j];
+      }
+    };
+    float ov[64];
+    #pragma unroll
+    for (int c16 = 0; c16 < 4; ++c16)
+      if (16 * c16 < HALF)
+        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), *reinterpret_cast<float(*)[16]>(ov + 16 * c16));
+    umma::wait_ld();
+    float inv = 1.f;
+    if (p.fuse_epilogue) {
+      f32x2 s2[2] = {0ull, 0ull};
+      #pragma unroll
+      for (int j = 0; j < 64; j += 2)
+        if (j < HALF) {
+          const f32x2 o2 = f2pk(ov[j], ov[j + 1]);
+          s2[(j >> 1) & 1] = f2fma(o2, o2, s2[(j >> 1) & 1]);
+        }
+      float s4[4];
+      f2un(s2[0], s4[0], s4[1]);
+      f2un(s2[1], s4[2], s4[3]);
+      sRms[orow * 2 + half] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      named_bar_x3(1, 128);
+      const float tot = sRms[orow * 2] + sRms[orow * 2 + 1];
+      inv = rsqrtf(tot / (float)V + p.eps);
+      named_bar_x3(1, 128);  // sRms reusable
+    }
+    if (orow < cv) {
+      TIN* op = static_cast<TIN*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
+                (int64_t)(t0 + orow) * p.out.s2 + col0;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (8 * j >= HALF) break;
+        float y[8];
+        #pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int cc = 8 * j + e;
+          y[e] = p.fuse_epilogue ? ov[cc] * inv * sOnw[col0 + cc] * silu_acc(gate_at(cc)) : ov[cc];
+        }
+        if constexpr (sizeof(TIN) == 2) {
+          uint4 pk;
+          pk.x = umma::pack_bf16x2(y[0], y[1]); pk.y = umma::pack_bf16x2(y[2], y[3]);
+          pk.z = umma::pack_bf16x2(y[4], y[5]); pk.w = umma::pack_bf16x2(y[6], y[7]);
+          reinterpret_cast<uint4*>(op)[j] = pk;
+        } else {
+          reinterpret_cast<float4*>(op)[2 * j] = make_float4(y[0], y[1], y[2], y[3]);
+          reinterpret_cast<float4*>(op)[2 * j + 1] = make_float4(y[4], y[5], y[6], y[7]);
+        }
+      }
+    }
+  };
+  if (sp >= 2) prefetch_gate(0);
+  else prefetch_u(0);
+
+  for (int c = 0; c < p.NC; ++c) {
+    const uint32_t tD = tD0 + (c & 1) * V;
+    mbar_wait_bounded(&bars[0], c & 1);  // [W; Qg] and gamma_last of chunk c
+    umma::fence_after_sync();
+
+    // MMA1: D = [W; Qg] S
+    if (tid == 0) {
+      const uint64_t dsh = umma::desc_mnmaj_base(sbase + S_HI, TC_K), dsl = umma::desc_mnmaj_base(sbase + S_LO, TC_K);
+      const uint64_t dwh = umma::desc_kmaj_base(sbase + WQ), dwl = umma::desc_kmaj_base(sbase + WQ + 32768);
+      #pragma unroll 1
+      for (int pass = 0; pass < 3; ++pass) {
+        const uint64_t da = pass == 1 ? dwl : dwh, db = pass == 2 ? dsl : dsh;
+        #pragma unroll
+        for (int j = 0; j < 8; ++j)
+          umma::mma_bf16(tD, umma::desc_kmaj_at(da, 128, j), umma::desc_mnmaj_at(db, j), i1, pass > 0 || j > 0);
+      }
+      umma::commit(&bars[2]);
+    }
+    // meanwhile: S <- diag(gamma_last) S in TMEM (all warps), then the epilogue of the previous chunk
+    // (sub-partitions 2, 3)
+    {
+      const float gam = sGl[(c & 1) * 128 + kk];
+      for (int b32 = 0; b32 < HALF; b32 += 32) {
+        float v[2][16];
+        #pragma unroll
+        for (int c16 = 0; c16 < 2; ++c16) umma::ld16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
+        umma::wait_ld();
+        #pragma unroll
+        for (int c16 = 0; c16 < 2; ++c16) {
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) v[c16][j] *= gam;
+          umma::st16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
+        }
+      }
+      umma::wait_st();
+    }
+    if (sp >= 2) {
+      umma::fence_before_sync();
+      mbar_arrive(&bars[4]);
+      if (c + 1 < p.NC) prefetch_gate(c + 1);
+      if (c > 0) epilogue(c - 1);
+    } else {
+      float u[64];
+      {
+        const float4* src = u_row(c);
+        #pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (4 * j < HALF) {
+            float4 f;
+            asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
+                : "l"(src + j));
+            u[4 * j] = f.x; u[4 * j + 1] = f.y; u[4 * j + 2] = f.z; u[4 * j + 3] = f.w;
+          }
+      }
+      mbar_wait_bounded(&bars[2], c & 1);
+      umma::fence_after_sync();
+      if (tid == 0 && c + 1 < p.NC) issueA(c + 1);  // MMA1 has read [W; Qg]; gamma_last goes to the other slot
+      // v_new = U - W S (rows 0..63 of D) -> hi / lo images
+      const int r = 32 * sp + lane;
+      #pragma unroll
+      for (int b32 = 0; b32 < 64; b32 += 32) {
+        if (b32 >= HALF) break;
+        float v[2][16];
+        #pragma unroll
+        for (int c16 = 0; c16 < 2; ++c16) umma::ld16(umma::taddr(tD, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
+        umma::wait_ld();
+        #pragma unroll
+        for (int c16 = 0; c16 < 2; ++c16) {
+          const int col = col0 + b32 + 16 * c16;
+          float vn[16];
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) vn[j] = u[b32 + 16 * c16 + j] - v[c16][j];
+          uint4 h0, l0, h1, l1;
+          split8(vn, h0, l0);
+          split8(vn + 8, h1, l1);
+          const uint32_t o0 = umma::mnmaj_chunk(r, col / 8, TC_C), o1 = umma::mnmaj_chunk(r, col / 8 + 1, TC_C);
+          *reinterpret_cast<uint4*>(sm + VN_HI + o0) = h0;
+          *reinterpret_cast<uint4*>(sm + VN_HI + o1) = h1;
+          *reinterpret_cast<uint4*>(sm + VN_LO + o0) = l0;
+          *reinterpret_cast<uint4*>(sm + VN_LO + o1) = l1;
+        }
+      }
+      fence_proxy_async_smem();
+      umma::fence_before_sync();
+      mbar_arrive(&bars[4]);
+      if (c + 1 < p.NC) prefetch_u(c + 1);
+    }
+
+    // MMA2: D += [*; Aqk] v_new ; MMA3: S += Kd^T v_new
+    if (tid == 0) {
+      mbar_wait_bounded(&bars[4], c & 1);
+      mbar_wait_bounded(&bars[1], c & 1);
+      umma::fence_after_sync();
+      const uint64_t dvh = umma::desc_mnmaj_base(sbase + VN_HI, TC_C), dvl = umma::desc_mnmaj_base(sbase + VN_LO, TC_C);
+      const uint64_t dth = umma::desc_kmaj_base(sbase + AQK - 8192), dtl = umma::desc_kmaj_base(sbase + AQK_LO - 8192);
+      const uint64_t dkh = umma::desc_mnmaj_base(sbase + KD_HI, TC_C), dkl = umma::desc_mnmaj_base(sbase + KD_LO, TC_C);
+      #pragma unroll 1
+      for (int pass = 0; pass < 3; ++pass) {
+        const uint64_t da = pass == 1 ? dtl : dth, db = pass == 2 ? dvl : dvh;
+        #pragma unroll
+        for (int j = 0; j < 4; ++j)
+          umma::mma_bf16(tD, umma::desc_kmaj_at(da, 128, j), umma::desc_mnmaj_at(db, j), i1, true);
+      }
+      #pragma unroll 1
+      for (int pass = 0; pass < 3; ++pass) {
+        const uint64_t da = pass == 1 ? dkl : dkh, db = pass == 2 ? dvl : dvh;
+        #pragma unroll
+        for (int j = 0; j < 4; ++j)
+          umma::mma_bf16(tS, umma::desc_mnmaj_at(da, j), umma::desc_mnmaj_at(db, j), i3, true);
+      }
+      umma::commit(&bars[3]);
+    }
+    mbar_wait_bounded(&bars[3], c & 1);
+    umma::fence_after_sync();
+    if (tid == 0 && c + 1 < p.NC) issueB(c + 1);  // MMA2 / MMA3 have read Aqk and Kd
+
+    // S (now S_{c+1}) -> hi / lo images for the next chunk
+    for (int b32 = 0; b32 < HALF; b32 += 32) {
+      float v[2][16];
+      #pragma unroll
+      for (int c16 = 0; c16 < 2; ++c16) umma::ld16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
+      umma::wait_ld();
+      #pragma unroll
+      for (int c16 = 0; c16 < 2; ++c16) {
+        const int col = col0 + b32 + 16 * c16;
+        uint4 h0, l0, h1, l1;
+        split8(v[c16], h0, l0);
+        split8(v[c16] + 8, h1, l1);
+        const uint32_t o0 = umma::mnmaj_chunk(kk, col / 8, TC_K), o1 = umma::mnmaj_chunk(kk, col / 8 + 1, TC_K);
+        *reinterpret_cast<uint4*>(sm + S_HI + o0) = h0;
+        *reinterpret_cast<uint4*>(sm + S_HI + o1) = h1;
+        *reinterpret_cast<uint4*>(sm + S_LO + o0) = l0;
+        *reinterpret_cast<uint4*>(sm + S_LO + o1) = l1;
+      }
+    }
+    fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+  }
+  if (sp >= 2) epilogue(p.NC - 1);
+
+  // ---- final state back to HBM (f32, in place) ----
+  for (int c16 = 0; c16 < HALF / 16; ++c16) {
+    const int col = col0 + 16 * c16;
+    float v[16];
+    umma::ld16(umma::taddr(tS, 32 * sp, col), v);
+    umma::wait_ld();
+    float4* dst = reinterpret_cast<float4*>(st + (size_t)kk * V + col);
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tD0, 512);
+}
+
+template <typename TIN>
+static int launch_inter_x3_t(const TcParams& p, cudaStream_t st) {
+  const size_t smem = nx3::TOTAL + 1024;
+  cudaError_t e =
+      cudaFuncSetAttribute((const void*)k_inter_x3<TIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "chunk inter (x3) smem attribute");
+  dim3 grid(1, p.HV, p.B);
+  k_inter_x3<TIN><<<grid, 256, smem, st>>>(p);
+  return check_cuda(cudaGetLastError(), "chunk inter (x3) launch");
+}
+
+int launch_inter_x3(const TcParams& p, int dtype, cudaStream_t st) {
+  return dtype == GDN2_DTYPE_BF16 ? launch_inter_x3_t<__nv_bfloat16>(p, st) : launch_inter_x3_t<float>(p, st);
+}
+
+GDN2_DEVICE_ERROR_READER(read_device_errors_inter_x3)
+
+}  // namespace gdn2

@@ -1,0 +1,113 @@
+// Split-operand ("x3") tensor-core chunk path: the chunk-intra and
+// chunk-inter kernels with f32-grade intermediates, for bf16 or f32 inputs,
+// K = 128 key channels, chunk 64, V in {64, 128}.
+//
+// Every tensor-core operand x that is not exactly a bf16 value is carried as
+// a pair of bf16 images, hi = bf16(x) and lo = bf16(x - hi) (x = hi + lo to
+// about 2^-17 relative), and every product is issued as three kind::f16 MMAs
+// into the same f32 TMEM accumulator: A_hi B_hi + A_lo B_hi + A_hi B_lo (the
+// dropped A_lo B_lo term is about 2^-18 of the product).  The path keeps the
+// tile-local decay scheme of src/forward.rs:86-274 and holds the reference's
+// f32 tolerance (rel 1e-3 / abs 1e-4 against a float64 restatement) for f32
+// inputs; with bf16 inputs it computes the same f32-grade intermediates.
+//
+// Per (b, hv, chunk) record written by the intra kernel (byte offsets):
+//   WQ_HI, WQ_LO [128][128] K-major : rows 0..63 W = (I+Akk)^-1 (b k gamma),
+//                                     rows 64..127 Qg = scale q gamma
+//   AQK_HI, AQK_LO [64][64] K-major : scale * causal(q k^T decay)
+//   KD_HI, KD_LO [64][128] MN-major : k exp(G_last - G)
+//   U    f32 [64][V] row-major      : (I+Akk)^-1 (w v)
+//   GL   f32 [128]                  : gamma_last = exp(G_last)
+// AQK_HI directly follows WQ_LO and AQK_LO directly follows AQK_HI: the
+// inter kernel's [*; Aqk] operand of M = 128 takes its first 64 rows from
+// the 8 KB in front of each Aqk image (their products land in accumulator
+// rows that are dead by then), so no zero half tile is needed.
+#pragma once
+
+#include "chunk_tc.cuh"
+#include "umma.cuh"
+
+namespace gdn2 {
+
+struct X3Record {
+  size_t wq_hi, wq_lo, aqk_hi, aqk_lo, kd_hi, kd_lo, u, gl, bytes;
+};
+
+__host__ __device__ inline X3Record x3_record_layout(int V) {
+  X3Record r;
+  r.wq_hi = 0;
+  r.wq_lo = r.wq_hi + 128 * 128 * 2;
+  r.aqk_hi = r.wq_lo + 128 * 128 * 2;
+  r.aqk_lo = r.aqk_hi + 64 * 64 * 2;
+  r.kd_hi = r.aqk_lo + 64 * 64 * 2;
+  r.kd_lo = r.kd_hi + 64 * 128 * 2;
+  r.u = r.kd_lo + 64 * 128 * 2;
+  r.gl = r.u + (size_t)64 * V * 4;
+  r.bytes = (r.gl + TC_K * 4 + 1023) / 1024 * 1024;
+  return r;
+}
+
+bool x3_supported(int K, int V, int C);
+int launch_intra_x3(const TcParams& p, int dtype, cudaStream_t st);
+int launch_inter_x3(const TcParams& p, int dtype, cudaStream_t st);
+
+// ---- device helpers shared by the two kernels ----
+
+// bf16 pair (lower channel in the low half) -> f32 pair, exact
+__device__ __forceinline__ f32x2 bf2f2(uint32_t u) {
+  return f2pk(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+// f32 pair -> bf16 pair, round to nearest even
+__device__ __forceinline__ uint32_t f2bf2(f32x2 r) {
+  float lo, hi;
+  f2un(r, lo, hi);
+  return umma::pack_bf16x2(lo, hi);
+}
+__device__ __forceinline__ f32x2 f2sub(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// x -> (hi, lo) bf16 pairs with hi = bf16(x), lo = bf16(x - hi); x - hi is exact in f32
+__device__ __forceinline__ void split2(f32x2 x, uint32_t& hi, uint32_t& lo) {
+  hi = f2bf2(x);
+  lo = f2bf2(f2sub(x, bf2f2(hi)));
+}
+// 8 consecutive f32 -> hi and lo images of 8 bf16 (one 16-byte chunk each)
+__device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
+  split2(f2pk(v[0], v[1]), hi.x, lo.x);
+  split2(f2pk(v[2], v[3]), hi.y, lo.y);
+  split2(f2pk(v[4], v[5]), hi.z, lo.z);
+  split2(f2pk(v[6], v[7]), hi.w, lo.w);
+}
+
+// Four consecutive input elements of one row as two f32 pairs, read with a
+// non-volatile non-coherent load (the compiler may hoist it above stores
+// into the record, which it would otherwise have to assume alias it).
+template <typename TIN>
+struct Raw4;
+template <>
+struct Raw4<__nv_bfloat16> {
+  uint2 r;
+  __device__ __forceinline__ void zero() { r = make_uint2(0u, 0u); }
+  __device__ __forceinline__ void load(const void* ptr) {
+    asm("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(ptr));
+  }
+  __device__ __forceinline__ f32x2 pair(int m) const { return bf2f2(m ? r.y : r.x); }
+};
+template <>
+struct Raw4<float> {
+  float4 r;
+  __device__ __forceinline__ void zero() { r = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void load(const void* ptr) {
+    asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(ptr));
+  }
+  __device__ __forceinline__ f32x2 pair(int m) const { return m ? f2pk(r.z, r.w) : f2pk(r.x, r.y); }
+};
+
+template <typename TIN>
+__device__ __forceinline__ const void* vptr(const DView& v, int bb, int h, int t, int c) {
+  return static_cast<const TIN*>(v.p) + bb * v.s0 + h * v.s1 + (int64_t)t * v.s2 + c;
+}
+
+}  // namespace gdn2

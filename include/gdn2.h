@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define GDN2_ABI_VERSION 1
+#define GDN2_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define GDN2_API __attribute__((visibility("default")))
@@ -49,6 +49,20 @@ typedef enum gdn2_status {
 } gdn2_status;
 
 typedef enum gdn2_dtype { GDN2_DTYPE_F32 = 0, GDN2_DTYPE_BF16 = 1 } gdn2_dtype;
+
+/* Arithmetic of the chunked forward's intermediates (gdn2_chunk_args.precision).
+ *  GDN2_PRECISION_F32 (0, the default): every intermediate of the chunk
+ *    algorithm is carried at f32 grade (the reference computes in f32,
+ *    src/kernel/fused_recurrent_cube.rs:74): on the tensor cores as hi + lo
+ *    bf16 operand pairs with f32 accumulation (K = 128, chunk 64,
+ *    V in {64, 128}, bf16 or f32 inputs), elsewhere exact f32 on the CUDA
+ *    cores.  Meets rel 1e-3 / abs 1e-4 against a float64 restatement.
+ *  GDN2_PRECISION_BF16 (1): bf16 inputs only; the per-chunk intermediates
+ *    (W, U, Qg, Kd, Aqk, v_new, the state operand) rounded to bf16 once,
+ *    on the tensor cores (K = 128, chunk 64, V in {64, 128, 256}): faster,
+ *    with a per-head normwise error of about 3e-3.  Other shapes and f32
+ *    inputs take the GDN2_PRECISION_F32 path. */
+typedef enum gdn2_precision { GDN2_PRECISION_F32 = 0, GDN2_PRECISION_BF16 = 1 } gdn2_precision;
 
 /* 4-D view [d0][d1][d2][d3], d3 contiguous; strides in elements. */
 typedef struct gdn2_view {
@@ -98,6 +112,7 @@ typedef struct gdn2_chunk_args {
   const float* o_norm_weight; /* [V] */
   float* state;
   gdn2_view out;
+  int32_t precision; /* gdn2_precision */
 } gdn2_chunk_args;
 
 /* Bytes of device workspace gdn2_chunk_fwd / _intra / _inter need. */

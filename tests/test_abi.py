@@ -27,7 +27,7 @@ def test_library_exports_every_header_symbol():
     assert not missing, missing
     for name in decls:
         assert hasattr(burn_gdn2.LIB, name)
-    assert burn_gdn2.LIB.gdn2_abi_version() == 1
+    assert burn_gdn2.LIB.gdn2_abi_version() == 2
 
 
 def test_struct_layout_matches_header():
@@ -46,7 +46,7 @@ int main() {
   P(gdn2_prologue_args, a_log) P(gdn2_prologue_args, decay_factors) P(gdn2_prologue_args, q)
   P(gdn2_prologue_args, g)
   P(gdn2_chunk_args, scale) P(gdn2_chunk_args, q) P(gdn2_chunk_args, gate) P(gdn2_chunk_args, o_norm_weight)
-  P(gdn2_chunk_args, state) P(gdn2_chunk_args, out)
+  P(gdn2_chunk_args, state) P(gdn2_chunk_args, out) P(gdn2_chunk_args, precision)
   P(gdn2_recurrent_args, q) P(gdn2_recurrent_args, conv_w_q) P(gdn2_recurrent_args, conv_v_out)
   P(gdn2_recurrent_args, gate) P(gdn2_recurrent_args, state) P(gdn2_recurrent_args, out)
   P(gdn2_config, expand_v) P(gdn2_config, num_v_heads) P(gdn2_config, norm_eps) P(gdn2_config, chunk_size)
