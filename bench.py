@@ -145,34 +145,12 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-    import burn_gdn2 as bg
-    from burn_gdn2 import ops
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
-    esize = 2 if dtype == torch.bfloat16 else 4
+def measure_core(torch, bg, ops, env, args, dtype, precision, with_e2e, clocks=False):
+    """BASELINE config 2 chunk core (intra + inter + fused gated RMS norm) in `dtype` with `precision`
+    intermediates: device-resident value, per-kernel split, and (with_e2e) the same step through the C ABI
+    from pinned host buffers with the host <-> device copies inside the timed region."""
+    dev, stream, rank, world = env["dev"], env["stream"], env["rank"], env["world"]
+    barrier, max_over_ranks = env["barrier"], env["max_over_ranks"]
     c = CFG2
     B, HV, T, K, V = c["B"], c["HV"], c["T"], c["K"], c["V"]
     x = make_inputs(torch, B, HV, T, K, V, dtype, dev, seed=1000 + rank)
@@ -182,12 +160,10 @@ def run_ours(args):
     onw = torch.ones(V, dtype=torch.float32, device=dev)
     a = ops.chunk_args(view(x["q"]), view(x["k"]), view(x["v"]), view(x["g"]), view(x["b"]), view(x["w"]), state,
                        view(out), K ** -0.5, c["chunk"], num_heads=c["H"], gate=view(x["gate"]),
-                       o_norm_weight=onw, norm_eps=1e-5)
+                       o_norm_weight=onw, norm_eps=1e-5, precision=precision)
     ws = ops.chunk_workspace(a, dev)
-    stream = torch.cuda.current_stream(dev)
     sh = ctypes.c_void_p(stream.cuda_stream)
     wsp, wsn = ctypes.c_void_p(ws.data_ptr()), ws.numel()
-
     ev = lambda: torch.cuda.Event(enable_timing=True)
 
     def step(e0=None, e1=None, e2=None):
@@ -206,7 +182,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local) if rank == 0 else None
+    sampler = ClockSampler(env["local"]) if (clocks and rank == 0) else None
     if sampler:
         sampler.start()
     evs = [(ev(), ev(), ev()) for _ in range(args.steps)]
@@ -216,14 +192,19 @@ def run_ours(args):
         step(*e)
     t_end.record(stream)
     torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
+    res = {"clocks": sampler.stop() if sampler else None}
     barrier()
-    ms_local = t_start.elapsed_time(t_end) / args.steps
+    ms = max_over_ranks(t_start.elapsed_time(t_end) / args.steps)
     intra_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in evs) / args.steps
     inter_ms = sum(e1.elapsed_time(e2) for _, e1, e2 in evs) / args.steps
-    ms = max_over_ranks(ms_local)
     tokens = B * T
-    value = tokens * world / (ms / 1e3)
+    esize = 2 if dtype == torch.bfloat16 else 4
+    alg_bytes = core_bytes_per_token_head(K, V, esize) * tokens * HV
+    flops = core_flops_per_token_head(K, V, c["chunk"]) * tokens * HV
+    res.update(value=tokens * world / (ms / 1e3), ms=ms, intra_ms=intra_ms, inter_ms=inter_ms, alg_bytes=alg_bytes,
+               flops=flops, tokens=tokens)
+    if not with_e2e:
+        return res
 
     # ---- e2e through the C ABI from pinned host buffers ----
     # Batch entries are independent chains, so the step is pipelined by batch
@@ -237,7 +218,8 @@ def run_ours(args):
     slice_args = [ops.chunk_args(view(dbuf["q"][i:i + 1]), view(dbuf["k"][i:i + 1]), view(dbuf["v"][i:i + 1]),
                                  view(dbuf["g"][i:i + 1]), view(dbuf["b"][i:i + 1]), view(dbuf["w"][i:i + 1]),
                                  state[i:i + 1], view(out[i:i + 1]), K ** -0.5, c["chunk"], num_heads=c["H"],
-                                 gate=view(dbuf["gate"][i:i + 1]), o_norm_weight=onw, norm_eps=1e-5)
+                                 gate=view(dbuf["gate"][i:i + 1]), o_norm_weight=onw, norm_eps=1e-5,
+                                 precision=precision)
                   for i in range(B)]
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
@@ -246,7 +228,7 @@ def run_ours(args):
         start.record(stream)
         s_in.wait_event(start)
         s_out.wait_event(start)
-        copied, done = [], []
+        copied = []
         for i in range(B):
             with torch.cuda.stream(s_in):
                 for n in host:
@@ -260,7 +242,6 @@ def run_ours(args):
             bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(slice_args[i]), wsp, wsn, sh))
             e = torch.cuda.Event()
             e.record(stream)
-            done.append(e)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(e)
                 hout[i].copy_(out[i], non_blocking=True)
@@ -280,67 +261,120 @@ def run_ours(args):
     s1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(s0.elapsed_time(s1) / e2e_steps)
-    e2e_value = tokens * world / (e2e_ms / 1e3)
+    res["e2e"] = {"value": tokens * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                  "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
     del host, dbuf
+    return res
 
-    # ---- decode step, BASELINE config 3 (one token, B = 256) ----
+
+def core_line(res, peaks, dtype_name, precision):
+    """Summary of one measure_core result: tokens/s, ms, the per-kernel split and the HBM roofline of the chunk
+    core (algorithmic bytes over the two kernels' CUDA-event time)."""
+    core_ms = res["intra_ms"] + res["inter_ms"]
+    achieved = res["alg_bytes"] / (core_ms / 1e3) / 1e9
+    out = {"value": res["value"], "unit": "tokens/s", "ms_per_step": res["ms"], "dtype": dtype_name,
+           "precision": precision,
+           "kernels_ms": {"chunk_intra": res["intra_ms"], "chunk_inter_plus_epilogue": res["inter_ms"]},
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": achieved / peaks["hbm_gbs"], "alg_bytes_per_step": res["alg_bytes"],
+                        "tc_frac": res["flops"] / (core_ms / 1e3) / (peaks["bf16_tflops"] * 1e12)}}
+    if "e2e" in res:
+        out["e2e"] = res["e2e"]
+    return out
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import burn_gdn2 as bg
+    from burn_gdn2 import comm, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        # NCCL communicators created non-blocking, every collective bounded by the group timeout
+        comm.init_process_group("nccl", timeout_s=120, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream(dev)
+    env = dict(dev=dev, stream=stream, rank=rank, world=world, local=local, barrier=barrier,
+               max_over_ranks=max_over_ranks)
+    peaks = load_peaks()
+    head_dt = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    head = measure_core(torch, bg, ops, env, args, head_dt, "f32", with_e2e=True, clocks=True)
+    # the other input dtype with f32-grade intermediates, and the opt-in bf16-intermediate path
+    other_dt = torch.float32 if head_dt == torch.bfloat16 else torch.bfloat16
+    other = None if args.core_only else measure_core(torch, bg, ops, env, args, other_dt, "f32", with_e2e=True)
+    fast = None if args.core_only else measure_core(torch, bg, ops, env, args, torch.bfloat16, "bf16",
+                                                    with_e2e=False)
+
+    # ---- decode step, BASELINE config 3 (one token, B = 256, state from a T = 512 prefill) ----
     decode = run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world)
     # ---- whole layer forward_train (projections on cuBLAS + the core) ----
     layer = run_layer(torch, bg, dev, stream, args, max_over_ranks, world) if not args.core_only else None
     # ---- N > 1: one config-2 layer split by heads, o_proj all-reduce timed apart ----
     layer_tp = run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world) if world > 1 else None
-    # ---- the f32 configuration of BASELINE config 2 (CUDA-core path) ----
-    f32 = run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world) if not args.core_only else None
-    # ---- BASELINE configs 4 and 5, chunk core ----
+    # ---- BASELINE configs 1, 4 and 5 ----
     others = None
     if not args.core_only:
-        others = {"cfg4_core": run_core_cfg(torch, bg, ops, dev, stream, CFG4, "config 4", max_over_ranks, world,
+        others = {"cfg1_layer": run_cfg1(torch, bg, dev, stream, max_over_ranks, world),
+                  "cfg4_core": run_core_cfg(torch, bg, ops, dev, stream, CFG4, "config 4", max_over_ranks, world,
                                             seed=4000 + 10 * rank),
+                  "cfg4_core_bf16_intermediates": run_core_cfg(torch, bg, ops, dev, stream, CFG4, "config 4",
+                                                               max_over_ranks, world, seed=4000 + 10 * rank,
+                                                               precision="bf16"),
                   "cfg5_core": run_core_cfg(torch, bg, ops, dev, stream, CFG5, "config 5", max_over_ranks, world,
                                             seed=5000 + 10 * rank),
                   # the config-5 layer split by heads over the N ranks (strong scaling, all-reduce timed apart)
                   "cfg5_layer_head_sharded": run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world)}
 
-    # ---- roofline of the dominant kernel ----
-    peaks = load_peaks()
-    bpt = core_bytes_per_token_head(K, V, esize)
-    alg_bytes = bpt * tokens * HV
-    dom_name, dom_ms = ("chunk_inter", inter_ms) if inter_ms >= intra_ms else ("chunk_intra", intra_ms)
-    core_ms = intra_ms + inter_ms
-    achieved = alg_bytes / (core_ms / 1e3) / 1e9
-    flops = core_flops_per_token_head(K, V, c["chunk"]) * tokens * HV
-    # bf16, K = 128, V in {64, 128}, chunk 64: tensor-core path (k_intra_tc + k_inter_tc);
-    # otherwise the CUDA-core path (k_intra_simt + k_inter_simt + k_chunk_out)
-    tc_path = dtype == torch.bfloat16 and K == 128 and V in (64, 128) and c["chunk"] == 64
-    launches_per_step = 2 if tc_path else 3
+    c = CFG2
+    B, HV, T, K, V = c["B"], c["HV"], c["T"], c["K"], c["V"]
+    hl = core_line(head, peaks, args.dtype, "f32")
+    dom_name = "chunk_inter" if head["inter_ms"] >= head["intra_ms"] else "chunk_intra"
     result = None
     if rank == 0:
         result = {
             "metric": "chunk-fwd tokens/s (H2048,T4096); decode tok/s @B256; % TC/HBM roofline",
-            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "value": head["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": args.dtype, "data": "synthetic (seeded, module value laws)",
             "config": {"workload": f"BASELINE config 2 chunked forward core: B={B} (per rank), T=4096, HV=16, "
-                                   "K=V=128, chunk 64, fused gated RMS-norm epilogue",
+                                   f"K=V=128, chunk 64, {args.dtype} inputs, f32-grade intermediates, f32 state, "
+                                   "fused gated RMS-norm epilogue",
                        "global_batch": B * world, "seq_len": T, "parallelism": f"chains x{world} (no collective)",
-                       "l2": f"inputs {alg_bytes / 1e9:.2f} GB/step > 126 MB L2, no flush"},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms},
-            "roofline": {"bound": "hbm", "kernel": "chunk core (intra + inter + epilogue) per step",
-                         "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / peaks["hbm_gbs"],
-                         # per-step DRAM bytes of the B = 8 capture, scaled by the batch (traffic is linear in B)
-                         "traffic": (lambda t: None if t is None else t * B / 8)(ncu_traffic("chunk_core_bf16_cfg2")),
-                         "peak_src": peaks["src"], "alg_bytes_per_step": alg_bytes,
-                         "tc_frac": flops / (core_ms / 1e3) / (peaks["bf16_tflops"] * 1e12)},
-            "kernels_ms": {"chunk_intra": intra_ms, "chunk_inter_plus_epilogue": inter_ms, "dominant": dom_name},
+                       "l2": f"inputs {head['alg_bytes'] / 1e9:.2f} GB/step > 126 MB L2, no flush"},
+            "e2e": head["e2e"],
+            "roofline": dict(hl["roofline"], kernel="chunk core (intra + inter + epilogue) per step",
+                             # DRAM bytes per step from the ncu capture, scaled by the batch (linear in B)
+                             traffic=(lambda t: None if t is None else t * B / 8)(
+                                 ncu_traffic(f"chunk_core_x3_{args.dtype}_cfg2")),
+                             peak_src=peaks["src"]),
+            "kernels_ms": dict(hl["kernels_ms"], dominant=dom_name),
+            "precision": "f32-grade intermediates (split bf16 operand pairs on tcgen05, f32 accumulation)",
+            ("bf16" if other_dt == torch.bfloat16 else "f32"): core_line(other, peaks,
+                                                                         "bf16" if other_dt == torch.bfloat16
+                                                                         else "f32", "f32") if other else None,
+            "bf16_intermediates": core_line(fast, peaks, "bf16", "bf16") if fast else None,
             "decode": decode,
             "layer": layer,
             "layer_head_sharded": layer_tp,
-            "f32": f32,
             "other_configs": others,
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks,
+            "gpu_launches": 2 * args.steps,
+            "clocks": head["clocks"],
         }
     if world > 1:
         dist.destroy_process_group()
@@ -495,54 +529,6 @@ def run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world):
     return out
 
 
-def run_core_f32(torch, bg, ops, dev, stream, args, max_over_ranks, world):
-    """BASELINE config 2 core in f32 (the exact CUDA-core path)."""
-    c = CFG2
-    B, HV, T, K, V = c["B"], c["HV"], c["T"], c["K"], c["V"]
-    x = make_inputs(torch, B, HV, T, K, V, torch.float32, dev, seed=2000)
-    view = lambda t: t.permute(0, 2, 1, 3)
-    state = torch.zeros(B, HV, K, V, dtype=torch.float32, device=dev)
-    out = torch.empty(B, T, HV, V, dtype=torch.float32, device=dev)
-    onw = torch.ones(V, dtype=torch.float32, device=dev)
-    a = ops.chunk_args(view(x["q"]), view(x["k"]), view(x["v"]), view(x["g"]), view(x["b"]), view(x["w"]), state,
-                       view(out), K ** -0.5, c["chunk"], num_heads=c["H"], gate=view(x["gate"]), o_norm_weight=onw,
-                       norm_eps=1e-5)
-    ws = ops.chunk_workspace(a, dev)
-    sh = ctypes.c_void_p(stream.cuda_stream)
-    run = lambda: bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ws.numel(), sh))
-    run()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = 3
-    e0.record(stream)
-    for _ in range(n):
-        state.zero_()
-        run()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / n)
-    # the same step as its two C-ABI phases, for the per-kernel split
-    wsp = ctypes.c_void_p(ws.data_ptr())
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
-    for ea, eb, ec in ev:
-        state.zero_()
-        ea.record(stream)
-        bg._lib.check(bg.LIB.gdn2_chunk_intra(ctypes.byref(a), wsp, ws.numel(), sh))
-        eb.record(stream)
-        bg._lib.check(bg.LIB.gdn2_chunk_inter(ctypes.byref(a), wsp, ws.numel(), sh))
-        ec.record(stream)
-    torch.cuda.synchronize()
-    split = {"chunk_intra": sum(ea.elapsed_time(eb) for ea, eb, _ in ev) / n,
-             "chunk_inter_plus_epilogue": sum(eb.elapsed_time(ec) for _, eb, ec in ev) / n}
-    del ws
-    alg = core_bytes_per_token_head(K, V, 4) * B * T * HV
-    peaks = load_peaks()
-    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "kernels_ms": split,
-            "workload": "BASELINE config 2 chunked forward core in f32 (CUDA-core path, exact f32)",
-            "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
-
-
 # BASELINE configs 4 (GVA: 8 key heads grouped over 16 value heads, V = 256, neg-eig b in [0, 2], min_decay 0.9)
 # and 5 (long context, 32 heads), chunk core only (bf16), measured beside the headline so the path each one
 # takes and its roofline fraction are on record.
@@ -550,7 +536,7 @@ CFG4 = dict(B=4, H=8, HV=16, T=8192, K=128, V=256, chunk=64, negeig=True, min_de
 CFG5 = dict(B=2, H=32, HV=32, T=65536, K=128, V=128, chunk=64, negeig=False, min_decay=None)
 
 
-def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, seed):
+def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, seed, precision="f32"):
     """Chunk core (intra + inter + fused epilogue) at one BASELINE config:
     tokens/s, ms/step and the fraction of the measured HBM copy bandwidth
     its algorithmic bytes reach.  Key-side inputs (q, k, g, b) have H heads
@@ -570,7 +556,7 @@ def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, se
     onw = torch.ones(V, dtype=torch.float32, device=dev)
     a = ops.chunk_args(view(xk["q"]), view(xk["k"]), view(xv["v"]), view(g.contiguous()), view(b), view(xv["w"]),
                        state, view(out), K ** -0.5, c["chunk"], num_heads=H, grouped=H < HV, gate=view(xv["gate"]),
-                       o_norm_weight=onw, norm_eps=1e-5)
+                       o_norm_weight=onw, norm_eps=1e-5, precision=precision)
     ws = ops.chunk_workspace(a, dev)
     sh = ctypes.c_void_p(stream.cuda_stream)
     run = lambda: bg._lib.check(bg.LIB.gdn2_chunk_fwd(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ws.numel(), sh))
@@ -588,36 +574,54 @@ def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, se
     # algorithmic bytes per value head: the key-side reads count once per value head, as the kernels read them
     alg = core_bytes_per_token_head(K, V, 2) * B * T * HV
     peaks = load_peaks()
-    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+    if precision == "bf16":
+        path = ("tensor cores, bf16 intermediates (k_intra_tc + k_inter_tc)" if V <= 128 else
+                "tensor cores, bf16 intermediates (k_intra_tc; k_inter_tc over two 128-column slices per chain, a "
+                "2-CTA cluster exchanging the gated RMS norm's row sums)")
+    else:
+        path = ("tensor cores, f32-grade intermediates (k_intra_x3 + k_inter_x3)" if V <= 128 else
+                "CUDA cores, exact f32 (k_intra_simt + k_inter_simt + k_chunk_out)")
+    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "precision": precision,
             "workload": f"BASELINE {name} chunk core: B={B} (per rank), T={T}, H={H}, HV={HV}, K={K}, V={V}, bf16",
-            "path": "tensor cores (k_intra_tc + k_inter_tc)" if V <= 128 else
-                    "tensor cores (k_intra_tc; k_inter_tc over two 128-column slices per chain, a 2-CTA cluster "
-                    "exchanging the gated RMS norm's row sums)",
+            "path": path,
             "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
 
 
 def run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world):
+    """GatedDeltaNet2 (hidden 2048, 16 x 128 heads, f32) prefills a seeded N(0,1) sequence of
+    T = 512 for B = 256 (the chunked path), then the decode kernel (3) runs 128 one-token steps from that state and
+    those conv caches, in place, with the fused short-conv + L2 prologue (raw projections of seeded N(0,1) tokens
+    through the layer's own weights) and the gated RMS-norm epilogue.  Also the whole layer's decode step
+    (projections + kernel + o_proj) through GatedDeltaNet2.forward."""
     c = CFG3
     B, HV, H, K, V = c["B"], c["HV"], c["H"], c["K"], c["V"]
+    D = H * K
+    cfg = bg.Gdn2Config(hidden_size=D, num_heads=H, head_dim=K, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
+    m = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.float32, seed=3)
     gen = torch.Generator(device=dev).manual_seed(7 + rank)
-    f = lambda *s: torch.randn(*s, generator=gen, device=dev, dtype=torch.float32)
-    S = f(B, HV, K, V) * 0.1
+    xp = torch.randn(B, 512, D, generator=gen, device=dev, dtype=torch.float32)
+    _, st = m.forward(xp, None, True)
+    del xp
+    torch.cuda.synchronize()
     kd, vd = H * K, HV * V
-    qr, kr, vr = f(B, 1, kd), f(B, 1, kd), f(B, 1, vd)
-    g = -torch.rand(B, 1, kd, generator=gen, device=dev) * 0.5
-    b = torch.rand(B, 1, kd, generator=gen, device=dev)
-    w = torch.rand(B, 1, vd, generator=gen, device=dev)
-    gate = f(B, 1, vd)
-    cq, ck, cv = f(B, 3, kd), f(B, 3, kd), f(B, 3, vd)
-    cw = [torch.rand(n, 4, generator=gen, device=dev) - 0.5 for n in (kd, kd, vd)]
-    onw = torch.ones(V, device=dev)
+    xt = torch.randn(B, 1, D, generator=gen, device=dev, dtype=torch.float32)
+    # the raw projections and gates of one seeded token through the layer's own weights (src/module.rs:400-476)
+    qr, kr, vr = m.q_proj.forward(xt), m.k_proj.forward(xt), m.v_proj.forward(xt)
+    f = m.f_proj_1.forward(m.f_proj_0.forward(xt))
+    g = -torch.exp(m.a_log).repeat_interleave(K).view(1, 1, kd) * torch.nn.functional.softplus(f + m.dt_bias)
+    b = torch.sigmoid(m.b_proj.forward(xt))
+    w = torch.sigmoid(m.w_proj.forward(xt))
+    gate = m.g_proj_1.forward(m.g_proj_0.forward(xt))
+    S = st.recurrent
+    cq, ck, cv = st.conv_q, st.conv_k, st.conv_v
+    cw = [m.q_conv_w, m.k_conv_w, m.v_conv_w]
     out = torch.empty(B, 1, HV, V, device=dev)
     to4 = lambda t, n, d: t.reshape(B, 1, n, d).permute(0, 2, 1, 3)
-    a = ops.recurrent_args(to4(qr, H, K), to4(kr, H, K), to4(vr, HV, V), to4(g, H, K), to4(b, H, K),
+    a = ops.recurrent_args(to4(qr, H, K), to4(kr, H, K), to4(vr, HV, V), to4(g.contiguous(), H, K), to4(b, H, K),
                            to4(w, HV, V), S, out.permute(0, 2, 1, 3), K ** -0.5, num_heads=H, grouped=True,
                            prologue=1, conv_w=cw, conv_in=(cq, ck, cv), conv_out=(cq, ck, cv),
-                           gate=to4(gate, HV, V), o_norm_weight=onw, norm_eps=1e-5)
+                           gate=to4(gate.contiguous(), HV, V), o_norm_weight=m.o_norm_weight, norm_eps=1e-5)
     sh = ctypes.c_void_p(stream.cuda_stream)
     run = lambda: bg._lib.check(bg.LIB.gdn2_recurrent_fwd(ctypes.byref(a), sh))
     for _ in range(max(3, args.warmup)):
@@ -631,68 +635,157 @@ def run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    # the whole layer's decode step from the same state: projections (cuBLAS) + kernel (3) + o_proj
+    for _ in range(3):
+        m.forward(xt, st, True)
+    torch.cuda.synchronize()
+    n = 16
+    e0.record(stream)
+    for _ in range(n):
+        m.forward(xt, st, True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    layer_ms = max_over_ranks(e0.elapsed_time(e1) / n)
     state_bytes = 2 * B * HV * K * V * 4
     vec_bytes = B * 1 * (3 * kd + 4 * vd) * 4 + B * HV * V * 4 + 2 * B * 3 * (2 * kd + vd) * 4
     peaks = load_peaks()
     gbs = (state_bytes + vec_bytes) / (ms / 1e3) / 1e9
     return {"value": B * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
             "workload": "BASELINE config 3 decode step: B=256 (per rank), HV=16, K=V=128, state f32 in place, "
-                        "fused short-conv + L2 prologue and gated RMS-norm epilogue",
+                        "initialised by a seeded T=512 prefill through GatedDeltaNet2.forward, fused short-conv + "
+                        "L2 prologue and gated RMS-norm epilogue",
+            "layer_decode_ms_per_step": layer_ms, "layer_decode_tokens_per_s": B * world / (layer_ms / 1e3),
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm_gbs"], "bytes_per_step": state_bytes + vec_bytes,
                          "traffic": ncu_traffic("decode_cfg3")}}
 
 
+def run_cfg1(torch, bg, dev, stream, max_over_ranks, world):
+    """BASELINE config 1 on the GPU: hidden 256, 4 x 64 heads, Chunk mode, f32, x [1, 1024, 256] ~ N(0,1) seed 0,
+    weights seeded 0: forward_train, and a T = 1024 prefill followed by one decode token with Gdn2State."""
+    cfg = bg.Gdn2Config(hidden_size=256, num_heads=4, head_dim=64, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
+    m = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.float32, seed=0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(1, 1025, 256, generator=gen, device=dev, dtype=torch.float32)
+
+    def prefill_decode():
+        _, st = m.forward(x[:, :1024], None, True)
+        return m.forward(x[:, 1024:], st, True)
+
+    out = {}
+    for name, fn in (("forward_train", lambda: m.forward_train(x[:, :1024])), ("prefill_1024_then_decode_1",
+                                                                             prefill_decode)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 10
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        out[name + "_ms"] = max_over_ranks(e0.elapsed_time(e1) / n)
+    out["workload"] = ("BASELINE config 1: GatedDeltaNet2 hidden 256, 4 x 64 heads, Chunk, f32, B=1, T=1024 "
+                       "(launch-bound at this size)")
+    out["forward_train_tokens_per_s"] = 1024 * world / (out["forward_train_ms"] / 1e3)
+    return out
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline: numpy restatement of the crate's tensor path (oracle)
 # ---------------------------------------------------------------------------
-def cpu_baseline(budget_s=12.0):
+def _blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(n[0]) if n else os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def cpu_sample_step(O, np, arr, s0):
+    """One step of the CPU port: chunk_wy_forward + rms_norm_gate_per_head over one sequence (B = 1 of
+    config 2's B = 8, full T = 4096, 16 value heads, K = V = 128, f32).  Returns seconds."""
+    c = CFG2
+    t0 = time.perf_counter()
+    o, _ = O.chunk_wy_forward(arr["q"], arr["k"], arr["v"], arr["g"], arr["b"], arr["w"], s0, c["K"] ** -0.5,
+                              c["chunk"])
+    O.rms_norm_gate_per_head(o.transpose(0, 2, 1, 3), arr["gate"], np.ones(c["V"], np.float32), 1e-5)
+    return time.perf_counter() - t0
+
+
+def _cpu_sample_inputs():
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import gdn2_oracle as O
 
     c = CFG2
-    Bs, Ts = 1, 256
-    arr = O.make_core_inputs(Bs, c["HV"], Ts, c["K"], c["V"], seed=3, dtype=np.float32)
-    s0 = np.zeros((Bs, c["HV"], c["K"], c["V"]), np.float32)
-    n = 0
+    arr = O.make_core_inputs(1, c["HV"], c["T"], c["K"], c["V"], seed=3, dtype=np.float32)
+    return O, np, arr, np.zeros((1, c["HV"], c["K"], c["V"]), np.float32)
+
+
+CPU_SAMPLE = ("numpy (OpenBLAS) restatement of the crate's f32 tensor path (chunk_wy_forward + rms_norm_gate, the "
+              "same op sequence as its NdArray backend): one sequence of BASELINE config 2 per step (B=1 of 8, "
+              "T=4096, HV=16, K=V=128, chunk 64); tokens/s scales linearly in B")
+
+
+def cpu_baseline(budget_s=10.0):
+    O, np, arr, s0 = _cpu_sample_inputs()
+    times = []
+    while sum(times) < budget_s or len(times) < 2:
+        times.append(cpu_sample_step(O, np, arr, s0))
+    el = sum(times)
+    out = {"value": len(times) * CFG2["T"] / el, "unit": "tokens/s", "cores": _blas_threads(), "kind": "port",
+           "sample": f"{CPU_SAMPLE}; {len(times)} steps in {el:.1f} s"}
+    out["cfg1"] = cpu_baseline_cfg1()
+    return out
+
+
+def cpu_baseline_cfg1():
+    """BASELINE config 1 in full on the CPU port: forward_train of x [1, 1024, 256] and a T = 1024 prefill
+    followed by one decode token (Gdn2State), f32, weights seeded 0."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import gdn2_oracle as O
+
+    cfg = O.Gdn2Config(hidden_size=256, num_heads=4, head_dim=64, mode="chunk", chunk_size=64)
+    layer = O.Gdn2Layer(cfg, O.init_weights(cfg, seed=0), np.float32)
+    x = np.random.default_rng(0).standard_normal((1, 1025, 256)).astype(np.float32)
     t0 = time.perf_counter()
-    while True:
-        o, _ = O.chunk_wy_forward(arr["q"], arr["k"], arr["v"], arr["g"], arr["b"], arr["w"], s0,
-                                  c["K"] ** -0.5, c["chunk"])
-        O.rms_norm_gate_per_head(o.transpose(0, 2, 1, 3), arr["gate"], np.ones(c["V"], np.float32), 1e-5)
-        n += 1
-        el = time.perf_counter() - t0
-        if el > budget_s:
-            break
-    tok_s = n * Bs * Ts / el
-    cores = os.cpu_count()
-    return {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"numpy (OpenBLAS) restatement of chunk_wy_forward + rms_norm_gate, f32, B={Bs} T={Ts} "
-                      f"HV={c['HV']} K=V={c['K']} chunk 64, {n} reps in {el:.1f}s (same op sequence as the "
-                      f"crate's NdArray path; tokens/s scales linearly in B*T)"}
+    layer.forward_train(x[:, :1024])
+    t1 = time.perf_counter()
+    _, st = layer.forward(x[:, :1024], None, True)
+    layer.forward(x[:, 1024:], st, True)
+    t2 = time.perf_counter()
+    return {"forward_train_ms": (t1 - t0) * 1e3, "prefill_1024_then_decode_1_ms": (t2 - t1) * 1e3,
+            "forward_train_tokens_per_s": 1024 / (t1 - t0), "cores": _blas_threads(), "kind": "port",
+            "workload": "BASELINE config 1 in full (hidden 256, 4 x 64 heads, Chunk, f32, B=1, T=1024)"}
 
 
 def run_reference(args):
+    """The reference arm: the crate's f32 tensor path, restated in numpy (the crate itself is Rust and cannot be
+    built here), timed on the host cores.  One step = one sequence of config 2 (B = 1 of 8, full T = 4096);
+    ms_per_step is that step's own measured time."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    per = []
+    O, np, arr, s0 = _cpu_sample_inputs()
     for _ in range(args.warmup):
-        cpu_baseline(budget_s=0.5)
-    for _ in range(args.steps):
-        per.append(cpu_baseline(budget_s=max(2.0, 20.0 / max(1, args.steps))))
-    value = sum(p["value"] for p in per) / len(per)
-    cb = dict(per[-1], value=value)
-    c = CFG2
+        cpu_sample_step(O, np, arr, s0)
+    times = [cpu_sample_step(O, np, arr, s0) for _ in range(args.steps)]
+    ms = sum(times) / len(times) * 1e3
+    value = CFG2["T"] / (ms / 1e3)
     return {"impl": "reference", "metric": "chunk-fwd tokens/s (H2048,T4096); decode tok/s @B256; % TC/HBM roofline",
             "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": c["B"] * c["T"] / value * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, module value laws)",
-            "config": {"workload": "BASELINE config 2 chunked forward core (CPU sample, see cpu_baseline)",
-                       "global_batch": c["B"], "seq_len": c["T"], "parallelism": "host cores"},
-            "cpu_baseline": cb,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, module value laws)",
+            "config": {"workload": "BASELINE config 2 chunked forward core, one sequence per step (B=1 of 8, "
+                                   "T=4096, HV=16, K=V=128, chunk 64, f32)",
+                       "global_batch": 1, "seq_len": CFG2["T"], "parallelism": "host cores (OpenBLAS threads)"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": _blas_threads(), "kind": "port",
+                             "sample": f"{CPU_SAMPLE}; {args.steps} steps of {ms:.0f} ms"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -702,9 +795,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--dtype", default="f32", choices=["bf16", "f32"],
+                    help="input dtype of the headline line (f32: the reference's own arithmetic)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--core-only", action="store_true", help="skip the layer and f32 side measurements")
+    ap.add_argument("--core-only", action="store_true", help="skip the side measurements (other dtype, layer, configs)")
     ap.add_argument("--batch", type=int, default=None,
                     help="batch of config 2 (default 8, the BASELINE value); smaller for profiling captures")
     args = ap.parse_args()

@@ -85,7 +85,7 @@ EXPORTS = (
     "gdn2_chunk_fwd_workspace_bytes", "gdn2_chunk_fwd", "gdn2_chunk_intra", "gdn2_chunk_inter",
     "gdn2_recurrent_fwd", "gdn2_short_conv", "gdn2_rms_norm_gate", "gdn2_config_validate",
     "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
-    "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc", "gdn2_project_activations",
+    "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc", "gdn2_project_activations", "gdn2_selftest_wait",
 )
 
 
@@ -120,6 +120,8 @@ def _load():
     lib.gdn2_read_device_errors.restype = ctypes.c_int
     lib.gdn2_selftest_umma.argtypes = [i32, vp, vp, vp, vp]
     lib.gdn2_selftest_umma.restype = ctypes.c_int
+    lib.gdn2_selftest_wait.argtypes = [ctypes.c_uint32, i32, ctypes.POINTER(ctypes.c_int32)]
+    lib.gdn2_selftest_wait.restype = ctypes.c_int
     return lib
 
 

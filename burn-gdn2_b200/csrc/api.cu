@@ -39,6 +39,7 @@ unsigned read_device_errors_inter_tc();
 unsigned read_device_errors_intra_x3();
 unsigned read_device_errors_inter_x3();
 int selftest_umma(int test, const float* A, const float* B, float* D, cudaStream_t st);
+int selftest_wait(unsigned spins, int arrive, int* completed);
 int launch_short_conv(int B, int Tn, int C, int dtype, const void* x, const float* w, const float* cin, float* cout,
                       void* y, cudaStream_t st);
 int launch_rms_norm_gate(const gdn2_dims& d, int dtype, const gdn2_view& o, const gdn2_view& gate, const float* w,
@@ -311,6 +312,13 @@ int gdn2_selftest_umma(int32_t test, const float* a, const float* b, float* d, v
   if (test < 0 || test > 3) return set_error(GDN2_EINVAL, "gdn2_selftest_umma: test %d not in 0..3", test);
   if (!a || !b || !d) return set_error(GDN2_EINVAL, "gdn2_selftest_umma: null pointer");
   return selftest_umma(test, a, b, d, (cudaStream_t)stream);
+}
+
+int gdn2_selftest_wait(uint32_t spins, int32_t arrive, int32_t* completed) {
+  if (!completed) return set_error(GDN2_EINVAL, "gdn2_selftest_wait: null completed");
+  if (spins == 0 || spins > (1u << 24))
+    return set_error(GDN2_EINVAL, "gdn2_selftest_wait: spins %u not in 1..2^24", spins);
+  return selftest_wait(spins, arrive ? 1 : 0, completed);
 }
 
 int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, void* stream) {

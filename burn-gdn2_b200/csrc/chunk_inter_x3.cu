@@ -100,9 +100,15 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     mbar_arrive_expect_tx(&bars[1], 49152u);
     bulk_g2s(sm + AQK, r + L.aqk_hi, 49152u, &bars[1]);
   };
+  // records two chunks ahead are pulled into L2 (one bulk prefetch per chunk), so the stage refills, issued
+  // as soon as a part is consumed, read from L2
+  auto prefetch_rec = [&](int c) {
+    if (c < p.NC) bulk_prefetch_l2(recs + (size_t)c * p.rec_bytes, (unsigned)L.bytes);
+  };
   if (tid == 0) {
     issueA(0);
     issueB(0);
+    prefetch_rec(1);
   }
 
   // ---- initial state: f32 master in TMEM, hi / lo images in smem ----
@@ -239,6 +245,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
 
     // MMA1: D = [W; Qg] S
     if (tid == 0) {
+      prefetch_rec(c + 2);
       const uint64_t dsh = umma::desc_mnmaj_base(sbase + S_HI, TC_K), dsl = umma::desc_mnmaj_base(sbase + S_LO, TC_K);
       const uint64_t dwh = umma::desc_kmaj_base(sbase + WQ), dwl = umma::desc_kmaj_base(sbase + WQ + 32768);
       #pragma unroll 1

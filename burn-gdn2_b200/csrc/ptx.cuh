@@ -60,9 +60,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
 }
 
 // Bounded wait for phase `parity` of `bar`.  Returns false (and records
-// DEVERR_MBAR_TIMEOUT) if the phase never completed.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i)
+// DEVERR_MBAR_TIMEOUT) if the phase did not complete within `limit`
+// try_wait rounds.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, unsigned limit = MBAR_SPIN_LIMIT) {
+  for (unsigned i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   atomicOr(&g_device_errors, DEVERR_MBAR_TIMEOUT);
   return false;
@@ -98,6 +99,12 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, unsigned 
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sdst)),
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Bulk prefetch of [gsrc, gsrc + bytes) into L2 (no completion tracking);
+// 16-byte aligned address, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
 }
 
 // 1-D bulk copy shared -> global in the thread's bulk async-group; both

@@ -92,6 +92,35 @@ int selftest_umma(int test, const float* A, const float* B, float* D, cudaStream
   return check_cuda(cudaGetLastError(), "selftest launch");
 }
 
+// Diagnostic of the failure path every kernel's waits share: thread 0 waits
+// on an mbarrier through mbar_wait_bounded with a limit of `spins` rounds.
+// With arrive = 0 nothing ever arrives, so the wait gives up, records
+// DEVERR_MBAR_TIMEOUT and the kernel returns normally (no trap, the context
+// stays usable); with arrive = 1 the phase completes at once.
+static __device__ int g_wait_completed = -1;
+
+__global__ void k_selftest_wait(unsigned spins, int arrive) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (arrive) mbar_arrive(&bar);
+    g_wait_completed = mbar_wait_bounded(&bar, 0, spins) ? 1 : 0;
+  }
+}
+
+int selftest_wait(unsigned spins, int arrive, int* completed) {
+  k_selftest_wait<<<1, 32>>>(spins, arrive);
+  int rc = check_cuda(cudaGetLastError(), "selftest wait launch");
+  if (rc) return rc;
+  rc = check_cuda(cudaDeviceSynchronize(), "selftest wait");
+  if (rc) return rc;
+  return check_cuda(cudaMemcpyFromSymbol(completed, g_wait_completed, sizeof(int)), "selftest wait result");
+}
+
 GDN2_DEVICE_ERROR_READER(read_device_errors_selftest)
 
 }  // namespace gdn2

@@ -308,6 +308,16 @@ GDN2_API int gdn2_read_device_errors(uint32_t* flags);
  * a, b, d: row-major f32 device arrays. */
 GDN2_API int gdn2_selftest_umma(int32_t test, const float* a, const float* b, float* d, void* stream);
 
+/* Diagnostic (no counterpart in the reference) of the failure path that
+ * every wait inside the kernels shares: one block whose thread 0 waits on
+ * an mbarrier with a bounded wait of `spins` try_wait rounds (1..2^24).
+ * arrive = 0: nothing arrives, so the wait gives up, sets bit 0 of the
+ * device error bits (gdn2_read_device_errors) and the kernel returns
+ * normally; *completed = 0.  arrive = 1: the phase completes; *completed
+ * = 1.  No trap and no fault either way: the context stays usable.
+ * Synchronises the current device. */
+GDN2_API int gdn2_selftest_wait(uint32_t spins, int32_t arrive, int32_t* completed);
+
 /* Error / version queries. */
 GDN2_API const char* gdn2_last_error(void);
 GDN2_API int gdn2_last_cuda_error(void);

@@ -7,15 +7,19 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 # f32: rel 1e-3 / abs 1e-4 (elementwise |a-b| <= 1e-4 + 1e-3 |b|)
 F32_TOL = dict(rtol=1e-3, atol=1e-4)
-# bf16 inputs with f32 accumulation: rel 2e-2.  The tensor-core path stores
-# its per-chunk intermediates (W, U, Qg, Kd, Aqk, v_new, the state operand)
-# in bf16, so entries that come out of a cancellation (|ref| << RMS) carry
-# an absolute error of a few 1e-3 of the RMS however small they are.  The
-# bf16 check is therefore (a) per-head normwise error <= 1e-2 and (b)
-# elementwise |d| <= 2e-2 |ref| + 5e-2 RMS(ref).
+# bf16 inputs with f32 accumulation: rel 2e-2 elementwise (north star), with
+# an absolute floor of 1e-2 x RMS(ref) for entries that are themselves the
+# result of a cancellation (|ref| << RMS, where no relative bound can hold
+# once the inputs are rounded), plus a per-head normwise error <= 1e-2.
 BF16_RTOL = 2e-2
-BF16_FLOOR = 5e-2
+BF16_FLOOR = 1e-2
 BF16_NORMWISE = 1e-2
+# The opt-in bf16-intermediate tensor-core path (precision="bf16") rounds
+# W, U, Qg, Kd, Aqk, v_new and the state operand to bf16 once per chunk:
+# per-head normwise error about 3e-3, elementwise within 2e-2 |ref| +
+# 5e-2 RMS(ref).  This is that option's documented accuracy, not the
+# default path's bar.
+BF16I_FLOOR = 5e-2
 
 
 def max_violation(a, b, rtol, atol):
@@ -38,12 +42,7 @@ def assert_close(a, b, rtol, atol, what=""):
                              f"want {b[i]:.6g} (|d|={err[i]:.3g}, lim={lim[i]:.3g}); max|d|={err.max():.3g}")
 
 
-def assert_close_bf16(a, b, what="", head_axes=2):
-    """bf16 criterion above; the leading `head_axes` dims index heads."""
-    a = np.asarray(a, dtype=np.float64)
-    b = np.asarray(b, dtype=np.float64)
-    assert a.shape == b.shape, (what, a.shape, b.shape)
-    assert np.all(np.isfinite(a)), f"{what}: non-finite values"
+def _normwise_per_head(a, b, head_axes, what):
     if a.ndim > head_axes:
         hs = a.shape[:head_axes]
         d = (a - b).reshape(int(np.prod(hs)), -1)
@@ -51,8 +50,29 @@ def assert_close_bf16(a, b, what="", head_axes=2):
         nd, nr = np.linalg.norm(d, axis=1), np.linalg.norm(r, axis=1)
         rel = nd / np.maximum(nr, 1e-30)
         assert rel.max() <= BF16_NORMWISE, f"{what}: per-head normwise error {rel.max():.3g} > {BF16_NORMWISE}"
+
+
+def assert_close_bf16(a, b, what="", head_axes=2):
+    """bf16 criterion: elementwise |d| <= 2e-2 |ref| + 1e-2 RMS(ref) and
+    per-head normwise <= 1e-2; the leading `head_axes` dims index heads."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    assert a.shape == b.shape, (what, a.shape, b.shape)
+    assert np.all(np.isfinite(a)), f"{what}: non-finite values"
+    _normwise_per_head(a, b, head_axes, what)
     rms = float(np.sqrt(np.mean(b * b))) if b.size else 0.0
     assert_close(a, b, BF16_RTOL, BF16_FLOOR * rms, what)
+
+
+def assert_close_bf16_intermediates(a, b, what="", head_axes=2):
+    """The precision="bf16" option's documented accuracy (see BF16I_FLOOR)."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    assert a.shape == b.shape, (what, a.shape, b.shape)
+    assert np.all(np.isfinite(a)), f"{what}: non-finite values"
+    _normwise_per_head(a, b, head_axes, what)
+    rms = float(np.sqrt(np.mean(b * b))) if b.size else 0.0
+    assert_close(a, b, BF16_RTOL, BF16I_FLOOR * rms, what)
 
 
 def assert_close_normwise(a, b, rtol, what=""):

@@ -143,6 +143,36 @@ def test_chunk_fwd_noalloc_size_limit():
     assert LIB.gdn2_chunk_fwd_noalloc(ctypes.byref(a), None) == _lib.GDN2_EINVAL
 
 
+def test_selftest_wait_argument_errors():
+    from burn_gdn2 import LIB, _lib
+
+    done = ctypes.c_int32(-1)
+    assert LIB.gdn2_selftest_wait(0, 0, ctypes.byref(done)) == _lib.GDN2_EINVAL
+    assert LIB.gdn2_selftest_wait((1 << 24) + 1, 0, ctypes.byref(done)) == _lib.GDN2_EINVAL
+    assert LIB.gdn2_selftest_wait(10, 0, None) == _lib.GDN2_EINVAL
+    assert done.value == -1
+
+
+def test_chunk_precision_argument():
+    from burn_gdn2 import LIB, _lib
+
+    a = _chunk_args(precision=5)
+    ws = ctypes.create_string_buffer(256)
+    assert LIB.gdn2_chunk_fwd(ctypes.byref(a), ctypes.addressof(ws), 256, None) == _lib.GDN2_EINVAL
+    assert "precision" in LIB.gdn2_last_error().decode()
+    assert LIB.gdn2_chunk_fwd_workspace_bytes(ctypes.byref(a)) == 0
+    # K = V = 128, chunk 64: the split-operand records (f32 precision) are larger than the bf16-intermediate ones
+    sizes = {}
+    for prec in (_lib.GDN2_PRECISION_F32, _lib.GDN2_PRECISION_BF16):
+        a = _chunk_args(precision=prec, dtype=_lib.GDN2_DTYPE_BF16)
+        a.dims = _lib.Dims(1, 128, 1, 1, 128, 128)
+        for n in ("q", "k", "v", "g", "b", "w", "out"):
+            setattr(a, n, _lib.View(1 << 20, 128 * 128, 128 * 128, 128))
+        sizes[prec] = LIB.gdn2_chunk_fwd_workspace_bytes(ctypes.byref(a))
+    assert sizes[_lib.GDN2_PRECISION_F32] == 2 * 148480
+    assert sizes[_lib.GDN2_PRECISION_BF16] == 2 * 74752
+
+
 def test_recurrent_argument_errors():
     from burn_gdn2 import LIB, _lib
 

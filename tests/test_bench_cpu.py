@@ -32,8 +32,12 @@ def test_core_bytes_and_flops_per_token_head(K, V, esize, C, nbytes, flops):
 
 
 def test_reference_arm_json_line():
-    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+    import time
+
+    t0 = time.monotonic()
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
                         "--warmup", "0"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    wall = time.monotonic() - t0
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.strip().splitlines() if l.startswith("{")]
     assert len(lines) == 1, r.stdout
@@ -44,6 +48,8 @@ def test_reference_arm_json_line():
     assert d["impl"] == "reference"
     assert d["value"] > 0 and d["unit"] == "tokens/s" and d["higher_is_better"] is True
     assert d["warmup"] >= 3
+    # the line's own per-step time is measured, so its steps fit inside the run
+    assert d["ms_per_step"] * (d["steps"] + d["warmup"]) / 1e3 < wall
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == d["unit"]
