@@ -20,6 +20,10 @@
 // The record parts sit in one stage and are refilled as soon as they are
 // consumed: [W; Qg] (and gamma_last) once MMA1 completed, Aqk and Kd once
 // MMA2 and MMA3 completed, so each copy has the rest of a chunk to land.
+// MMA3 (the recurrence) is issued and committed before MMA2 (the o rows),
+// and the decay of the next chunk is applied to the TMEM master in the same
+// pass that writes the next S images, so the chain from one chunk's MMA1 to
+// the next runs MMA1 -> v_new -> MMA3 -> S images only.
 #include "chunk_x3.cuh"
 
 namespace gdn2 {
@@ -56,9 +60,9 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   float* sRms = reinterpret_cast<float*>(sm + RMS);
   float* sOnw = reinterpret_cast<float*>(sm + ONW);
   const float* sGl = reinterpret_cast<const float*>(sm + GL);
-  // fullA (W, Qg, gamma_last), fullB (Aqk, Kd), mma1, mma2/3, operands ready
+  // fullA (W, Qg, gamma_last), fullB (Aqk, Kd), mma1, mma3 (the state update), operands ready, mma2 (o rows)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
 
   const int hv = blockIdx.y, bb = blockIdx.z;
   const int V = p.V, HALF = V / 2;
@@ -79,6 +83,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
     mbar_init(&bars[4], 256);
+    mbar_init(&bars[5], 1);
     fence_mbar_init();
   }
   umma::fence_before_sync();
@@ -111,8 +116,11 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     prefetch_rec(1);
   }
 
-  // ---- initial state: f32 master in TMEM, hi / lo images in smem ----
+  // ---- initial state: hi / lo images of S in smem, f32 master diag(gamma_last) S in TMEM (the decay that
+  // MMA3 of chunk 0 accumulates onto; every later rescale rides on the S-image pass of the chunk before) ----
   const int kk = 32 * sp + lane;  // key channel = TMEM lane of this thread
+  mbar_wait_bounded(&bars[0], 0);
+  const float gam0 = sGl[kk];
   for (int c16 = 0; c16 < HALF / 16; ++c16) {
     const int col = col0 + 16 * c16;
     float v[16];
@@ -122,7 +130,6 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       const float4 f = src[j];
       v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
     }
-    umma::st16(umma::taddr(tS, 32 * sp, col), v);
     uint4 h0, l0, h1, l1;
     split8(v, h0, l0);
     split8(v + 8, h1, l1);
@@ -131,6 +138,9 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     *reinterpret_cast<uint4*>(sm + S_HI + o1) = h1;
     *reinterpret_cast<uint4*>(sm + S_LO + o0) = l0;
     *reinterpret_cast<uint4*>(sm + S_LO + o1) = l1;
+    #pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= gam0;
+    umma::st16(umma::taddr(tS, 32 * sp, col), v);
   }
   umma::wait_st();
   fence_proxy_async_smem();
@@ -152,10 +162,9 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     for (int b = 0; b < HALF * 4; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + b));
   };
 
-  // o rows of chunk c live in rows 64..127 of D[c & 1] (sub-partitions 2, 3);
-  // their epilogue runs while the tensor core does MMA1 of chunk c + 1.  The
-  // gate rows of a chunk are prefetched to L2 one chunk ahead and read into
-  // registers when its epilogue starts.
+  // o rows of chunk c live in rows 64..127 of D[c & 1] (sub-partitions 2, 3); their epilogue runs during
+  // chunk c + 1, once MMA2 of chunk c completed.  The gate rows of chunk c are read into registers during
+  // chunk c (after the previous epilogue), prefetched to L2 a chunk earlier.
   constexpr int GW = 64 * (int)sizeof(TIN) / 16;  // 16-byte gate words per row half
   const int orow = 32 * (sp - 2) + lane;
   auto gate_row = [&](int c) {
@@ -163,30 +172,33 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
                                           (int64_t)(c * TC_C + orow) * p.gate.s2 + col0);
   };
   auto prefetch_gate = [&](int c) {
-    if (p.fuse_epilogue && orow < min(TC_C, p.T - c * TC_C)) {
+    if (p.fuse_epilogue && c < p.NC && orow < min(TC_C, p.T - c * TC_C)) {
       const char* g = reinterpret_cast<const char*>(gate_row(c));
       for (int b = 0; b < HALF * (int)sizeof(TIN); b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + b));
+    }
+  };
+  uint4 graw[GW];
+  auto load_gate = [&](int c) {
+    if (p.fuse_epilogue && orow < min(TC_C, p.T - c * TC_C)) {
+      const uint4* gp = gate_row(c);
+      #pragma unroll
+      for (int j = 0; j < GW; ++j)
+        if (j * 16 < HALF * (int)sizeof(TIN)) graw[j] = gp[j];
+    }
+  };
+  auto gate_at = [&](int j) -> float {  // gate element j of this row half
+    if constexpr (sizeof(TIN) == 2) {
+      const uint32_t w32 = reinterpret_cast<const uint32_t*>(graw)[j >> 1];
+      return __uint_as_float((j & 1) ? (w32 & 0xffff0000u) : (w32 << 16));
+    } else {
+      return reinterpret_cast<const float*>(graw)[j];
     }
   };
   auto epilogue = [&](int c) {
     const int t0 = c * TC_C;
     const int cv = min(TC_C, p.T - t0);
     const uint32_t tD = tD0 + (c & 1) * V;
-    uint4 graw[GW];
-    if (p.fuse_epilogue && orow < cv) {
-      const uint4* gp = gate_row(c);
-      #pragma unroll
-      for (int j = 0; j < GW; ++j)
-        if (j * 16 < HALF * (int)sizeof(TIN)) graw[j] = gp[j];
-    }
-    auto gate_at = [&](int j) -> float {  // gate element j of this row half
-      if constexpr (sizeof(TIN) == 2) {
-        const uint32_t w32 = reinterpret_cast<const uint32_t*>(graw)[j >> 1];
-        return __uint_as_float((j & 1) ? (w32 & 0xffff0000u) : (w32 << 16));
-      } else {
-        return reinterpret_cast<const float*>(graw)[j];
-      }
-    };
+    // MMA2 of chunk c has completed: thread 0 waited for it before the barrier that closed chunk c
     float ov[64];
     #pragma unroll
     for (int c16 = 0; c16 < 4; ++c16)
@@ -235,16 +247,23 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       }
     }
   };
-  if (sp >= 2) prefetch_gate(0);
-  else prefetch_u(0);
+  if (sp >= 2) {
+    load_gate(0);
+    prefetch_gate(1);
+  } else {
+    prefetch_u(0);
+  }
 
+  // Every mbarrier wait below is on a phase that cannot be overtaken by the next one before the waiting thread
+  // passes the barrier closing the chunk (each next phase needs work issued after that barrier), so the
+  // parity waits are unambiguous; only thread 0 waits for the [W; Qg] copy of the chunk it starts.
   for (int c = 0; c < p.NC; ++c) {
     const uint32_t tD = tD0 + (c & 1) * V;
-    mbar_wait_bounded(&bars[0], c & 1);  // [W; Qg] and gamma_last of chunk c
-    umma::fence_after_sync();
 
-    // MMA1: D = [W; Qg] S
+    // MMA1: D = [W; Qg] S  (the master already holds diag(gamma_last) S for MMA3)
     if (tid == 0) {
+      mbar_wait_bounded(&bars[0], c & 1);  // [W; Qg] and gamma_last of chunk c
+      umma::fence_after_sync();
       prefetch_rec(c + 2);
       const uint64_t dsh = umma::desc_mnmaj_base(sbase + S_HI, TC_K), dsl = umma::desc_mnmaj_base(sbase + S_LO, TC_K);
       const uint64_t dwh = umma::desc_kmaj_base(sbase + WQ), dwl = umma::desc_kmaj_base(sbase + WQ + 32768);
@@ -257,31 +276,14 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       }
       umma::commit(&bars[2]);
     }
-    // meanwhile: S <- diag(gamma_last) S in TMEM (all warps), then the epilogue of the previous chunk
-    // (sub-partitions 2, 3)
-    {
-      const float gam = sGl[(c & 1) * 128 + kk];
-      for (int b32 = 0; b32 < HALF; b32 += 32) {
-        float v[2][16];
-        #pragma unroll
-        for (int c16 = 0; c16 < 2; ++c16) umma::ld16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
-        umma::wait_ld();
-        #pragma unroll
-        for (int c16 = 0; c16 < 2; ++c16) {
-          #pragma unroll
-          for (int j = 0; j < 16; ++j) v[c16][j] *= gam;
-          umma::st16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
-        }
-      }
-      umma::wait_st();
-    }
     if (sp >= 2) {
-      umma::fence_before_sync();
+      // the epilogue of the previous chunk while the tensor core does MMA1, then the next gate rows
       mbar_arrive(&bars[4]);
-      if (c + 1 < p.NC) prefetch_gate(c + 1);
       if (c > 0) epilogue(c - 1);
+      load_gate(c);
+      prefetch_gate(c + 1);
     } else {
-      float u[64];
+      float u[64];  // U rows of this chunk: read while MMA1 runs
       {
         const float4* src = u_row(c);
         #pragma unroll
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       if (c + 1 < p.NC) prefetch_u(c + 1);
     }
 
-    // MMA2: D += [*; Aqk] v_new ; MMA3: S += Kd^T v_new
+    // MMA3: S += Kd^T v_new (the recurrence: committed on its own), then MMA2: D += [*; Aqk] v_new (the o rows)
     if (tid == 0) {
       mbar_wait_bounded(&bars[4], c & 1);
       mbar_wait_bounded(&bars[1], c & 1);
@@ -338,25 +340,31 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       const uint64_t dkh = umma::desc_mnmaj_base(sbase + KD_HI, TC_C), dkl = umma::desc_mnmaj_base(sbase + KD_LO, TC_C);
       #pragma unroll 1
       for (int pass = 0; pass < 3; ++pass) {
-        const uint64_t da = pass == 1 ? dtl : dth, db = pass == 2 ? dvl : dvh;
-        #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          umma::mma_bf16(tD, umma::desc_kmaj_at(da, 128, j), umma::desc_mnmaj_at(db, j), i1, true);
-      }
-      #pragma unroll 1
-      for (int pass = 0; pass < 3; ++pass) {
         const uint64_t da = pass == 1 ? dkl : dkh, db = pass == 2 ? dvl : dvh;
         #pragma unroll
         for (int j = 0; j < 4; ++j)
           umma::mma_bf16(tS, umma::desc_mnmaj_at(da, j), umma::desc_mnmaj_at(db, j), i3, true);
       }
       umma::commit(&bars[3]);
+      #pragma unroll 1
+      for (int pass = 0; pass < 3; ++pass) {
+        const uint64_t da = pass == 1 ? dtl : dth, db = pass == 2 ? dvl : dvh;
+        #pragma unroll
+        for (int j = 0; j < 4; ++j)
+          umma::mma_bf16(tD, umma::desc_kmaj_at(da, 128, j), umma::desc_mnmaj_at(db, j), i1, true);
+      }
+      umma::commit(&bars[5]);
     }
     mbar_wait_bounded(&bars[3], c & 1);
     umma::fence_after_sync();
-    if (tid == 0 && c + 1 < p.NC) issueB(c + 1);  // MMA2 / MMA3 have read Aqk and Kd
 
-    // S (now S_{c+1}) -> hi / lo images for the next chunk
+    // S_{c+1} -> hi / lo images for MMA1 of the next chunk, and the master rescaled by that chunk's gamma_last
+    const bool more = c + 1 < p.NC;
+    float gam = 1.f;
+    if (more) {
+      mbar_wait_bounded(&bars[0], (c + 1) & 1);  // gamma_last of chunk c + 1 (issued with its [W; Qg])
+      gam = sGl[((c + 1) & 1) * 128 + kk];
+    }
     for (int b32 = 0; b32 < HALF; b32 += 32) {
       float v[2][16];
       #pragma unroll
@@ -373,7 +381,17 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
         *reinterpret_cast<uint4*>(sm + S_HI + o1) = h1;
         *reinterpret_cast<uint4*>(sm + S_LO + o0) = l0;
         *reinterpret_cast<uint4*>(sm + S_LO + o1) = l1;
+        if (more) {
+          #pragma unroll
+          for (int j = 0; j < 16; ++j) v[c16][j] *= gam;
+          umma::st16(umma::taddr(tS, 32 * sp, col0 + b32 + 16 * c16), v[c16]);
+        }
       }
+    }
+    if (more) umma::wait_st();
+    if (tid == 0) {
+      mbar_wait_bounded(&bars[5], c & 1);  // MMA2 has read Aqk (MMA3 read Kd before it)
+      if (more) issueB(c + 1);
     }
     fence_proxy_async_smem();
     umma::fence_before_sync();
