@@ -47,6 +47,7 @@ struct TcParams {
   float* state;
   unsigned char* rec;  // NC records per (b, hv), record bytes each
   size_t rec_bytes;
+  unsigned char* scratch;  // split-operand intra kernel: one L2-resident slot per CTA (after the records)
 };
 
 int launch_intra_tc(const TcParams& p, cudaStream_t st);

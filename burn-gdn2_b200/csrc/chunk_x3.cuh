@@ -47,6 +47,17 @@ __host__ __device__ inline X3Record x3_record_layout(int V) {
   return r;
 }
 
+// Per-CTA scratch of the intra kernel, in the workspace after the records: the shared-memory images of the
+// second score pass (row tiles 1 and 2) and rhs_k / rhs_v, written in the chunk's single pass over its rows
+// and brought back by bulk copies.  At most X3_SLOTS CTAs (two per SM of a B200) run, so the slots of all of
+// them (about 40 MB) stay resident in L2 while they are reused chunk after chunk.
+constexpr size_t X3_SLOT_PASSB = 73728;
+constexpr size_t X3_SLOT_BYTES = X3_SLOT_PASSB + 65536;
+constexpr int X3_SLOTS = 2 * 148;
+inline size_t x3_scratch_bytes(long long items) {
+  return (size_t)(items < X3_SLOTS ? items : X3_SLOTS) * X3_SLOT_BYTES;
+}
+
 bool x3_supported(int K, int V, int C);
 int launch_intra_x3(const TcParams& p, int dtype, cudaStream_t st);
 int launch_inter_x3(const TcParams& p, int dtype, cudaStream_t st);
@@ -68,17 +79,24 @@ __device__ __forceinline__ f32x2 f2sub(f32x2 a, f32x2 b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
-// x -> (hi, lo) bf16 pairs with hi = bf16(x), lo = bf16(x - hi); x - hi is exact in f32
+// (x0, x1) -> (hi, lo) bf16 pairs with hi = bf16(x), lo = bf16(x - hi); x - hi is exact in f32.  Plain
+// 32-bit operations: two conversions, two masks, two subtractions.
+__device__ __forceinline__ void split2f(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+  const float l0 = x0 - __uint_as_float(hi << 16), l1 = x1 - __uint_as_float(hi & 0xffff0000u);
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(l1), "f"(l0));
+}
 __device__ __forceinline__ void split2(f32x2 x, uint32_t& hi, uint32_t& lo) {
-  hi = f2bf2(x);
-  lo = f2bf2(f2sub(x, bf2f2(hi)));
+  float x0, x1;
+  f2un(x, x0, x1);
+  split2f(x0, x1, hi, lo);
 }
 // 8 consecutive f32 -> hi and lo images of 8 bf16 (one 16-byte chunk each)
 __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
-  split2(f2pk(v[0], v[1]), hi.x, lo.x);
-  split2(f2pk(v[2], v[3]), hi.y, lo.y);
-  split2(f2pk(v[4], v[5]), hi.z, lo.z);
-  split2(f2pk(v[6], v[7]), hi.w, lo.w);
+  split2f(v[0], v[1], hi.x, lo.x);
+  split2f(v[2], v[3], hi.y, lo.y);
+  split2f(v[4], v[5], hi.z, lo.z);
+  split2f(v[6], v[7], hi.w, lo.w);
 }
 
 // Four consecutive input elements of one row as two f32 pairs, read with a
