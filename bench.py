@@ -325,6 +325,8 @@ def run_ours(args):
     decode = run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world)
     # ---- whole layer forward_train (projections on cuBLAS + the core) ----
     layer = run_layer(torch, bg, dev, stream, args, max_over_ranks, world) if not args.core_only else None
+    layer_fast = (run_layer(torch, bg, dev, stream, args, max_over_ranks, world, precision="bf16")
+                  if not args.core_only else None)
     # ---- N > 1: one config-2 layer split by heads, o_proj all-reduce timed apart ----
     layer_tp = run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world) if world > 1 else None
     # ---- BASELINE configs 1, 4 and 5 ----
@@ -371,6 +373,7 @@ def run_ours(args):
             "bf16_intermediates": core_line(fast, peaks, "bf16", "bf16") if fast else None,
             "decode": decode,
             "layer": layer,
+            "layer_bf16_intermediates": layer_fast,
             "layer_head_sharded": layer_tp,
             "other_configs": others,
             "gpu_launches": 2 * args.steps,
@@ -393,13 +396,14 @@ def ncu_traffic(key):
     return None
 
 
-def run_layer(torch, bg, dev, stream, args, max_over_ranks, world):
+def run_layer(torch, bg, dev, stream, args, max_over_ranks, world, precision="f32"):
     """GatedDeltaNet2.forward_train at BASELINE config 2 (hidden 2048,
     16 x 128 heads, chunk 64, bf16, B=8, T=4096): tokens/s and the fraction
-    of the dense bf16 tensor-core peak the whole layer reaches."""
+    of the dense bf16 tensor-core peak the whole layer reaches, with the
+    core's intermediates at `precision`."""
     c = CFG2
     cfg = bg.Gdn2Config(hidden_size=2048, num_heads=16, head_dim=128, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
-    m = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=0)
+    m = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=0, precision=precision)
     g = torch.Generator(device=dev).manual_seed(11)
     x = torch.randn(c["B"], c["T"], 2048, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     for _ in range(2):
@@ -421,7 +425,7 @@ def run_layer(torch, bg, dev, stream, args, max_over_ranks, world):
     core_flops = core_flops_per_token_head(128, 128, 64) * tokens * 16
     peaks = load_peaks()
     flops = proj_flops + core_flops
-    return {"value": tokens * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+    return {"value": tokens * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "precision": precision,
             "workload": f"GatedDeltaNet2.forward_train, BASELINE config 2 (D=2048, 16x128 heads, B={c['B']}, T=4096, bf16)",
             "tflops": flops / (ms / 1e3) / 1e12, "tc_frac": flops / (ms / 1e3) / (peaks["bf16_tflops"] * 1e12),
             "flops_per_step": flops}
@@ -580,7 +584,8 @@ def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, se
                 "2-CTA cluster exchanging the gated RMS norm's row sums)")
     else:
         path = ("tensor cores, f32-grade intermediates (k_intra_x3 + k_inter_x3)" if V <= 128 else
-                "CUDA cores, exact f32 (k_intra_simt + k_inter_simt + k_chunk_out)")
+                "tensor cores, f32-grade intermediates (k_intra_x3 with U in two 128-column halves; k_inter_x3 over "
+                "two 128-column slices per chain, a 2-CTA cluster exchanging the gated RMS norm's row sums)")
     return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "precision": precision,
             "workload": f"BASELINE {name} chunk core: B={B} (per rank), T={T}, H={H}, HV={HV}, K={K}, V={V}, bf16",
             "path": path,

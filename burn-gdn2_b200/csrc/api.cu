@@ -107,7 +107,7 @@ static size_t rec_bytes(const gdn2_dims& d, bool x3) {
 
 static size_t tc_workspace_bytes(const gdn2_dims& d, bool x3) {
   const size_t nch = (size_t)d.batch * d.num_v_heads * ((d.seq_len + TC_C - 1) / TC_C);
-  return nch * rec_bytes(d, x3) + (x3 ? x3_scratch_bytes((long long)nch) : 0);
+  return nch * rec_bytes(d, x3) + (x3 ? x3_scratch_bytes((long long)nch, d.head_v_dim) : 0);
 }
 
 static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, const char* fn, bool x3) {

@@ -1,11 +1,14 @@
 // Kernel (2), split-operand form: chunk-inter for bf16 or f32 inputs,
-// K = 128, C = 64, V in {64, 128}, with the SiLU-gated RMS-norm epilogue
+// K = 128, C = 64, V in {64, 128, 256}, with the SiLU-gated RMS-norm epilogue
 // fused, f32-grade intermediates (chunk_x3.cuh).
 //
 // Replaces gdn2_chunk_inter_kernel (src/kernel/chunk_cube.rs:300-610); math
 // of src/forward.rs:263-274 with the epilogue of src/module.rs:501-517.
-// One CTA (8 warps, one per SM) per (value head, batch) walks the chunks in
-// order.  The state S [K][V] stays in TMEM in f32 for the whole sequence;
+// One CTA (8 warps, one per SM) per (value-column slice, value head, batch)
+// walks the chunks in order; V <= 128 is one slice, V = 256 two slices of
+// 128 columns (the value columns of the recurrence are independent), whose
+// CTAs form a 2-CTA cluster that exchanges the RMS norm's row sums through
+// distributed shared memory.  The state S [K][V] stays in TMEM in f32 for the whole sequence;
 // its hi and lo bf16 images in shared memory are the MMA operands.  Per
 // chunk (every product as three MMAs: hi.hi + lo.hi + hi.lo):
 //   MMA1  D = [W; Qg] S                      (M=128, N=V, K=128)
@@ -42,7 +45,9 @@ constexpr uint32_t VN_LO = VN_HI + 16384;
 constexpr uint32_t RMS = VN_LO + 16384;   // f32 [64][2]
 constexpr uint32_t ONW = RMS + 512;       // f32 [V]
 constexpr uint32_t BARS = ONW + 512;
-constexpr uint32_t TOTAL = BARS + 128;
+constexpr uint32_t XSUM = BARS + 128;   // f32 [2][64]: the peer slice's row sums, by chunk parity (V = 256)
+constexpr uint32_t XBARS = XSUM + 512;  // 2 mbarriers: the peer's 128 epilogue threads arrived, by chunk parity
+constexpr uint32_t TOTAL = XBARS + 64;
 }  // namespace nx3
 
 __device__ __forceinline__ void named_bar_x3(int id, int nthreads) {
@@ -52,7 +57,9 @@ __device__ __forceinline__ void named_bar_x3(int id, int nthreads) {
 // SiLU in f32: g sigma(g) with the MUFU exponential and a fast divide (a few ulp)
 __device__ __forceinline__ float silu_acc(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-template <typename TIN>
+// XCHG: V = 256 as two 128-column CTAs per chain (a 2-CTA cluster) that exchange the RMS norm's row sums;
+// a separate instantiation keeps the one-slice kernel free of that code.
+template <typename TIN, bool XCHG>
 __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   using namespace nx3;
   extern __shared__ __align__(1024) unsigned char smraw[];
@@ -64,14 +71,19 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
 
+  float* sXsum = reinterpret_cast<float*>(sm + XSUM);
+  uint64_t* xbars = reinterpret_cast<uint64_t*>(sm + XBARS);
+
   const int hv = blockIdx.y, bb = blockIdx.z;
-  const int V = p.V, HALF = V / 2;
+  const int V = p.vt, HALF = V / 2;               // columns of this CTA's slice
+  const int VF = p.V, cbase = blockIdx.x * p.vt;  // full row width, first column of the slice
+  const uint32_t peer = blockIdx.x ^ 1u;          // cluster rank of the other slice's CTA (XCHG)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sp = warp & 3, half = warp >> 2;
   const int col0 = half * HALF;
-  const X3Record L = x3_record_layout(V);
+  const X3Record L = x3_record_layout(VF);
   const unsigned char* recs = p.rec + ((size_t)bb * p.HV + hv) * p.NC * p.rec_bytes;
-  float* st = p.state + ((size_t)bb * p.HV + hv) * (size_t)TC_K * V;
+  float* st = p.state + ((size_t)bb * p.HV + hv) * (size_t)TC_K * VF + cbase;
   const uint32_t sbase = smem_u32(sm);
 
   if (warp == 0) {
@@ -79,15 +91,18 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     umma::tmem_relinquish();
   }
   if (p.fuse_epilogue)
-    for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[i];
+    for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[cbase + i];
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
     mbar_init(&bars[4], 256);
     mbar_init(&bars[5], 1);
+    mbar_init(&xbars[0], 128);
+    mbar_init(&xbars[1], 128);
     fence_mbar_init();
   }
   umma::fence_before_sync();
   __syncthreads();
+  if (XCHG) cluster_sync_all();  // the peer's exchange barriers are initialised before anyone arrives on them
   umma::fence_after_sync();
   const uint32_t tD0 = *tslot;       // D of even chunks: cols [0, V); odd chunks: [V, 2V)
   const uint32_t tS = tD0 + 2 * V;   // S master: cols [2V, 3V)
@@ -124,7 +139,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   for (int c16 = 0; c16 < HALF / 16; ++c16) {
     const int col = col0 + 16 * c16;
     float v[16];
-    const float4* src = reinterpret_cast<const float4*>(st + (size_t)kk * V + col);
+    const float4* src = reinterpret_cast<const float4*>(st + (size_t)kk * VF + col);
     #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 f = src[j];
@@ -151,11 +166,12 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   const uint32_t i1 = umma::idesc_bf16(128, V, false, true);  // [W;Qg] . S and [*;Aqk] . v_new
   const uint32_t i3 = umma::idesc_bf16(128, V, true, true);   // Kd^T . v_new
 
-  // U row of this thread (sub-partitions 0, 1: row 32 sp + lane, this half's columns) in the record of chunk c;
-  // prefetched to L2 one chunk ahead, read into registers while MMA1 runs
+  // U row of this thread (sub-partitions 0, 1: row 32 sp + lane, this half's columns of this CTA's slice; the
+  // record keeps U slice by slice) in the record of chunk c; prefetched to L2 one chunk ahead, read into
+  // registers while MMA1 runs
   auto u_row = [&](int c) {
     return reinterpret_cast<const float4*>(recs + (size_t)c * p.rec_bytes + L.u +
-                                           ((size_t)(32 * sp + lane) * V + col0) * 4);
+                                           (((size_t)blockIdx.x * 64 + 32 * sp + lane) * V + col0) * 4);
   };
   auto prefetch_u = [&](int c) {
     const char* g = reinterpret_cast<const char*>(u_row(c));
@@ -169,7 +185,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   const int orow = 32 * (sp - 2) + lane;
   auto gate_row = [&](int c) {
     return reinterpret_cast<const uint4*>(static_cast<const TIN*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
-                                          (int64_t)(c * TC_C + orow) * p.gate.s2 + col0);
+                                          (int64_t)(c * TC_C + orow) * p.gate.s2 + cbase + col0);
   };
   auto prefetch_gate = [&](int c) {
     if (p.fuse_epilogue && c < p.NC && orow < min(TC_C, p.T - c * TC_C)) {
@@ -219,13 +235,20 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       f2un(s2[1], s4[2], s4[3]);
       sRms[orow * 2 + half] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       named_bar_x3(1, 128);
-      const float tot = sRms[orow * 2] + sRms[orow * 2 + 1];
-      inv = rsqrtf(tot / (float)V + p.eps);
+      float tot = sRms[orow * 2] + sRms[orow * 2 + 1];
+      if (XCHG) {  // add the other slice's sum of this row (both halves of a row send the same value)
+        const int par = c & 1;
+        st_cluster_f32(cluster_addr(sXsum + par * 64 + orow, peer), tot);
+        mbar_arrive_cluster(cluster_addr(&xbars[par], peer));
+        mbar_wait_cluster_bounded(&xbars[par], (c >> 1) & 1);
+        tot += sXsum[par * 64 + orow];
+      }
+      inv = rsqrtf(tot / (float)VF + p.eps);
       named_bar_x3(1, 128);  // sRms reusable
     }
     if (orow < cv) {
       TIN* op = static_cast<TIN*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
-                (int64_t)(t0 + orow) * p.out.s2 + col0;
+                (int64_t)(t0 + orow) * p.out.s2 + cbase + col0;
       #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if (8 * j >= HALF) break;
@@ -406,24 +429,38 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     float v[16];
     umma::ld16(umma::taddr(tS, 32 * sp, col), v);
     umma::wait_ld();
-    float4* dst = reinterpret_cast<float4*>(st + (size_t)kk * V + col);
+    float4* dst = reinterpret_cast<float4*>(st + (size_t)kk * VF + col);
     #pragma unroll
     for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
   umma::fence_before_sync();
   __syncthreads();
+  if (XCHG) cluster_sync_all();  // no CTA leaves while its peer may still reach its shared memory
   if (warp == 0) umma::tmem_dealloc(tD0, 512);
 }
 
 template <typename TIN>
 static int launch_inter_x3_t(const TcParams& p, cudaStream_t st) {
   const size_t smem = nx3::TOTAL + 1024;
-  cudaError_t e =
-      cudaFuncSetAttribute((const void*)k_inter_x3<TIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const bool xchg = p.vsplit > 1 && p.fuse_epilogue;  // the slices of a chain exchange row sums: one cluster each
+  void (*fn)(const TcParams) = xchg ? k_inter_x3<TIN, true> : k_inter_x3<TIN, false>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "chunk inter (x3) smem attribute");
-  dim3 grid(1, p.HV, p.B);
-  k_inter_x3<TIN><<<grid, 256, smem, st>>>(p);
-  return check_cuda(cudaGetLastError(), "chunk inter (x3) launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.vsplit, p.HV, p.B);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (xchg) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.vsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return check_cuda(cudaLaunchKernelEx(&cfg, fn, p), "chunk inter (x3) launch");
 }
 
 int launch_inter_x3(const TcParams& p, int dtype, cudaStream_t st) {

@@ -115,7 +115,9 @@ __device__ __forceinline__ void put_split4(unsigned char* hi, size_t dlo, f32x2 
 // Persistent: two CTAs per SM walk the chunk items item = blockIdx.x + i * gridDim.x (item = ((b * HV + hv) *
 // NC + chunk)).  TMEM is allocated once per CTA; the next chunk's input rows are pulled into L2 while a chunk
 // computes; the record's bulk copies of one chunk drain while the next chunk loads its rows.
-template <typename TIN>
+// V256: V = 256, rhs_v and U in two 128-column halves (a separate instantiation keeps the V <= 128 kernel free
+// of the second half's loads and MMAs).
+template <typename TIN, bool V256>
 __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitems) {
   using namespace ix3;
   constexpr uint32_t TCOLS = 256;   // score D [0, 128), then W [0, 128) and U [128, 128 + V)
@@ -123,11 +125,13 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
   unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
   float* sHalf = reinterpret_cast<float*>(sm + MISC);  // [8][128] g sums of each 8-row half tile
   float* sGlast = sHalf + 8 * 128;
-  // score MMAs of tiles 0 / 3, of tiles 1 / 2, W / U MMAs, the slot's score image, the slot's rhs images
+  // score MMAs of tiles 0 / 3, of tiles 1 / 2, W / U MMAs, the slot's score image, the slot's rhs images,
+  // (V = 256) the slot's second rhs_v half, the second U MMA
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGlast + 128);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 7);
 
   const int V = p.V;
+  const int VU = V256 ? 128 : V;  // value columns of one rhs_v / U half
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tp = warp >> 1, hh = warp & 1;  // row tile, half of it (rows 16 tp + 8 hh + i)
   const int r0 = tp * 16 + hh * 8;
@@ -138,7 +142,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
   const int cx = (ch & 63) >> 3, kb = ch >> 6, eb = (ch & 7) * 2, rg = r0 >> 3;
 
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     // ---- 2. one pass over this warp's rows: every operand of the chunk.  Row tiles 0 and 3 (X and Ks images)
     // go to the shared buffer of the first score pass; row tiles 1 and 2 to this CTA's scratch slot, laid out
     // as the buffer of the second pass; rhs_k / rhs_v to the slot too; Qg and Kd into the record. ----
-    unsigned char* const slot = p.scratch + (size_t)blockIdx.x * X3_SLOT_BYTES;
+    unsigned char* const slot = p.scratch + (size_t)blockIdx.x * x3_slot_bytes(V);
     {
       f32x2 cks2[4][2], eGbpS2[2], edk2[2];
       {
@@ -244,12 +248,15 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
       unsigned char* const rkr = slot + X3_SLOT_PASSB + RK_HI + kb * 64 * 128 + rg * 1024 + eb;
       unsigned char* const rvr = slot + X3_SLOT_PASSB + RV_HI + kb * 64 * 128 + rg * 1024 + eb;
       float gl[4] = {off[0], off[1], off[2], off[3]};
-      Raw4<TIN> nq, nk, nb, nv, nw;
+      Raw4<TIN> nq, nk, nb, nv, nw, nv2, nw2;  // nv2, nw2: value channels 128 + ch (V = 256)
       float4 ng;
       auto fetch = [&](int i) {
         const int r = r0 + i;
         ng = g_row(i);
         nq.zero(); nk.zero(); nb.zero(); nv.zero(); nw.zero();
+        if (V256) {
+          nv2.zero(); nw2.zero();
+        }
         if (r < cv) {
           nq.load(vptr<TIN>(p.q, bb, kh, t0 + r, ch));
           nk.load(vptr<TIN>(p.k, bb, kh, t0 + r, ch));
@@ -258,12 +265,16 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
             nv.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch));
             nw.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch));
           }
+          if (V256) {
+            nv2.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch + 128));
+            nw2.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch + 128));
+          }
         }
       };
       fetch(0);
       #pragma unroll 1
       for (int i = 0; i < 8; ++i) {
-        const Raw4<TIN> cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw;
+        const Raw4<TIN> cq = nq, ck = nk, cb = nb, cvv = nv, cw = nw, cv2 = nv2, cw2 = nw2;
         gl[0] += ng.x; gl[1] += ng.y; gl[2] += ng.z; gl[3] += ng.w;
         if (i + 1 < 8) fetch(i + 1);
         const uint32_t ro = (uint32_t)(i * 128 + ((cx ^ i) << 4));
@@ -289,6 +300,8 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
         put_split4(kdr + ro, L.kd_lo - L.kd_hi, f2mul(kinv2[0], edk2[0]), f2mul(kinv2[1], edk2[1]));
         put_split4(rkr + ro, RK_LO - RK_HI, f2mul(bks2[0], eGbp2[0]), f2mul(bks2[1], eGbp2[1]));
         if (ch < V) put_split4(rvr + ro, RV_LO - RV_HI, f2mul(cw.pair(0), cvv.pair(0)), f2mul(cw.pair(1), cvv.pair(1)));
+        if (V256)  // the second rhs_v half, 32 KB after the first in the slot
+          put_split4(rvr + 32768 + ro, RV_LO - RV_HI, f2mul(cw2.pair(0), cv2.pair(0)), f2mul(cw2.pair(1), cv2.pair(1)));
       }
     }
     if (warp == 0) {
@@ -475,13 +488,13 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     __syncthreads();
 
     // ---- 4. rhs_k and rhs_v back from the slot (one bulk copy), then W = T rhs_k, U = T rhs_v ----
-    if (tid == 0) {  // W into the score columns [0, 128) (read out above), U into [128, 128 + V)
+    if (tid == 0) {  // W into the score columns [0, 128) (read out above), U into [128, 128 + VU)
       mbar_arrive_expect_tx(&bars[4], 65536u);
       bulk_g2s(sm + RK_HI, slot + X3_SLOT_PASSB, 65536u, &bars[4]);
       mbar_wait_bounded(&bars[4], par);
       const uint32_t sbase = smem_u32(sm);
       const uint32_t iw = umma::idesc_bf16(64, 128, false, true);
-      const uint32_t iu = umma::idesc_bf16(64, V, false, true);
+      const uint32_t iu = umma::idesc_bf16(64, VU, false, true);
       #pragma unroll 1
       for (int ps = 0; ps < 3; ++ps) {
         const uint64_t dt = umma::desc_kmaj_base(sbase + (ps == 1 ? TI_LO : TI_HI));
@@ -499,11 +512,32 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     mbar_wait_bounded(&bars[2], par);
     umma::fence_after_sync();
 
-    // ---- 5. W (hi / lo images) and U (f32) staged in shared memory (warp w: sub-partition w % 4, column
-    // half w / 4), then bulk copies into the record (they drain while the next chunk starts) ----
+    // ---- 5. W (hi / lo images) and U (f32, one 128-column slice at a time) staged in shared memory (warp w:
+    // sub-partition w % 4, column half w / 4), then bulk copies into the record (they drain while the next
+    // chunk starts) ----
+    const int sp = warp & 3, half = warp >> 2;
+    const int r = 16 * sp + lane;  // valid for lane < 16
+    auto stage_u = [&](unsigned char* dst) {  // U columns [128, 128 + VU) of TMEM -> UST -> the record at dst
+      for (int c16 = 0; c16 < VU / 32; ++c16) {
+        const int col = half * (VU / 2) + 16 * c16;
+        float v[16];
+        umma::ld16(umma::taddr(tA, 32 * sp, 128 + col), v);
+        umma::wait_ld();
+        if (lane < 16) {
+          float4* urow = reinterpret_cast<float4*>(sm + UST + (size_t)r * VU * 4 + col * 4);
+          #pragma unroll
+          for (int j = 0; j < 4; ++j) urow[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      umma::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        bulk_s2g(dst, sm + UST, (unsigned)(64 * VU * 4));
+        bulk_commit();
+      }
+    };
     {
-      const int sp = warp & 3, half = warp >> 2;
-      const int r = 16 * sp + lane;  // valid for lane < 16
       #pragma unroll
       for (int c16 = 0; c16 < 4; ++c16) {
         const int col = half * 64 + 16 * c16;
@@ -521,28 +555,39 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
           *reinterpret_cast<uint4*>(sm + WST_LO + o1) = l1;
         }
       }
-      for (int c16 = 0; c16 < V / 32; ++c16) {
-        const int col = half * (V / 2) + 16 * c16;
-        float v[16];
-        umma::ld16(umma::taddr(tA, 32 * sp, 128 + col), v);
-        umma::wait_ld();
-        if (lane < 16) {
-          float4* urow = reinterpret_cast<float4*>(sm + UST + (size_t)r * V * 4 + col * 4);
-          #pragma unroll
-          for (int j = 0; j < 4; ++j) urow[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        }
-      }
-      fence_proxy_async_smem();
-      umma::fence_before_sync();
-      __syncthreads();
+      stage_u(rec + L.u);  // its proxy fence and barrier also cover the W images
       if (tid == 0) {
         bulk_s2g(rec + L.wq_hi, sm + WST_HI, 8192u);
         bulk_s2g(rec + L.wq_hi + 16384, sm + WST_HI + 8192, 8192u);
         bulk_s2g(rec + L.wq_lo, sm + WST_LO, 8192u);
         bulk_s2g(rec + L.wq_lo + 16384, sm + WST_LO + 8192, 8192u);
-        bulk_s2g(rec + L.u, sm + UST, (unsigned)(64 * V * 4));
         bulk_commit();
       }
+    }
+    if (V256) {
+      // the second rhs_v half into the rhs_v tiles (which the U staging shares: wait for its copy to read it),
+      // U columns 128..255 into the same TMEM columns, staged and copied as the record's second U slice
+      if (tid == 0) {
+        umma::fence_after_sync();  // the first U half is read out of TMEM
+        bulk_wait_read_all();
+        mbar_arrive_expect_tx(&bars[5], 32768u);
+        bulk_g2s(sm + RV_HI, slot + X3_SLOT_PASSB + 65536, 32768u, &bars[5]);
+        mbar_wait_bounded(&bars[5], par);
+        const uint32_t sbase = smem_u32(sm);
+        const uint32_t iu = umma::idesc_bf16(64, 128, false, true);
+        #pragma unroll 1
+        for (int ps = 0; ps < 3; ++ps) {
+          const uint64_t dt = umma::desc_kmaj_base(sbase + (ps == 1 ? TI_LO : TI_HI));
+          const uint64_t drv = umma::desc_mnmaj_base(sbase + (ps == 2 ? RV_LO : RV_HI), 64);
+          #pragma unroll
+          for (int j = 0; j < 4; ++j)
+            umma::mma_bf16(tA + 128, umma::desc_kmaj_at(dt, 64, j), umma::desc_mnmaj_at(drv, j), iu, ps > 0 || j > 0);
+        }
+        umma::commit(&bars[6]);
+      }
+      mbar_wait_bounded(&bars[6], par);
+      umma::fence_after_sync();
+      stage_u(rec + L.u + 64 * 128 * 4);
     }
     umma::fence_after_sync();
   }  // chunk items
@@ -555,8 +600,8 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
 template <typename TIN>
 static int launch_intra_x3_t(const TcParams& p, cudaStream_t st) {
   const size_t smem = ix3::TOTAL + 1024;
-  cudaError_t e =
-      cudaFuncSetAttribute((const void*)k_intra_x3<TIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  void (*fn)(const TcParams, int) = p.V > 128 ? k_intra_x3<TIN, true> : k_intra_x3<TIN, false>;
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "chunk intra (x3) smem attribute");
   int dev = 0, sms = 0;
   e = cudaGetDevice(&dev);
@@ -566,7 +611,7 @@ static int launch_intra_x3_t(const TcParams& p, cudaStream_t st) {
   if (items > 0x7fffffffLL) return set_error(GDN2_EUNSUPPORTED, "chunk intra (x3): %lld chunk items", items);
   const long long slots = 2LL * sms;  // two CTAs per SM (87 KB of shared memory, 256 TMEM columns each)
   const int grid = (int)(items < slots ? items : slots);
-  k_intra_x3<TIN><<<grid, 256, smem, st>>>(p, (int)items);
+  fn<<<grid, 256, smem, st>>>(p, (int)items);
   return check_cuda(cudaGetLastError(), "chunk intra (x3) launch");
 }
 
@@ -574,7 +619,7 @@ int launch_intra_x3(const TcParams& p, int dtype, cudaStream_t st) {
   return dtype == GDN2_DTYPE_BF16 ? launch_intra_x3_t<__nv_bfloat16>(p, st) : launch_intra_x3_t<float>(p, st);
 }
 
-bool x3_supported(int K, int V, int C) { return K == TC_K && C == TC_C && (V == 64 || V == 128); }
+bool x3_supported(int K, int V, int C) { return K == TC_K && C == TC_C && (V == 64 || V == 128 || V == 256); }
 
 GDN2_DEVICE_ERROR_READER(read_device_errors_intra_x3)
 

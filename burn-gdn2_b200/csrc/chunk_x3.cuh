@@ -1,6 +1,6 @@
 // Split-operand ("x3") tensor-core chunk path: the chunk-intra and
 // chunk-inter kernels with f32-grade intermediates, for bf16 or f32 inputs,
-// K = 128 key channels, chunk 64, V in {64, 128}.
+// K = 128 key channels, chunk 64, V in {64, 128, 256}.
 //
 // Every tensor-core operand x that is not exactly a bf16 value is carried as
 // a pair of bf16 images, hi = bf16(x) and lo = bf16(x - hi) (x = hi + lo to
@@ -16,7 +16,8 @@
 //                                     rows 64..127 Qg = scale q gamma
 //   AQK_HI, AQK_LO [64][64] K-major : scale * causal(q k^T decay)
 //   KD_HI, KD_LO [64][128] MN-major : k exp(G_last - G)
-//   U    f32 [64][V] row-major      : (I+Akk)^-1 (w v)
+//   U    f32 [V/128 or 1][64][min(V,128)] : (I+Akk)^-1 (w v), slice by slice
+//                                     of 128 value columns
 //   GL   f32 [128]                  : gamma_last = exp(G_last)
 // AQK_HI directly follows WQ_LO and AQK_LO directly follows AQK_HI: the
 // inter kernel's [*; Aqk] operand of M = 128 takes its first 64 rows from
@@ -48,14 +49,15 @@ __host__ __device__ inline X3Record x3_record_layout(int V) {
 }
 
 // Per-CTA scratch of the intra kernel, in the workspace after the records: the shared-memory images of the
-// second score pass (row tiles 1 and 2) and rhs_k / rhs_v, written in the chunk's single pass over its rows
-// and brought back by bulk copies.  At most X3_SLOTS CTAs (two per SM of a B200) run, so the slots of all of
-// them (about 40 MB) stay resident in L2 while they are reused chunk after chunk.
+// second score pass (row tiles 1 and 2), then rhs_k and rhs_v (value columns 0..127, and 128..255 for
+// V = 256), written in the chunk's single pass over its rows and brought back by bulk copies.  At most
+// X3_SLOTS CTAs (two per SM of a B200) run, so the slots of all of them (40-50 MB) stay resident in L2 while
+// they are reused chunk after chunk.
 constexpr size_t X3_SLOT_PASSB = 73728;
-constexpr size_t X3_SLOT_BYTES = X3_SLOT_PASSB + 65536;
+__host__ __device__ inline size_t x3_slot_bytes(int V) { return X3_SLOT_PASSB + 65536 + (V > 128 ? 32768 : 0); }
 constexpr int X3_SLOTS = 2 * 148;
-inline size_t x3_scratch_bytes(long long items) {
-  return (size_t)(items < X3_SLOTS ? items : X3_SLOTS) * X3_SLOT_BYTES;
+inline size_t x3_scratch_bytes(long long items, int V) {
+  return (size_t)(items < X3_SLOTS ? items : X3_SLOTS) * x3_slot_bytes(V);
 }
 
 bool x3_supported(int K, int V, int C);

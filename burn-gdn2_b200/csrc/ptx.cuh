@@ -71,6 +71,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
   return false;
 }
 
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+// Bounded wait with cluster-scope acquire (the arrivals come from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, unsigned parity) {
+  for (unsigned i = 0; i < MBAR_SPIN_LIMIT; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  atomicOr(&g_device_errors, DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Pairs of f32 in one 64-bit register for the packed sm_100 multiply / fma
 // (mul.rn.f32x2, fma.rn.f32x2: two IEEE round-to-nearest results per
 // instruction, the same values as two scalar instructions).

@@ -254,11 +254,12 @@ def test_short_conv_and_rms_norm_gate_kernels():
     assert_close(y.cpu().numpy(), yr, what="rms", **F32_TOL)
 
 
-@pytest.mark.parametrize("shape", [(2, 3, 190, 128, 64), (1, 2, 64, 128, 128), (2, 2, 1, 128, 128)])
+@pytest.mark.parametrize("shape", [(2, 3, 190, 128, 64), (1, 2, 64, 128, 128), (2, 2, 1, 128, 128),
+                                   (1, 2, 200, 128, 256)])
 @pytest.mark.parametrize("precision", ["f32", "bf16"])
 def test_chunk_tensor_core_path_bf16(shape, precision):
     """bf16, K = 128, chunk 64 (the tcgen05 paths: split-operand for
-    precision "f32", bf16 intermediates for "bf16"), V = 64 / 128, full and
+    precision "f32", bf16 intermediates for "bf16"), V = 64 / 128 / 256, full and
     partial chunks including T = 1; permuted [B,T,H,D] storage views like
     the module's; random initial state; vs the f64 oracle."""
     import burn_gdn2 as bg
@@ -280,12 +281,11 @@ def test_chunk_tensor_core_path_bf16(shape, precision):
     chk(s.cpu().numpy(), s_ref, what="state")
 
 
-@pytest.mark.parametrize("V,precision", [(128, "f32"), (128, "bf16"), (256, "bf16")])
+@pytest.mark.parametrize("V,precision", [(128, "f32"), (128, "bf16"), (256, "f32"), (256, "bf16")])
 def test_chunk_tensor_core_path_is_deterministic(V, precision):
     """The tensor-core chunk paths have no atomics and no order-dependent
     reductions: two calls on the same inputs give bit-identical outputs and
-    states (V = 256 of the bf16-intermediate path runs each chain as two
-    128-column CTAs)."""
+    states (V = 256 runs each chain as two 128-column CTAs)."""
     import burn_gdn2 as bg
 
     B, HV, T, K = 2, 3, 300, 128
@@ -335,8 +335,9 @@ def test_chunk_tensor_core_grouped_heads_and_epilogue(precision):
 def test_chunk_config4_features_bf16():
     """BASELINE config-4 core features at small size: 2 key heads grouped
     over 4 value heads (value head hv reads key head hv // 2), K = 128,
-    V = 256 (with the default precision: the exact-f32 CUDA-core kernels with
-    the separate gated RMS-norm epilogue), neg-eig b in [0, 2], g after the
+    V = 256 (with the default precision: the split-operand tensor-core
+    kernels, each chain as a 2-CTA cluster of 128-column halves that exchange
+    the gated RMS norm's row sums), neg-eig b in [0, 2], g after the
     min_decay 0.9 remap, a partial last chunk; bf16 vs the f64 oracle."""
     import ctypes
     import burn_gdn2 as bg
