@@ -107,18 +107,20 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   const uint32_t tD0 = *tslot;       // D of even chunks: cols [0, V); odd chunks: [V, 2V)
   const uint32_t tS = tD0 + 2 * V;   // S master: cols [2V, 3V)
 
+  // a record is read once (evict-first), or by both CTAs of a cluster at about the same time
+  const uint64_t pol_rec = gridDim.x == 1 ? l2_policy_evict_first() : l2_policy_evict_normal();
   auto issueA = [&](int c) {  // thread 0: [W; Qg] hi / lo and gamma_last of chunk c
     const unsigned char* r = recs + (size_t)c * p.rec_bytes;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[0], 65536u + 512u);
-    bulk_g2s(sm + WQ, r + L.wq_hi, 65536u, &bars[0]);
-    bulk_g2s(sm + GL + (c & 1) * 512, r + L.gl, 512u, &bars[0]);
+    bulk_g2s_hint(sm + WQ, r + L.wq_hi, 65536u, &bars[0], pol_rec);
+    bulk_g2s_hint(sm + GL + (c & 1) * 512, r + L.gl, 512u, &bars[0], pol_rec);
   };
   auto issueB = [&](int c) {  // thread 0: Aqk and Kd hi / lo of chunk c
     const unsigned char* r = recs + (size_t)c * p.rec_bytes;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&bars[1], 49152u);
-    bulk_g2s(sm + AQK, r + L.aqk_hi, 49152u, &bars[1]);
+    bulk_g2s_hint(sm + AQK, r + L.aqk_hi, 49152u, &bars[1], pol_rec);
   };
   // records two chunks ahead are pulled into L2 (one bulk prefetch per chunk), so the stage refills, issued
   // as soon as a part is consumed, read from L2
@@ -169,12 +171,12 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   // U row of this thread (sub-partitions 0, 1: row 32 sp + lane, this half's columns of this CTA's slice; the
   // record keeps U slice by slice) in the record of chunk c; prefetched to L2 one chunk ahead, read into
   // registers while MMA1 runs
-  auto u_row = [&](int c) {
+  auto u_row = [&](int c) {  // the row's start; word k of the row is at k ^ (row & 7)
     return reinterpret_cast<const float4*>(recs + (size_t)c * p.rec_bytes + L.u +
-                                           (((size_t)blockIdx.x * 64 + 32 * sp + lane) * V + col0) * 4);
+                                           ((size_t)blockIdx.x * 64 + 32 * sp + lane) * V * 4);
   };
   auto prefetch_u = [&](int c) {
-    const char* g = reinterpret_cast<const char*>(u_row(c));
+    const char* g = reinterpret_cast<const char*>(u_row(c)) + col0 * 4;
     for (int b = 0; b < HALF * 4; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + b));
   };
 
@@ -309,13 +311,14 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       float u[64];  // U rows of this chunk: read while MMA1 runs
       {
         const float4* src = u_row(c);
+        const int sw = lane & 7;  // = row & 7
         #pragma unroll
         for (int j = 0; j < 16; ++j)
           if (4 * j < HALF) {
             float4 f;
             asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
                 : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
-                : "l"(src + j));
+                : "l"(src + ((col0 / 4 + j) ^ sw)));
             u[4 * j] = f.x; u[4 * j + 1] = f.y; u[4 * j + 2] = f.z; u[4 * j + 3] = f.w;
           }
       }

@@ -69,9 +69,11 @@ constexpr uint32_t MISC = R_END;         // half-tile g sums [8][128] f32, sGlas
 constexpr uint32_t TOTAL = MISC + 4096 + 512 + 64;
 }  // namespace ix3
 
-__device__ __forceinline__ float4 ld_f4_nc_x3(const float* ptr) {
+__device__ __forceinline__ float4 ld_f4_nc_x3(const float* ptr, uint64_t pol) {
   float4 r;
-  asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(ptr));
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+      : "l"(ptr), "l"(pol));
   return r;
 }
 
@@ -110,6 +112,16 @@ __device__ __forceinline__ void put_split4(unsigned char* hi, size_t dlo, f32x2 
   split2(b, h1, l1);
   *reinterpret_cast<uint2*>(hi) = make_uint2(h0, h1);
   *reinterpret_cast<uint2*>(hi + dlo) = make_uint2(l0, l1);
+}
+// the same into global memory with an L2 eviction policy (record lines: written once, read by another kernel)
+__device__ __forceinline__ void put_split4_g(unsigned char* hi, size_t dlo, f32x2 a, f32x2 b, uint64_t pol) {
+  uint32_t h0, l0, h1, l1;
+  split2(a, h0, l0);
+  split2(b, h1, l1);
+  asm volatile("st.global.L2::cache_hint.v2.u32 [%0], {%1, %2}, %3;" ::"l"(hi), "r"(h0), "r"(h1), "l"(pol)
+               : "memory");
+  asm volatile("st.global.L2::cache_hint.v2.u32 [%0], {%1, %2}, %3;" ::"l"(hi + dlo), "r"(l0), "r"(l1), "l"(pol)
+               : "memory");
 }
 
 // Persistent: two CTAs per SM walk the chunk items item = blockIdx.x + i * gridDim.x (item = ((b * HV + hv) *
@@ -153,6 +165,11 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tA = *tslot;
+  // records are read only by the inter kernel, long after: evict-first.  Inputs are read once by this CTA
+  // unless value heads share key heads (then by the CTAs of the other value heads too): evict-first
+  // unless shared.
+  const uint64_t pol_rec = l2_policy_evict_first();
+  const uint64_t pol_in = l2_policy_evict_first(), pol_kin = p.rep == 1 ? pol_in : l2_policy_evict_normal();
 
   int it = 0;
   for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++it) {
@@ -165,7 +182,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
     auto g_row = [&](int i) {
       const int r = r0 + i;
-      return r < cv ? ld_f4_nc_x3(gbase + (int64_t)(t0 + r) * p.g.s2) : make_float4(0.f, 0.f, 0.f, 0.f);
+      return r < cv ? ld_f4_nc_x3(gbase + (int64_t)(t0 + r) * p.g.s2, pol_kin) : make_float4(0.f, 0.f, 0.f, 0.f);
     };
 
     // ---- 1. sums of g over each half tile ----
@@ -258,16 +275,16 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
           nv2.zero(); nw2.zero();
         }
         if (r < cv) {
-          nq.load(vptr<TIN>(p.q, bb, kh, t0 + r, ch));
-          nk.load(vptr<TIN>(p.k, bb, kh, t0 + r, ch));
-          nb.load(vptr<TIN>(p.b, bb, kh, t0 + r, ch));
+          nq.load(vptr<TIN>(p.q, bb, kh, t0 + r, ch), pol_kin);
+          nk.load(vptr<TIN>(p.k, bb, kh, t0 + r, ch), pol_kin);
+          nb.load(vptr<TIN>(p.b, bb, kh, t0 + r, ch), pol_kin);
           if (ch < V) {
-            nv.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch));
-            nw.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch));
+            nv.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch), pol_in);
+            nw.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch), pol_in);
           }
           if (V256) {
-            nv2.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch + 128));
-            nw2.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch + 128));
+            nv2.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch + 128), pol_in);
+            nw2.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch + 128), pol_in);
           }
         }
       };
@@ -296,8 +313,8 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
           if (pp < tp) continue;
           put_split4(ks_row(pp) + ro, 4096 * (pp + 1), f2mul(kinv2[0], cks2[pp][0]), f2mul(kinv2[1], cks2[pp][1]));
         }
-        put_split4(wqr + ro, L.wq_lo - L.wq_hi, f2mul(qs2[0], eGbpS2[0]), f2mul(qs2[1], eGbpS2[1]));
-        put_split4(kdr + ro, L.kd_lo - L.kd_hi, f2mul(kinv2[0], edk2[0]), f2mul(kinv2[1], edk2[1]));
+        put_split4_g(wqr + ro, L.wq_lo - L.wq_hi, f2mul(qs2[0], eGbpS2[0]), f2mul(qs2[1], eGbpS2[1]), pol_rec);
+        put_split4_g(kdr + ro, L.kd_lo - L.kd_hi, f2mul(kinv2[0], edk2[0]), f2mul(kinv2[1], edk2[1]), pol_rec);
         put_split4(rkr + ro, RK_LO - RK_HI, f2mul(bks2[0], eGbp2[0]), f2mul(bks2[1], eGbp2[1]));
         if (ch < V) put_split4(rvr + ro, RV_LO - RV_HI, f2mul(cw.pair(0), cvv.pair(0)), f2mul(cw.pair(1), cvv.pair(1)));
         if (V256)  // the second rhs_v half, 32 KB after the first in the slot
@@ -523,17 +540,18 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
         float v[16];
         umma::ld16(umma::taddr(tA, 32 * sp, 128 + col), v);
         umma::wait_ld();
-        if (lane < 16) {
-          float4* urow = reinterpret_cast<float4*>(sm + UST + (size_t)r * VU * 4 + col * 4);
+        if (lane < 16) {  // 16-byte word k of row r at k ^ (r & 7) (the record's layout; no bank conflicts)
+          float4* urow = reinterpret_cast<float4*>(sm + UST + (size_t)r * VU * 4);
           #pragma unroll
-          for (int j = 0; j < 4; ++j) urow[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int j = 0; j < 4; ++j)
+            urow[(col / 4 + j) ^ (r & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
       }
       fence_proxy_async_smem();
       umma::fence_before_sync();
       __syncthreads();
       if (tid == 0) {
-        bulk_s2g(dst, sm + UST, (unsigned)(64 * VU * 4));
+        bulk_s2g_hint(dst, sm + UST, (unsigned)(64 * VU * 4), pol_rec);
         bulk_commit();
       }
     };
@@ -557,10 +575,10 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
       }
       stage_u(rec + L.u);  // its proxy fence and barrier also cover the W images
       if (tid == 0) {
-        bulk_s2g(rec + L.wq_hi, sm + WST_HI, 8192u);
-        bulk_s2g(rec + L.wq_hi + 16384, sm + WST_HI + 8192, 8192u);
-        bulk_s2g(rec + L.wq_lo, sm + WST_LO, 8192u);
-        bulk_s2g(rec + L.wq_lo + 16384, sm + WST_LO + 8192, 8192u);
+        bulk_s2g_hint(rec + L.wq_hi, sm + WST_HI, 8192u, pol_rec);
+        bulk_s2g_hint(rec + L.wq_hi + 16384, sm + WST_HI + 8192, 8192u, pol_rec);
+        bulk_s2g_hint(rec + L.wq_lo, sm + WST_LO, 8192u, pol_rec);
+        bulk_s2g_hint(rec + L.wq_lo + 16384, sm + WST_LO + 8192, 8192u, pol_rec);
         bulk_commit();
       }
     }

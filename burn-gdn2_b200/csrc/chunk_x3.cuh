@@ -17,7 +17,8 @@
 //   AQK_HI, AQK_LO [64][64] K-major : scale * causal(q k^T decay)
 //   KD_HI, KD_LO [64][128] MN-major : k exp(G_last - G)
 //   U    f32 [V/128 or 1][64][min(V,128)] : (I+Akk)^-1 (w v), slice by slice
-//                                     of 128 value columns
+//                                     of 128 value columns; within a row,
+//                                     16-byte word k is stored at k ^ (row & 7)
 //   GL   f32 [128]                  : gamma_last = exp(G_last)
 // AQK_HI directly follows WQ_LO and AQK_LO directly follows AQK_HI: the
 // inter kernel's [*; Aqk] operand of M = 128 takes its first 64 rows from
@@ -113,6 +114,11 @@ struct Raw4<__nv_bfloat16> {
   __device__ __forceinline__ void load(const void* ptr) {
     asm("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(ptr));
   }
+  __device__ __forceinline__ void load(const void* ptr, uint64_t pol) {  // with an L2 eviction policy
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0, %1}, [%2], %3;"
+        : "=r"(r.x), "=r"(r.y)
+        : "l"(ptr), "l"(pol));
+  }
   __device__ __forceinline__ f32x2 pair(int m) const { return bf2f2(m ? r.y : r.x); }
 };
 template <>
@@ -121,6 +127,11 @@ struct Raw4<float> {
   __device__ __forceinline__ void zero() { r = make_float4(0.f, 0.f, 0.f, 0.f); }
   __device__ __forceinline__ void load(const void* ptr) {
     asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(ptr));
+  }
+  __device__ __forceinline__ void load(const void* ptr, uint64_t pol) {  // with an L2 eviction policy
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+        : "l"(ptr), "l"(pol));
   }
   __device__ __forceinline__ f32x2 pair(int m) const { return m ? f2pk(r.z, r.w) : f2pk(r.x, r.y); }
 };

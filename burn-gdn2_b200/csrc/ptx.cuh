@@ -135,6 +135,16 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, unsigned 
       : "memory");
 }
 
+// The same copy with an L2 eviction policy for the read lines (l2_policy_*, below).
+__device__ __forceinline__ void bulk_g2s_hint(void* sdst, const void* gsrc, unsigned bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(sdst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
 // Bulk prefetch of [gsrc, gsrc + bytes) into L2 (no completion tracking);
 // 16-byte aligned address, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, unsigned bytes) {
@@ -147,6 +157,25 @@ __device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, unsigned 
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
                "r"(bytes)
                : "memory");
+}
+// The same copy with an L2 eviction policy for the written lines (l2_policy_*).
+__device__ __forceinline__ void bulk_s2g_hint(void* gdst, const void* ssrc, unsigned bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;" ::"l"(gdst),
+               "r"(smem_u32(ssrc)), "r"(bytes), "l"(pol)
+               : "memory");
+}
+// L2 eviction policies for the .L2::cache_hint forms.  Lines that are written or read once and not touched
+// again soon (the chunk records, inputs read by one CTA) are marked evict-first, so that L2 keeps the lines
+// that are re-read soon (rows prefetched for the next chunk, per-CTA scratch).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // until every bulk copy this thread committed has read its shared-memory source
