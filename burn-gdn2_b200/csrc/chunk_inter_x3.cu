@@ -57,8 +57,8 @@ __device__ __forceinline__ void named_bar_x3(int id, int nthreads) {
 // SiLU in f32: g sigma(g) with the MUFU exponential and a fast divide (a few ulp)
 __device__ __forceinline__ float silu_acc(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-// XCHG: V = 256 as two 128-column CTAs per chain (a 2-CTA cluster) that exchange the RMS norm's row sums;
-// a separate instantiation keeps the one-slice kernel free of that code.
+// XCHG: a chain as two CTAs of V / 2 columns (a 2-CTA cluster: V = 256, or V = 128 with few chains) that
+// exchange the RMS norm's row sums; a separate instantiation keeps the one-slice kernel free of that code.
 template <typename TIN, bool XCHG>
 __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   using namespace nx3;
@@ -171,12 +171,15 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   // U row of this thread (sub-partitions 0, 1: row 32 sp + lane, this half's columns of this CTA's slice; the
   // record keeps U slice by slice) in the record of chunk c; prefetched to L2 one chunk ahead, read into
   // registers while MMA1 runs
+  // U slice of this CTA (cbase / 128; rows of min(VF, 128) floats), first column of this half in it
+  const int uc = cbase % 128 + col0;
+  const unsigned char* const urow0 =
+      recs + L.u + ((size_t)(cbase / 128) * 64 + 32 * sp + lane) * (VF < 128 ? VF : 128) * 4;
   auto u_row = [&](int c) {  // the row's start; word k of the row is at k ^ (row & 7)
-    return reinterpret_cast<const float4*>(recs + (size_t)c * p.rec_bytes + L.u +
-                                           ((size_t)blockIdx.x * 64 + 32 * sp + lane) * V * 4);
+    return reinterpret_cast<const float4*>(urow0 + (size_t)c * p.rec_bytes);
   };
   auto prefetch_u = [&](int c) {
-    const char* g = reinterpret_cast<const char*>(u_row(c)) + col0 * 4;
+    const char* g = reinterpret_cast<const char*>(u_row(c)) + uc * 4;
     for (int b = 0; b < HALF * 4; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + b));
   };
 
@@ -216,22 +219,24 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     const int t0 = c * TC_C;
     const int cv = min(TC_C, p.T - t0);
     const uint32_t tD = tD0 + (c & 1) * V;
-    // MMA2 of chunk c has completed: thread 0 waited for it before the barrier that closed chunk c
-    float ov[64];
-    #pragma unroll
-    for (int c16 = 0; c16 < 4; ++c16)
-      if (16 * c16 < HALF)
-        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), *reinterpret_cast<float(*)[16]>(ov + 16 * c16));
-    umma::wait_ld();
+    // MMA2 of chunk c has completed: thread 0 waited for it before the barrier that closed chunk c.  The o row
+    // is read from TMEM twice, 16 columns at a time (sum of squares, then the scaled output), so that no
+    // 64-float copy of it is live next to the gate row.
     float inv = 1.f;
     if (p.fuse_epilogue) {
       f32x2 s2[2] = {0ull, 0ull};
       #pragma unroll
-      for (int j = 0; j < 64; j += 2)
-        if (j < HALF) {
+      for (int c16 = 0; c16 < 4; ++c16) {
+        if (16 * c16 >= HALF) break;
+        float ov[16];
+        umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), ov);
+        umma::wait_ld();
+        #pragma unroll
+        for (int j = 0; j < 16; j += 2) {
           const f32x2 o2 = f2pk(ov[j], ov[j + 1]);
           s2[(j >> 1) & 1] = f2fma(o2, o2, s2[(j >> 1) & 1]);
         }
+      }
       float s4[4];
       f2un(s2[0], s4[0], s4[1]);
       f2un(s2[1], s4[2], s4[3]);
@@ -248,26 +253,33 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       inv = rsqrtf(tot / (float)VF + p.eps);
       named_bar_x3(1, 128);  // sRms reusable
     }
-    if (orow < cv) {
-      TIN* op = static_cast<TIN*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
-                (int64_t)(t0 + orow) * p.out.s2 + cbase + col0;
-      #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (8 * j >= HALF) break;
-        float y[8];
+    TIN* op = static_cast<TIN*>(const_cast<void*>(p.out.p)) + bb * p.out.s0 + hv * p.out.s1 +
+              (int64_t)(t0 + orow) * p.out.s2 + cbase + col0;
+    #pragma unroll
+    for (int c16 = 0; c16 < 4; ++c16) {
+      if (16 * c16 >= HALF) break;
+      float ov[16];
+      umma::ld16(umma::taddr(tD, 32 * sp, col0 + 16 * c16), ov);  // warp-wide: before the row guard
+      umma::wait_ld();
+      if (orow < cv) {
         #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int cc = 8 * j + e;
-          y[e] = p.fuse_epilogue ? ov[cc] * inv * sOnw[col0 + cc] * silu_acc(gate_at(cc)) : ov[cc];
-        }
-        if constexpr (sizeof(TIN) == 2) {
-          uint4 pk;
-          pk.x = umma::pack_bf16x2(y[0], y[1]); pk.y = umma::pack_bf16x2(y[2], y[3]);
-          pk.z = umma::pack_bf16x2(y[4], y[5]); pk.w = umma::pack_bf16x2(y[6], y[7]);
-          reinterpret_cast<uint4*>(op)[j] = pk;
-        } else {
-          reinterpret_cast<float4*>(op)[2 * j] = make_float4(y[0], y[1], y[2], y[3]);
-          reinterpret_cast<float4*>(op)[2 * j + 1] = make_float4(y[4], y[5], y[6], y[7]);
+        for (int h = 0; h < 2; ++h) {
+          const int j = 2 * c16 + h;
+          float y[8];
+          #pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int cc = 8 * j + e;
+            y[e] = p.fuse_epilogue ? ov[8 * h + e] * inv * sOnw[col0 + cc] * silu_acc(gate_at(cc)) : ov[8 * h + e];
+          }
+          if constexpr (sizeof(TIN) == 2) {
+            uint4 pk;
+            pk.x = umma::pack_bf16x2(y[0], y[1]); pk.y = umma::pack_bf16x2(y[2], y[3]);
+            pk.z = umma::pack_bf16x2(y[4], y[5]); pk.w = umma::pack_bf16x2(y[6], y[7]);
+            reinterpret_cast<uint4*>(op)[j] = pk;
+          } else {
+            reinterpret_cast<float4*>(op)[2 * j] = make_float4(y[0], y[1], y[2], y[3]);
+            reinterpret_cast<float4*>(op)[2 * j + 1] = make_float4(y[4], y[5], y[6], y[7]);
+          }
         }
       }
     }
@@ -318,7 +330,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
             float4 f;
             asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
                 : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
-                : "l"(src + ((col0 / 4 + j) ^ sw)));
+                : "l"(src + ((uc / 4 + j) ^ sw)));
             u[4 * j] = f.x; u[4 * j + 1] = f.y; u[4 * j + 2] = f.z; u[4 * j + 3] = f.w;
           }
       }
@@ -442,8 +454,23 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   if (warp == 0) umma::tmem_dealloc(tD0, 512);
 }
 
+// Fewer chains than half the SMs (long sequences, few heads): each chain's 128 value columns are split over
+// two CTAs of 64 (a 2-CTA cluster, as for V = 256), which halves the per-chunk work on a chain's critical path.
+static TcParams inter_x3_split(const TcParams& p) {
+  TcParams q = p;
+  int dev = 0, sms = 0;
+  if (p.V == 128 && cudaGetDevice(&dev) == cudaSuccess &&
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+      2LL * p.B * p.HV <= sms) {
+    q.vt = 64;
+    q.vsplit = 2;
+  }
+  return q;
+}
+
 template <typename TIN>
-static int launch_inter_x3_t(const TcParams& p, cudaStream_t st) {
+static int launch_inter_x3_t(const TcParams& p0, cudaStream_t st) {
+  const TcParams p = inter_x3_split(p0);
   const size_t smem = nx3::TOTAL + 1024;
   const bool xchg = p.vsplit > 1 && p.fuse_epilogue;  // the slices of a chain exchange row sums: one cluster each
   void (*fn)(const TcParams) = xchg ? k_inter_x3<TIN, true> : k_inter_x3<TIN, false>;

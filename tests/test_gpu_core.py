@@ -254,6 +254,29 @@ def test_short_conv_and_rms_norm_gate_kernels():
     assert_close(y.cpu().numpy(), yr, what="rms", **F32_TOL)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_chunk_split_path_one_and_two_ctas_per_chain(dtype):
+    """K = V = 128 on the split-operand path with the fused gated RMS norm,
+    once with more chains than half the SMs (one CTA per chain: B = 2,
+    HV = 40) and once with few chains (each chain's value columns over two
+    64-column CTAs that exchange the norm's row sums: B = 1, HV = 3); both
+    vs the f64 oracle, the gated output elementwise and the final state."""
+    import burn_gdn2 as bg
+
+    for B, HV, T in ((2, 40, 130), (1, 3, 200)):
+        K = V = 128
+        arrs = O.make_core_inputs(B, HV, T, K, V, seed=77, dtype=np.float32, decay=(-1.6, -0.001))
+        d = _to_dev({k: arrs[k] for k in "qkvgbw"}, dtype)
+        gate = torch.tensor(arrs["gate"], device=DEV, dtype=dtype)
+        onw = torch.tensor(np.random.default_rng(78).uniform(0.5, 1.5, V).astype(np.float32), device=DEV)
+        s0 = torch.tensor(np.random.default_rng(79).standard_normal((B, HV, K, V)).astype(np.float32), device=DEV)
+        y, st = _chunk_full(d, gate, onw, s0, HV, False)
+        y_ref, s_ref = _oracle_full(d, gate, onw, s0)
+        _check(y.float().cpu().numpy(), y_ref, dtype, "gated out")
+        _check(st.cpu().numpy(), s_ref, torch.float32 if dtype == torch.float32 else dtype, "state")
+    assert bg._lib.read_device_errors() == 0
+
+
 @pytest.mark.parametrize("shape", [(2, 3, 190, 128, 64), (1, 2, 64, 128, 128), (2, 2, 1, 128, 128),
                                    (1, 2, 200, 128, 256)])
 @pytest.mark.parametrize("precision", ["f32", "bf16"])
