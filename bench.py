@@ -340,6 +340,12 @@ def run_ours(args):
                                                                precision="bf16"),
                   "cfg5_core": run_core_cfg(torch, bg, ops, dev, stream, CFG5, "config 5", max_over_ranks, world,
                                             seed=5000 + 10 * rank),
+                  # the config-2 core split by heads over the N ranks (strong scaling; no collective)
+                  "cfg2_core_head_split": (run_core_cfg(torch, bg, ops, dev, stream,
+                                                        dict(CFG2, H=16 // world, HV=16 // world, negeig=False,
+                                                             min_decay=None), "config 2", max_over_ranks, world,
+                                                        seed=2000 + 10 * rank, strong=True)
+                                           if 16 % world == 0 else None),
                   # the config-5 layer split by heads over the N ranks (strong scaling, all-reduce timed apart)
                   "cfg5_layer_head_sharded": run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world)}
 
@@ -440,37 +446,74 @@ def run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world):
     c = CFG2
     cfg = bg.Gdn2Config(hidden_size=2048, num_heads=16, head_dim=128, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
     full = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=0)
-    W = {n: getattr(full, a).weight.detach().float().cpu() for n, a in
-         (("q_proj", "q_proj"), ("k_proj", "k_proj"), ("v_proj", "v_proj"), ("f_proj_0", "f_proj_0"),
-          ("f_proj_1", "f_proj_1"), ("b_proj", "b_proj"), ("w_proj", "w_proj"), ("g_proj_0", "g_proj_0"),
-          ("o_proj", "o_proj"))}
-    W["g_proj_1_w"] = full.g_proj_1.weight.float().cpu()
-    W["g_proj_1_b"] = full.g_proj_1.bias.float().cpu()
-    for n, a in (("A_log", "a_log"), ("dt_bias", "dt_bias"), ("o_norm_w", "o_norm_weight"), ("q_conv_w", "q_conv_w"),
-                 ("k_conv_w", "k_conv_w"), ("v_conv_w", "v_conv_w")):
-        W[n] = getattr(full, a).float().cpu()
+    W = full.export_weights()
     del full
     m = sharding.ShardedGatedDeltaNet2(cfg, W, device=dev, dtype=torch.bfloat16)
     g = torch.Generator(device=dev).manual_seed(11)
     x = torch.randn(c["B"], c["T"], 2048, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    for _ in range(2):
-        m.forward_train(x)
-    torch.cuda.synchronize()
-    n = 5
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    m.pop_allreduce_ms()
-    e0.record(stream)
-    for _ in range(n):
-        m.forward_train(x)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / n)
-    ar_ms = max_over_ranks(sum(m.pop_allreduce_ms()) / n)
+    ms, ar_ms, local_ms = time_sharded(torch, m, x, stream, max_over_ranks, n=5)
     nbytes = c["B"] * c["T"] * 2048 * 2
     return {"value": c["B"] * c["T"] / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
             "workload": f"GatedDeltaNet2.forward_train, BASELINE config 2, 16 heads split over {world} GPUs",
             "allreduce_ms": ar_ms, "allreduce_bytes": nbytes,
-            "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / (ar_ms / 1e3) / 1e9}
+            "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / (ar_ms / 1e3) / 1e9,
+            **overlap_fields(ms, ar_ms, local_ms, m.overlap_segments),
+            "parity_vs_unsharded": sharded_parity(torch, bg, sharding, dev, world)}
+
+
+def time_sharded(torch, m, x, stream, max_over_ranks, n):
+    """Sharded forward_train per step (max over ranks), its all-reduce time
+    (summed over the overlapped ranges) and the same rank's local layer alone
+    (no collective, one core call): the step minus the local layer is the
+    all-reduce time left exposed."""
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        m.forward_train(x)
+        m.local.forward_train(x)
+    torch.cuda.synchronize()
+    m.pop_allreduce_ms()
+    e0, e1, e2 = ev(), ev(), ev()
+    e0.record(stream)
+    for _ in range(n):
+        m.forward_train(x)
+    e1.record(stream)
+    for _ in range(n):
+        m.local.forward_train(x)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    local_ms = max_over_ranks(e1.elapsed_time(e2) / n)
+    ar_ms = max_over_ranks(sum(m.pop_allreduce_ms()) / n)
+    return ms, ar_ms, local_ms
+
+
+def overlap_fields(ms, ar_ms, local_ms, segments):
+    exposed = max(0.0, ms - local_ms)
+    return {"local_layer_ms": local_ms, "exposed_allreduce_ms": exposed, "overlap_segments": segments,
+            "allreduce_hidden_frac": max(0.0, 1.0 - exposed / ar_ms) if ar_ms > 0 else None}
+
+
+def sharded_parity(torch, bg, sharding, dev, world):
+    """ShardedGatedDeltaNet2 (NCCL all-reduce, overlapped forward_train) vs the unsharded layer on rank 0, both
+    on the CUDA path: a bf16 layer of 8 x 128 heads, hidden 1024, B = 2, T = 320 (five chunks over the ranges),
+    judged by the whole-layer criterion of the tests (relative Frobenius error <= 1e-2, max |d| <= 2.5e-2 of the
+    reference's max magnitude: the ranks' o_proj partials are bf16 before their sum)."""
+    import torch.distributed as dist
+    cfg = bg.Gdn2Config(hidden_size=1024, num_heads=8, head_dim=128, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
+    full = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=21)
+    W = full.export_weights()
+    m = sharding.ShardedGatedDeltaNet2(cfg, W, device=dev, dtype=torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(22)
+    x = torch.randn(2, 320, 1024, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    y = m.forward_train(x).float()
+    ref = full.forward_train(x).float()
+    torch.cuda.synchronize()
+    rel = float((y - ref).norm() / ref.norm())
+    worst = float((y - ref).abs().max() / ref.abs().max())
+    ok = torch.tensor([1.0 if rel <= 1e-2 and worst <= 2.5e-2 else 0.0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    return {"workload": "bf16 layer, hidden 1024, 8 x 128 heads, B=2, T=320, chunk mode", "ranks": world,
+            "rel_fro": rel, "max_abs_err_over_max_ref": worst, "pass": bool(ok.item() == 1.0)}
 
 
 def layer_flops(tokens, D, H, K, HV, V, C):
@@ -491,13 +534,7 @@ def run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world):
     full = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=7)
     if world > 1:
         from burn_gdn2 import sharding
-        W = {n: getattr(full, n).weight.detach().float().cpu() for n in
-             ("q_proj", "k_proj", "v_proj", "f_proj_0", "f_proj_1", "b_proj", "w_proj", "g_proj_0", "o_proj")}
-        W["g_proj_1_w"] = full.g_proj_1.weight.float().cpu()
-        W["g_proj_1_b"] = full.g_proj_1.bias.float().cpu()
-        for n, a in (("A_log", "a_log"), ("dt_bias", "dt_bias"), ("o_norm_w", "o_norm_weight"),
-                     ("q_conv_w", "q_conv_w"), ("k_conv_w", "k_conv_w"), ("v_conv_w", "v_conv_w")):
-            W[n] = getattr(full, a).float().cpu()
+        W = full.export_weights()
         del full
         m = sharding.ShardedGatedDeltaNet2(cfg, W, device=dev, dtype=torch.bfloat16)
         del W
@@ -505,20 +542,20 @@ def run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world):
         m = full
     g = torch.Generator(device=dev).manual_seed(7)
     x = torch.randn(B, T, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    for _ in range(2):
-        m.forward_train(x)
-    torch.cuda.synchronize()
     n = 3
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
-        m.pop_allreduce_ms()
-    e0.record(stream)
-    for _ in range(n):
-        m.forward_train(x)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / n)
-    ar = sum(m.pop_allreduce_ms()) if world > 1 else 0.0
+        ms, ar_ms, local_ms = time_sharded(torch, m, x, stream, max_over_ranks, n)
+    else:
+        for _ in range(2):
+            m.forward_train(x)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            m.forward_train(x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / n)
     flops = layer_flops(B * T, D, H, K, H, K, 64)
     out = {"value": B * T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "scaling": "strong",
            "workload": f"GatedDeltaNet2.forward_train, BASELINE config 5 (D=4096, 32x128 heads, B=2, T=65536, bf16), "
@@ -526,9 +563,9 @@ def run_layer_cfg5(torch, bg, dev, stream, max_over_ranks, world):
            "tc_frac_of_all_gpus": flops / (ms / 1e3) / (load_peaks()["bf16_tflops"] * 1e12 * world)}
     if world > 1:
         nbytes = B * T * D * 2
-        ar_ms = max_over_ranks(ar / n)
         out.update({"allreduce_ms": ar_ms, "allreduce_bytes": nbytes,
-                    "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / (ar_ms / 1e3) / 1e9})
+                    "allreduce_busbw_gbs": 2 * (world - 1) / world * nbytes / (ar_ms / 1e3) / 1e9,
+                    **overlap_fields(ms, ar_ms, local_ms, m.overlap_segments)})
     del m, x
     return out
 
@@ -540,11 +577,13 @@ CFG4 = dict(B=4, H=8, HV=16, T=8192, K=128, V=256, chunk=64, negeig=True, min_de
 CFG5 = dict(B=2, H=32, HV=32, T=65536, K=128, V=128, chunk=64, negeig=False, min_decay=None)
 
 
-def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, seed, precision="f32"):
+def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, seed, precision="f32", strong=False):
     """Chunk core (intra + inter + fused epilogue) at one BASELINE config:
     tokens/s, ms/step and the fraction of the measured HBM copy bandwidth
     its algorithmic bytes reach.  Key-side inputs (q, k, g, b) have H heads
-    and are read grouped (value head hv uses key head hv // (HV / H))."""
+    and are read grouped (value head hv uses key head hv // (HV / H)).
+    strong: `c` is this rank's share of one job split by heads over the
+    ranks (tokens/s counts the job's B x T tokens once)."""
     B, H, HV, T, K, V = c["B"], c["H"], c["HV"], c["T"], c["K"], c["V"]
     xk = make_inputs(torch, B, H, T, K, K, torch.bfloat16, dev, seed=seed)
     xv = make_inputs(torch, B, HV, T, V, V, torch.bfloat16, dev, seed=seed + 1)
@@ -586,8 +625,11 @@ def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, se
         path = ("tensor cores, f32-grade intermediates (k_intra_x3 + k_inter_x3)" if V <= 128 else
                 "tensor cores, f32-grade intermediates (k_intra_x3 with U in two 128-column halves; k_inter_x3 over "
                 "two 128-column slices per chain, a 2-CTA cluster exchanging the gated RMS norm's row sums)")
-    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "precision": precision,
-            "workload": f"BASELINE {name} chunk core: B={B} (per rank), T={T}, H={H}, HV={HV}, K={K}, V={V}, bf16",
+    return {"value": B * T * (1 if strong else world) / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "precision": precision, "scaling": "strong" if strong else "weak",
+            "workload": (f"BASELINE {name} chunk core, {H * world} key / {HV * world} value heads split over {world} "
+                         f"GPU(s): B={B}, T={T}, H={H}, HV={HV} per rank, K={K}, V={V}, bf16" if strong else
+                         f"BASELINE {name} chunk core: B={B} (per rank), T={T}, H={H}, HV={HV}, K={K}, V={V}, bf16"),
             "path": path,
             "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}

@@ -150,6 +150,21 @@ class GatedDeltaNet2:
             W["decay_factors"] = torch.full((h, hk), 2.0, dtype=torch.float64)
         return cls(cfg, {k: v.float() for k, v in W.items()}, device=device, dtype=dtype, **kw)
 
+    def export_weights(self) -> dict:
+        """The layer's weights as the constructor takes them (names of
+        WEIGHTS, projections [in, out]), f32 on the host: e.g. to build
+        per-rank shards of this layer (sharding.shard_weights)."""
+        f = lambda t: t.detach().float().cpu()
+        W = {n: f(getattr(self, n).weight) for n in
+             ("q_proj", "k_proj", "v_proj", "f_proj_0", "f_proj_1", "b_proj", "w_proj", "g_proj_0", "o_proj")}
+        W["g_proj_1_w"], W["g_proj_1_b"] = f(self.g_proj_1.weight), f(self.g_proj_1.bias)
+        for n, a in (("A_log", "a_log"), ("dt_bias", "dt_bias"), ("o_norm_w", "o_norm_weight"),
+                     ("q_conv_w", "q_conv_w"), ("k_conv_w", "k_conv_w"), ("v_conv_w", "v_conv_w")):
+            W[n] = f(getattr(self, a))
+        if self.decay_factors is not None:
+            W["decay_factors"] = f(self.decay_factors)
+        return W
+
     # -- helpers -------------------------------------------------------------
     @property
     def _dims(self):

@@ -64,15 +64,24 @@ class ShardedGatedDeltaNet2:
 
     Each rank holds a GatedDeltaNet2 of H/N key heads (and HV/N value heads)
     built from `shard_weights`; `forward_train` / `forward` return the full
-    output after one all-reduce (sum) of the row-parallel o_proj partials.
-    Every all-reduce is bracketed by CUDA events on the current stream and
+    output after the all-reduce (sum) of the row-parallel o_proj partials.
+
+    `forward_train` in chunk mode overlaps that all-reduce with the
+    recurrence: the chunk core runs over `overlap_segments` consecutive
+    token ranges (whole chunks, the state carried from one to the next, which
+    is the same recurrence as one call), and as each range completes, its
+    o_proj GEMM and its all-reduce run on a side stream while the core walks
+    the next range (the core occupies few SMs when a rank holds few chains).
+    Only the last range's o_proj and all-reduce are exposed.
+
+    Every all-reduce is bracketed by CUDA events on the stream it runs on and
     nothing waits on them here, so a timed loop of layer calls never stalls
     the host; `pop_allreduce_ms()` (after the caller has synchronised) returns
-    the all-reduce time of each call since the last pop, so it can be
-    reported separately.
+    the all-reduce time of each call since the last pop (summed over its
+    ranges), so it can be reported separately.
     """
 
-    def __init__(self, cfg, weights: dict, group=None, device="cuda", dtype=None, **kw):
+    def __init__(self, cfg, weights: dict, group=None, device="cuda", dtype=None, overlap_segments: int = 4, **kw):
         import torch
         import torch.distributed as dist
 
@@ -83,9 +92,11 @@ class ShardedGatedDeltaNet2:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.config = cfg
+        self.overlap_segments = int(overlap_segments)
         self.local = GatedDeltaNet2(shard_config(cfg, self.world), shard_weights(weights, cfg, self.rank, self.world),
                                     device=device, dtype=dtype or torch.float32, **kw)
         self._events = []
+        self._side = None
 
     def _reduce(self, y):
         import torch
@@ -94,18 +105,69 @@ class ShardedGatedDeltaNet2:
         e0.record()
         self.dist.all_reduce(y, op=self.dist.ReduceOp.SUM, group=self.group)
         e1.record()
-        self._events.append((e0, e1))
+        self._events.append([(e0, e1)])
         return y
+
+    def _forward_train_overlapped(self, x):
+        """Chunk-mode forward_train with the o_proj all-reduce overlapped
+        with the recurrence (see the class docstring)."""
+        import dataclasses as dc
+
+        import torch
+
+        m = self.local
+        C = m.config.chunk_size
+        B, T, D = x.shape
+        h, hk, hv, vh = m._dims
+        nch = (T + C - 1) // C
+        seg = -(-nch // self.overlap_segments) * C  # tokens per range, whole chunks
+        p, _ = m.project(x, None)
+        state = torch.zeros(B, hv, hk, vh, dtype=torch.float32, device=x.device)
+        y = torch.empty(B, T, D, dtype=x.dtype, device=x.device)
+        main = torch.cuda.current_stream(x.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=x.device)
+        side = self._side
+        side.wait_stream(main)  # y and the weights exist before the side stream writes or reads them
+        evs = []
+        for t0 in range(0, T, seg):
+            t1 = min(T, t0 + seg)
+            ps = dc.replace(p, q=p.q[:, :, t0:t1], k=p.k[:, :, t0:t1], v=p.v[:, :, t0:t1], g=p.g[:, :, t0:t1],
+                            b=p.b[:, :, t0:t1], w=p.w[:, :, t0:t1], gate=p.gate[:, t0:t1])
+            normed = m._chunk_core(ps, state)
+            done = torch.cuda.Event()
+            done.record(main)
+            with torch.cuda.stream(side):
+                side.wait_event(done)
+                normed.record_stream(side)
+                part = m._out_proj(normed)  # [B, t1 - t0, D], contiguous
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(side)
+                self.dist.all_reduce(part, op=self.dist.ReduceOp.SUM, group=self.group)
+                e1.record(side)
+                evs.append((e0, e1))
+                y[:, t0:t1].copy_(part)
+        main.wait_stream(side)
+        self._events.append(evs)
+        return y
+
+    def _overlap_applies(self, x):
+        from .config import Gdn2Mode
+
+        return (self.overlap_segments > 1 and self.world > 1 and Gdn2Mode(self.local.config.mode) == Gdn2Mode.Chunk
+                and x.is_cuda and x.shape[1] >= 2 * self.local.config.chunk_size)
 
     def pop_allreduce_ms(self):
         """All-reduce times (ms) of the calls since the last pop, oldest
         first.  Call after the work has completed (e.g. after
         torch.cuda.synchronize()); it does not wait itself."""
-        out = [e0.elapsed_time(e1) for e0, e1 in self._events]
+        out = [sum(e0.elapsed_time(e1) for e0, e1 in call) for call in self._events]
         self._events = []
         return out
 
     def forward_train(self, x):
+        if self._overlap_applies(x):
+            return self._forward_train_overlapped(x)
         return self._reduce(self.local.forward_train(x))
 
     def forward(self, x, state=None, update_state=True):
