@@ -88,8 +88,8 @@ static bool use_tc(const gdn2_chunk_args* a) {
 }
 
 // The split-operand tensor-core path (f32-grade intermediates): bf16 or f32
-// inputs, K = 128, V in {64, 128}, 64-token chunks.  Every other shape runs
-// on the exact-f32 CUDA-core path.
+// inputs, K = 128, V in {64, 128, 256}, 64-token chunks.  Every other shape
+// runs on the exact-f32 CUDA-core path.
 static bool use_x3(const gdn2_chunk_args* a) {
   const gdn2_dims& d = a->dims;
   const int C = a->chunk_size < CP ? a->chunk_size : CP;
@@ -105,9 +105,28 @@ static size_t rec_bytes(const gdn2_dims& d, bool x3) {
   return x3 ? x3_record_layout(d.head_v_dim).bytes : tc_record_layout(d.head_v_dim).bytes;
 }
 
+// SMs of the current device (148 on a B200 if the query fails): sizes the scan segments.
+static int device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();
+    return 148;
+  }
+  return sms;
+}
+
+static int scan_segments(const gdn2_dims& d, bool x3) {
+  return x3 ? x3_scan_segments(d.batch, d.num_v_heads, (d.seq_len + TC_C - 1) / TC_C, d.head_v_dim, device_sms())
+            : 1;
+}
+
 static size_t tc_workspace_bytes(const gdn2_dims& d, bool x3) {
   const size_t nch = (size_t)d.batch * d.num_v_heads * ((d.seq_len + TC_C - 1) / TC_C);
-  return nch * rec_bytes(d, x3) + (x3 ? x3_scratch_bytes((long long)nch, d.head_v_dim) : 0);
+  return nch * rec_bytes(d, x3) +
+         (x3 ? x3_scratch_bytes((long long)nch, d.head_v_dim) +
+                   x3_scan_bytes(d.batch, d.num_v_heads, d.head_v_dim, scan_segments(d, true))
+             : 0);
 }
 
 static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, const char* fn, bool x3) {
@@ -129,6 +148,15 @@ static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, 
   p.rec = static_cast<unsigned char*>(ws);
   p.rec_bytes = rec_bytes(d, x3);
   p.scratch = p.rec + (size_t)p.B * p.HV * p.NC * p.rec_bytes;
+  p.nseg = scan_segments(d, x3);
+  p.seg_len = (p.NC + p.nseg - 1) / p.nseg;
+  p.scan_phase = 0;
+  p.seg_state = nullptr;
+  p.seg_trans = nullptr;
+  if (p.nseg > 1) {
+    p.seg_state = reinterpret_cast<float*>(p.scratch + x3_scratch_bytes((long long)p.B * p.HV * p.NC, p.V));
+    p.seg_trans = p.seg_state + (size_t)p.B * p.HV * p.nseg * TC_K * p.V;
+  }
   return GDN2_OK;
 }
 

@@ -74,23 +74,51 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   float* sXsum = reinterpret_cast<float*>(sm + XSUM);
   uint64_t* xbars = reinterpret_cast<uint64_t*>(sm + XBARS);
 
-  const int hv = blockIdx.y, bb = blockIdx.z;
-  const int V = p.vt, HALF = V / 2;               // columns of this CTA's slice
-  const int VF = p.V, cbase = blockIdx.x * p.vt;  // full row width, first column of the slice
-  const uint32_t peer = blockIdx.x ^ 1u;          // cluster rank of the other slice's CTA (XCHG)
+  // blockIdx.z = (batch entry, segment of the chain); blockIdx.x = column slice.  Scan phase A: slices
+  // 0 .. VF / V - 1 carry the state's value columns (from a zero start, U from the record), slice VF / V the
+  // segment's transition (K columns from the identity, U = 0); no output.
+  const bool scanA = p.scan_phase == 1;
+  const int zseg = scanA ? p.nseg - 1 : p.nseg;  // segments in the grid: phase A skips the last one
+  const int hv = blockIdx.y, seg = blockIdx.z % zseg, bb = blockIdx.z / zseg;
+  const int V = p.vt, HALF = V / 2;  // columns of this CTA's slice
+  const int VF = p.V;                // full row width
+  const bool tslice = scanA && (int)blockIdx.x * V >= VF;          // the transition slice (phase A)
+  const int cbase = tslice ? (int)blockIdx.x * V - VF : (int)blockIdx.x * V;  // first column of the slice
+  const uint32_t peer = blockIdx.x ^ 1u;  // cluster rank of the other slice's CTA (XCHG)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sp = warp & 3, half = warp >> 2;
   const int col0 = half * HALF;
   const X3Record L = x3_record_layout(VF);
-  const unsigned char* recs = p.rec + ((size_t)bb * p.HV + hv) * p.NC * p.rec_bytes;
-  float* st = p.state + ((size_t)bb * p.HV + hv) * (size_t)TC_K * VF + cbase;
+  const size_t chain = (size_t)bb * p.HV + hv;
+  const int c0 = seg * p.seg_len;                  // first chunk of this segment
+  const int NCL = min(p.NC, c0 + p.seg_len) - c0;  // its chunks
+  const unsigned char* recs = p.rec + (chain * p.NC + c0) * p.rec_bytes;
+  // start state (null: zero, or the identity for a transition slice) and where the end state goes (null:
+  // nowhere), rows of srow floats
+  const float* st_in;
+  float* st_out;
+  int srow = VF;
+  if (scanA) {
+    st_in = nullptr;
+    if (tslice) {
+      srow = TC_K;
+      st_out = p.seg_trans + (chain * (p.nseg - 1) + seg) * TC_K * TC_K + cbase;
+    } else {
+      st_out = p.seg_state + (chain * p.nseg + seg + 1) * TC_K * VF + cbase;  // N_seg, in slot seg + 1
+    }
+  } else if (p.nseg == 1) {
+    st_in = st_out = p.state + chain * TC_K * VF + cbase;
+  } else {
+    st_in = p.seg_state + (chain * p.nseg + seg) * TC_K * VF + cbase;
+    st_out = seg == p.nseg - 1 ? p.state + chain * TC_K * VF + cbase : nullptr;
+  }
   const uint32_t sbase = smem_u32(sm);
 
   if (warp == 0) {
     umma::tmem_alloc(tslot, 512);
     umma::tmem_relinquish();
   }
-  if (p.fuse_epilogue)
+  if (p.fuse_epilogue && !scanA)
     for (int i = tid; i < V; i += 256) sOnw[i] = p.onw[cbase + i];
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
@@ -125,7 +153,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   // records two chunks ahead are pulled into L2 (one bulk prefetch per chunk), so the stage refills, issued
   // as soon as a part is consumed, read from L2
   auto prefetch_rec = [&](int c) {
-    if (c < p.NC) bulk_prefetch_l2(recs + (size_t)c * p.rec_bytes, (unsigned)L.bytes);
+    if (c < NCL) bulk_prefetch_l2(recs + (size_t)c * p.rec_bytes, (unsigned)L.bytes);
   };
   if (tid == 0) {
     issueA(0);
@@ -141,11 +169,16 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   for (int c16 = 0; c16 < HALF / 16; ++c16) {
     const int col = col0 + 16 * c16;
     float v[16];
-    const float4* src = reinterpret_cast<const float4*>(st + (size_t)kk * VF + col);
-    #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float4 f = src[j];
-      v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+    if (st_in) {
+      const float4* src = reinterpret_cast<const float4*>(st_in + (size_t)kk * srow + col);
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 f = src[j];
+        v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+      }
+    } else {  // zero, or the identity (row kk of the transition: 1 in column kk)
+      #pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = (tslice && cbase + col + j == kk) ? 1.f : 0.f;
     }
     uint4 h0, l0, h1, l1;
     split8(v, h0, l0);
@@ -190,17 +223,17 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   const int orow = 32 * (sp - 2) + lane;
   auto gate_row = [&](int c) {
     return reinterpret_cast<const uint4*>(static_cast<const TIN*>(p.gate.p) + bb * p.gate.s0 + hv * p.gate.s1 +
-                                          (int64_t)(c * TC_C + orow) * p.gate.s2 + cbase + col0);
+                                          (int64_t)((c0 + c) * TC_C + orow) * p.gate.s2 + cbase + col0);
   };
   auto prefetch_gate = [&](int c) {
-    if (p.fuse_epilogue && c < p.NC && orow < min(TC_C, p.T - c * TC_C)) {
+    if (p.fuse_epilogue && c < NCL && orow < min(TC_C, p.T - (c0 + c) * TC_C)) {
       const char* g = reinterpret_cast<const char*>(gate_row(c));
       for (int b = 0; b < HALF * (int)sizeof(TIN); b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(g + b));
     }
   };
   uint4 graw[GW];
   auto load_gate = [&](int c) {
-    if (p.fuse_epilogue && orow < min(TC_C, p.T - c * TC_C)) {
+    if (p.fuse_epilogue && orow < min(TC_C, p.T - (c0 + c) * TC_C)) {
       const uint4* gp = gate_row(c);
       #pragma unroll
       for (int j = 0; j < GW; ++j)
@@ -216,7 +249,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     }
   };
   auto epilogue = [&](int c) {
-    const int t0 = c * TC_C;
+    const int t0 = (c0 + c) * TC_C;
     const int cv = min(TC_C, p.T - t0);
     const uint32_t tD = tD0 + (c & 1) * V;
     // MMA2 of chunk c has completed: thread 0 waited for it before the barrier that closed chunk c.  The o row
@@ -285,16 +318,18 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     }
   };
   if (sp >= 2) {
-    load_gate(0);
-    prefetch_gate(1);
-  } else {
+    if (!scanA) {
+      load_gate(0);
+      prefetch_gate(1);
+    }
+  } else if (!tslice) {
     prefetch_u(0);
   }
 
   // Every mbarrier wait below is on a phase that cannot be overtaken by the next one before the waiting thread
   // passes the barrier closing the chunk (each next phase needs work issued after that barrier), so the
   // parity waits are unambiguous; only thread 0 waits for the [W; Qg] copy of the chunk it starts.
-  for (int c = 0; c < p.NC; ++c) {
+  for (int c = 0; c < NCL; ++c) {
     const uint32_t tD = tD0 + (c & 1) * V;
 
     // MMA1: D = [W; Qg] S  (the master already holds diag(gamma_last) S for MMA3)
@@ -316,12 +351,16 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     if (sp >= 2) {
       // the epilogue of the previous chunk while the tensor core does MMA1, then the next gate rows
       mbar_arrive(&bars[4]);
-      if (c > 0) epilogue(c - 1);
-      load_gate(c);
-      prefetch_gate(c + 1);
+      if (!scanA) {
+        if (c > 0) epilogue(c - 1);
+        load_gate(c);
+        prefetch_gate(c + 1);
+      }
     } else {
-      float u[64];  // U rows of this chunk: read while MMA1 runs
-      {
+      float u[64];  // U rows of this chunk: read while MMA1 runs (zero for a transition slice)
+      #pragma unroll
+      for (int j = 0; j < 64; ++j) u[j] = 0.f;
+      if (!tslice) {
         const float4* src = u_row(c);
         const int sw = lane & 7;  // = row & 7
         #pragma unroll
@@ -336,7 +375,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       }
       mbar_wait_bounded(&bars[2], c & 1);
       umma::fence_after_sync();
-      if (tid == 0 && c + 1 < p.NC) issueA(c + 1);  // MMA1 has read [W; Qg]; gamma_last goes to the other slot
+      if (tid == 0 && c + 1 < NCL) issueA(c + 1);  // MMA1 has read [W; Qg]; gamma_last goes to the other slot
       // v_new = U - W S (rows 0..63 of D) -> hi / lo images
       const int r = 32 * sp + lane;
       #pragma unroll
@@ -365,7 +404,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       fence_proxy_async_smem();
       umma::fence_before_sync();
       mbar_arrive(&bars[4]);
-      if (c + 1 < p.NC) prefetch_u(c + 1);
+      if (c + 1 < NCL && !tslice) prefetch_u(c + 1);
     }
 
     // MMA3: S += Kd^T v_new (the recurrence: committed on its own), then MMA2: D += [*; Aqk] v_new (the o rows)
@@ -384,20 +423,22 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
           umma::mma_bf16(tS, umma::desc_mnmaj_at(da, j), umma::desc_mnmaj_at(db, j), i3, true);
       }
       umma::commit(&bars[3]);
-      #pragma unroll 1
-      for (int pass = 0; pass < 3; ++pass) {
-        const uint64_t da = pass == 1 ? dtl : dth, db = pass == 2 ? dvl : dvh;
-        #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          umma::mma_bf16(tD, umma::desc_kmaj_at(da, 128, j), umma::desc_mnmaj_at(db, j), i1, true);
+      if (!scanA) {
+        #pragma unroll 1
+        for (int pass = 0; pass < 3; ++pass) {
+          const uint64_t da = pass == 1 ? dtl : dth, db = pass == 2 ? dvl : dvh;
+          #pragma unroll
+          for (int j = 0; j < 4; ++j)
+            umma::mma_bf16(tD, umma::desc_kmaj_at(da, 128, j), umma::desc_mnmaj_at(db, j), i1, true);
+        }
+        umma::commit(&bars[5]);
       }
-      umma::commit(&bars[5]);
     }
     mbar_wait_bounded(&bars[3], c & 1);
     umma::fence_after_sync();
 
     // S_{c+1} -> hi / lo images for MMA1 of the next chunk, and the master rescaled by that chunk's gamma_last
-    const bool more = c + 1 < p.NC;
+    const bool more = c + 1 < NCL;
     float gam = 1.f;
     if (more) {
       mbar_wait_bounded(&bars[0], (c + 1) & 1);  // gamma_last of chunk c + 1 (issued with its [W; Qg])
@@ -428,7 +469,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     }
     if (more) umma::wait_st();
     if (tid == 0) {
-      mbar_wait_bounded(&bars[5], c & 1);  // MMA2 has read Aqk (MMA3 read Kd before it)
+      if (!scanA) mbar_wait_bounded(&bars[5], c & 1);  // MMA2 has read Aqk (MMA3 read Kd before it)
       if (more) issueB(c + 1);
     }
     fence_proxy_async_smem();
@@ -436,17 +477,19 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
     __syncthreads();
     umma::fence_after_sync();
   }
-  if (sp >= 2) epilogue(p.NC - 1);
+  if (sp >= 2 && !scanA) epilogue(NCL - 1);
 
-  // ---- final state back to HBM (f32, in place) ----
-  for (int c16 = 0; c16 < HALF / 16; ++c16) {
-    const int col = col0 + 16 * c16;
-    float v[16];
-    umma::ld16(umma::taddr(tS, 32 * sp, col), v);
-    umma::wait_ld();
-    float4* dst = reinterpret_cast<float4*>(st + (size_t)kk * VF + col);
-    #pragma unroll
-    for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  // ---- end state back to HBM (f32: in place, or the segment's slot) ----
+  if (st_out) {
+    for (int c16 = 0; c16 < HALF / 16; ++c16) {
+      const int col = col0 + 16 * c16;
+      float v[16];
+      umma::ld16(umma::taddr(tS, 32 * sp, col), v);
+      umma::wait_ld();
+      float4* dst = reinterpret_cast<float4*>(st_out + (size_t)kk * srow + col);
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
   }
   umma::fence_before_sync();
   __syncthreads();
@@ -454,14 +497,69 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   if (warp == 0) umma::tmem_dealloc(tD0, 512);
 }
 
-// Fewer chains than half the SMs (long sequences, few heads): each chain's 128 value columns are split over
-// two CTAs of 64 (a 2-CTA cluster, as for V = 256), which halves the per-chunk work on a chain's critical path.
-static TcParams inter_x3_split(const TcParams& p) {
+// Scan phase B: the start state of every segment, in order, for one 32-column block of one chain:
+// slot 0 = the initial state, slot s + 1 = M_s slot s + N_s (N_s is in slot s + 1 already; updated in place).
+// f32 on the CUDA cores: M_s (row stride 129: conflict-free column walks) and the column block in shared
+// memory; thread t owns row t / 2 and 16 columns.
+__global__ void __launch_bounds__(256) k_scan_combine_x3(const TcParams p) {
+  extern __shared__ __align__(16) float smf[];
+  float* sM = smf;                 // [128][129]
+  float* sS = smf + TC_K * 129;    // [128][32]
+  const int VF = p.V, cb = blockIdx.x * 32, tid = threadIdx.x;
+  const size_t chain = (size_t)blockIdx.z * p.HV + blockIdx.y;
+  float* slots = p.seg_state + chain * p.nseg * TC_K * VF + cb;
+  const float* st0 = p.state + chain * TC_K * VF + cb;
+  for (int i = tid; i < TC_K * 8; i += 256) {  // float4 (row i / 8, columns 4 (i % 8) ..)
+    const int r = i >> 3, c4 = (i & 7) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(st0 + (size_t)r * VF + c4);
+    *reinterpret_cast<float4*>(sS + r * 32 + c4) = v;
+    *reinterpret_cast<float4*>(slots + (size_t)r * VF + c4) = v;
+  }
+  const int r = tid >> 1, cq = (tid & 1) * 16;
+  for (int sg = 0; sg + 1 < p.nseg; ++sg) {
+    const float* M = p.seg_trans + (chain * (p.nseg - 1) + sg) * TC_K * TC_K;
+    for (int i = tid; i < TC_K * TC_K / 4; i += 256) {
+      const float4 v = reinterpret_cast<const float4*>(M)[i];
+      const int rr = (4 * i) / TC_K, cc = (4 * i) % TC_K;
+      float* d = sM + rr * 129 + cc;
+      d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+    }
+    float* nxt = slots + (size_t)(sg + 1) * TC_K * VF + (size_t)r * VF + cq;
+    float acc[16];
+    #pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(nxt + j);
+      acc[j] = v.x; acc[j + 1] = v.y; acc[j + 2] = v.z; acc[j + 3] = v.w;
+    }
+    __syncthreads();  // sM and sS complete
+    #pragma unroll 4
+    for (int k = 0; k < TC_K; ++k) {
+      const float m = sM[r * 129 + k];
+      const float4* srow = reinterpret_cast<const float4*>(sS + k * 32 + cq);
+      #pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 x = srow[j];
+        acc[4 * j] = fmaf(m, x.x, acc[4 * j]);
+        acc[4 * j + 1] = fmaf(m, x.y, acc[4 * j + 1]);
+        acc[4 * j + 2] = fmaf(m, x.z, acc[4 * j + 2]);
+        acc[4 * j + 3] = fmaf(m, x.w, acc[4 * j + 3]);
+      }
+    }
+    __syncthreads();  // every read of sS and sM done
+    #pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      *reinterpret_cast<float4*>(sS + r * 32 + cq + j) = v;
+      *reinterpret_cast<float4*>(nxt + j) = v;
+    }
+  }
+}
+
+// Fewer chains (times segments) than half the SMs: each chain's 128 value columns are split over two CTAs
+// of 64 (a 2-CTA cluster, as for V = 256), which halves the per-chunk work on a chain's critical path.
+static TcParams inter_x3_split(const TcParams& p, int sms) {
   TcParams q = p;
-  int dev = 0, sms = 0;
-  if (p.V == 128 && cudaGetDevice(&dev) == cudaSuccess &&
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
-      2LL * p.B * p.HV <= sms) {
+  if (p.V == 128 && 2LL * p.B * p.HV * p.nseg <= sms) {
     q.vt = 64;
     q.vsplit = 2;
   }
@@ -470,27 +568,52 @@ static TcParams inter_x3_split(const TcParams& p) {
 
 template <typename TIN>
 static int launch_inter_x3_t(const TcParams& p0, cudaStream_t st) {
-  const TcParams p = inter_x3_split(p0);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return check_cuda(cudaGetLastError(), "chunk inter (x3) device query");
   const size_t smem = nx3::TOTAL + 1024;
-  const bool xchg = p.vsplit > 1 && p.fuse_epilogue;  // the slices of a chain exchange row sums: one cluster each
-  void (*fn)(const TcParams) = xchg ? k_inter_x3<TIN, true> : k_inter_x3<TIN, false>;
-  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return check_cuda(e, "chunk inter (x3) smem attribute");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.vsplit, p.HV, p.B);
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  if (xchg) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = p.vsplit;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+  for (void (*f)(const TcParams) : {k_inter_x3<TIN, true>, k_inter_x3<TIN, false>}) {
+    const cudaError_t e = cudaFuncSetAttribute((const void*)f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "chunk inter (x3) smem attribute");
   }
-  return check_cuda(cudaLaunchKernelEx(&cfg, fn, p), "chunk inter (x3) launch");
+  auto launch = [&](const TcParams& p, int slices, int zseg, bool xchg) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(slices, p.HV, p.B * zseg);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (xchg) {
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = slices;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+    }
+    return check_cuda(cudaLaunchKernelEx(&cfg, xchg ? k_inter_x3<TIN, true> : k_inter_x3<TIN, false>, p),
+                      "chunk inter (x3) launch");
+  };
+  if (p0.nseg > 1) {
+    // phase A: (N, M) of segments 0 .. nseg - 2, one CTA per 128-column slice of the state and one for the
+    // transition (no cluster: no output)
+    TcParams a = p0;
+    a.scan_phase = 1;
+    a.vt = 128;
+    int rc = launch(a, p0.V / 128 + 1, p0.nseg - 1, false);
+    if (rc) return rc;
+    // phase B
+    const size_t bsmem = (TC_K * 129 + TC_K * 32) * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute((const void*)k_scan_combine_x3, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)bsmem);
+    if (e != cudaSuccess) return check_cuda(e, "chunk scan (x3) smem attribute");
+    k_scan_combine_x3<<<dim3(p0.V / 32, p0.HV, p0.B), 256, bsmem, st>>>(p0);
+    rc = check_cuda(cudaGetLastError(), "chunk scan (x3) launch");
+    if (rc) return rc;
+  }
+  // phase C (or the whole chain when nseg = 1)
+  const TcParams p = inter_x3_split(p0, sms);
+  return launch(p, p.vsplit, p.nseg, p.vsplit > 1 && p.fuse_epilogue);
 }
 
 int launch_inter_x3(const TcParams& p, int dtype, cudaStream_t st) {

@@ -61,6 +61,28 @@ inline size_t x3_scratch_bytes(long long items, int V) {
   return (size_t)(items < X3_SLOTS ? items : X3_SLOTS) * x3_slot_bytes(V);
 }
 
+// Chunk-parallel state scan.  Over a segment of chunks the recurrence S' = (diag(gamma_last) - Kd^T W) S +
+// Kd^T U is affine in the segment's start state: S_end = M S_start + N, where N is the end state from a zero
+// start and M the product of the chunks' transitions (the same recurrence run on K columns with U = 0 from
+// the identity).  With few chains (long sequences, few heads per GPU) a chain's chunks are cut into nseg
+// segments: phase A computes (N, M) of every segment but the last in parallel, a short sequential pass
+// chains the start states (S_{s+1} = M_s S_s + N_s, f32), and phase C runs all segments in parallel from
+// their start states, writing the outputs.  Segments for V in {128, 256} when at least three fit (every
+// phase-A CTA of a segment, V / 128 state slices + 1 transition slice, on its own SM) with >= 8 chunks each;
+// otherwise 1 (no scan).
+inline int x3_scan_segments(long long B, long long HV, long long NC, int V, int sms) {
+  if (V != 128 && V != 256) return 1;
+  const long long slices = V / 128 + 1;
+  long long n = sms / (B * HV * slices);
+  if (n > NC / 8) n = NC / 8;
+  if (n < 3) return 1;
+  const long long len = (NC + n - 1) / n;  // chunks per segment; every segment non-empty
+  return (int)((NC + len - 1) / len);
+}
+inline size_t x3_scan_bytes(long long B, long long HV, int V, int nseg) {
+  return nseg > 1 ? (size_t)(B * HV) * ((size_t)nseg * TC_K * V + (size_t)(nseg - 1) * TC_K * TC_K) * 4 : 0;
+}
+
 bool x3_supported(int K, int V, int C);
 int launch_intra_x3(const TcParams& p, int dtype, cudaStream_t st);
 int launch_inter_x3(const TcParams& p, int dtype, cudaStream_t st);

@@ -277,6 +277,30 @@ def test_chunk_split_path_one_and_two_ctas_per_chain(dtype):
     assert bg._lib.read_device_errors() == 0
 
 
+@pytest.mark.parametrize("shape", [(1, 3, 1600, 128, 128), (1, 1, 2048, 128, 256)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_chunk_state_scan_segments(shape, dtype):
+    """Few long chains: the split-operand inter kernel cuts each chain into
+    segments (3 of 9, 9 and 7 chunks for 3 chains at V = 128; 4 of 8 at
+    V = 256), computes every segment's end state from zero and its state
+    transition in parallel, chains the start states, then runs the segments
+    in parallel.  With the fused gated RMS norm and a random initial state,
+    vs the f64 oracle: gated output elementwise, final state."""
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = shape
+    arrs = O.make_core_inputs(B, HV, T, K, V, seed=87, dtype=np.float32, decay=(-0.4, -0.001))
+    d = _to_dev({k: arrs[k] for k in "qkvgbw"}, dtype)
+    gate = torch.tensor(arrs["gate"], device=DEV, dtype=dtype)
+    onw = torch.tensor(np.random.default_rng(88).uniform(0.5, 1.5, V).astype(np.float32), device=DEV)
+    s0 = torch.tensor(np.random.default_rng(89).standard_normal((B, HV, K, V)).astype(np.float32), device=DEV)
+    y, st = _chunk_full(d, gate, onw, s0, HV, False)
+    y_ref, s_ref = _oracle_full(d, gate, onw, s0)
+    _check(y.float().cpu().numpy(), y_ref, dtype, "gated out")
+    _check(st.cpu().numpy(), s_ref, torch.float32 if dtype == torch.float32 else dtype, "state")
+    assert bg._lib.read_device_errors() == 0
+
+
 @pytest.mark.parametrize("shape", [(2, 3, 190, 128, 64), (1, 2, 64, 128, 128), (2, 2, 1, 128, 128),
                                    (1, 2, 200, 128, 256)])
 @pytest.mark.parametrize("precision", ["f32", "bf16"])
