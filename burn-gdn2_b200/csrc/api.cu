@@ -150,7 +150,6 @@ static int prep_tc(const gdn2_chunk_args* a, void* ws, size_t wsb, TcParams& p, 
   p.scratch = p.rec + (size_t)p.B * p.HV * p.NC * p.rec_bytes;
   p.nseg = scan_segments(d, x3);
   p.seg_len = (p.NC + p.nseg - 1) / p.nseg;
-  p.scan_phase = 0;
   p.seg_state = nullptr;
   p.seg_trans = nullptr;
   if (p.nseg > 1) {

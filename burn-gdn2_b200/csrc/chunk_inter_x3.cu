@@ -59,7 +59,9 @@ __device__ __forceinline__ float silu_acc(float g) { return __fdividef(g, 1.0f +
 
 // XCHG: a chain as two CTAs of V / 2 columns (a 2-CTA cluster: V = 256, or V = 128 with few chains) that
 // exchange the RMS norm's row sums; a separate instantiation keeps the one-slice kernel free of that code.
-template <typename TIN, bool XCHG>
+// PHA: scan phase A (segment end states from zero and segment transitions, no output); its own instantiation
+// keeps the transition slice's branches out of the output kernels.
+template <typename TIN, bool XCHG, bool PHA>
 __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   using namespace nx3;
   extern __shared__ __align__(1024) unsigned char smraw[];
@@ -77,7 +79,7 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
   // blockIdx.z = (batch entry, segment of the chain); blockIdx.x = column slice.  Scan phase A: slices
   // 0 .. VF / V - 1 carry the state's value columns (from a zero start, U from the record), slice VF / V the
   // segment's transition (K columns from the identity, U = 0); no output.
-  const bool scanA = p.scan_phase == 1;
+  constexpr bool scanA = PHA;
   const int zseg = scanA ? p.nseg - 1 : p.nseg;  // segments in the grid: phase A skips the last one
   const int hv = blockIdx.y, seg = blockIdx.z % zseg, bb = blockIdx.z / zseg;
   const int V = p.vt, HALF = V / 2;  // columns of this CTA's slice
@@ -358,9 +360,10 @@ __global__ void __launch_bounds__(256, 1) k_inter_x3(const TcParams p) {
       }
     } else {
       float u[64];  // U rows of this chunk: read while MMA1 runs (zero for a transition slice)
-      #pragma unroll
-      for (int j = 0; j < 64; ++j) u[j] = 0.f;
-      if (!tslice) {
+      if (tslice) {
+        #pragma unroll
+        for (int j = 0; j < 64; ++j) u[j] = 0.f;
+      } else {
         const float4* src = u_row(c);
         const int sw = lane & 7;  // = row & 7
         #pragma unroll
@@ -572,11 +575,12 @@ static int launch_inter_x3_t(const TcParams& p0, cudaStream_t st) {
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return check_cuda(cudaGetLastError(), "chunk inter (x3) device query");
   const size_t smem = nx3::TOTAL + 1024;
-  for (void (*f)(const TcParams) : {k_inter_x3<TIN, true>, k_inter_x3<TIN, false>}) {
+  for (void (*f)(const TcParams) : {k_inter_x3<TIN, true, false>, k_inter_x3<TIN, false, false>,
+                                     k_inter_x3<TIN, false, true>}) {
     const cudaError_t e = cudaFuncSetAttribute((const void*)f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return check_cuda(e, "chunk inter (x3) smem attribute");
   }
-  auto launch = [&](const TcParams& p, int slices, int zseg, bool xchg) {
+  auto launch = [&](const TcParams& p, int slices, int zseg, bool xchg, bool pha) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(slices, p.HV, p.B * zseg);
     cfg.blockDim = dim3(256);
@@ -591,16 +595,16 @@ static int launch_inter_x3_t(const TcParams& p0, cudaStream_t st) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
     }
-    return check_cuda(cudaLaunchKernelEx(&cfg, xchg ? k_inter_x3<TIN, true> : k_inter_x3<TIN, false>, p),
-                      "chunk inter (x3) launch");
+    void (*fn)(const TcParams) =
+        pha ? k_inter_x3<TIN, false, true> : xchg ? k_inter_x3<TIN, true, false> : k_inter_x3<TIN, false, false>;
+    return check_cuda(cudaLaunchKernelEx(&cfg, fn, p), "chunk inter (x3) launch");
   };
   if (p0.nseg > 1) {
     // phase A: (N, M) of segments 0 .. nseg - 2, one CTA per 128-column slice of the state and one for the
     // transition (no cluster: no output)
     TcParams a = p0;
-    a.scan_phase = 1;
     a.vt = 128;
-    int rc = launch(a, p0.V / 128 + 1, p0.nseg - 1, false);
+    int rc = launch(a, p0.V / 128 + 1, p0.nseg - 1, false, true);
     if (rc) return rc;
     // phase B
     const size_t bsmem = (TC_K * 129 + TC_K * 32) * sizeof(float);
@@ -613,7 +617,7 @@ static int launch_inter_x3_t(const TcParams& p0, cudaStream_t st) {
   }
   // phase C (or the whole chain when nseg = 1)
   const TcParams p = inter_x3_split(p0, sms);
-  return launch(p, p.vsplit, p.nseg, p.vsplit > 1 && p.fuse_epilogue);
+  return launch(p, p.vsplit, p.nseg, p.vsplit > 1 && p.fuse_epilogue, false);
 }
 
 int launch_inter_x3(const TcParams& p, int dtype, cudaStream_t st) {

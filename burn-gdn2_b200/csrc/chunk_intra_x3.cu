@@ -85,23 +85,21 @@ __device__ __forceinline__ void prefetch_rows_x3(const TcParams& p, int item, in
   const int kh = hv / p.rep, t0 = c * TC_C, cv = min(TC_C, p.T - t0);
   constexpr int LQ = 128 * (int)sizeof(TIN) / 128;    // lines of a q / k / b row
   const int lv = max(1, p.V * (int)sizeof(TIN) / 128);  // lines of a v / w row
-  const int per_row = 3 * LQ + 2 * lv + 4;             // + four lines of g (f32)
-  for (int idx = lane; idx < 8 * per_row; idx += 32) {
-    const int r = r0 + idx / per_row;
-    int j = idx % per_row;
-    if (r >= cv) continue;
-    const char* a;
-    if (j < 3 * LQ) {
-      const DView& v = j < LQ ? p.q : j < 2 * LQ ? p.k : p.b;
-      a = reinterpret_cast<const char*>(vptr<TIN>(v, bb, kh, t0 + r, 0)) + (j % LQ) * 128;
-    } else if ((j -= 3 * LQ) < 2 * lv) {
-      const DView& v = j < lv ? p.v : p.w;
-      a = reinterpret_cast<const char*>(vptr<TIN>(v, bb, hv, t0 + r, 0)) + (j % lv) * 128;
-    } else {
-      a = reinterpret_cast<const char*>(static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 +
-                                        (int64_t)(t0 + r) * p.g.s2) + (j - 2 * lv) * 128;
-    }
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+  // lane: row r0 + lane / 4, every fourth line of that row's q, k, b, v, w and g (f32, four lines) from lane % 4
+  const int r = r0 + (lane >> 2), q4 = lane & 3;
+  if (r >= cv) return;
+  const char* rows[6] = {
+      reinterpret_cast<const char*>(vptr<TIN>(p.q, bb, kh, t0 + r, 0)),
+      reinterpret_cast<const char*>(vptr<TIN>(p.k, bb, kh, t0 + r, 0)),
+      reinterpret_cast<const char*>(vptr<TIN>(p.b, bb, kh, t0 + r, 0)),
+      reinterpret_cast<const char*>(vptr<TIN>(p.v, bb, hv, t0 + r, 0)),
+      reinterpret_cast<const char*>(vptr<TIN>(p.w, bb, hv, t0 + r, 0)),
+      reinterpret_cast<const char*>(static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 +
+                                    (int64_t)(t0 + r) * p.g.s2)};
+  #pragma unroll
+  for (int s = 0; s < 6; ++s) {
+    const int nl = s < 3 ? LQ : s < 5 ? lv : 4;
+    for (int j = q4; j < nl; j += 4) asm volatile("prefetch.global.L2 [%0];" ::"l"(rows[s] + j * 128));
   }
 }
 

@@ -49,9 +49,9 @@ struct TcParams {
   size_t rec_bytes;
   unsigned char* scratch;  // split-operand intra kernel: one L2-resident slot per CTA (after the records)
   // chunk-parallel state scan of the split-operand inter kernel (nseg = 1: one CTA walks the whole chain):
-  // the chain's chunks in nseg segments of seg_len; scan_phase 1 computes each segment's end state from zero
-  // and its state transition, scan_phase 0 (with nseg > 1) runs the segments from their start states.
-  int nseg, seg_len, scan_phase;
+  // the chain's chunks in nseg segments of seg_len; phase A computes each segment's end state from zero and
+  // its state transition, then (nseg > 1) the segments run from their start states.
+  int nseg, seg_len;
   float* seg_state;  // [B][HV][nseg][K][V]: slot s = the start state of segment s
   float* seg_trans;  // [B][HV][nseg - 1][K][K]: the transition over segment s
 };
