@@ -111,17 +111,21 @@ __device__ __forceinline__ void split2f(float x0, float x1, uint32_t& hi, uint32
   const float l0 = x0 - __uint_as_float(hi << 16), l1 = x1 - __uint_as_float(hi & 0xffff0000u);
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(l1), "f"(l0));
 }
+// The same for a packed pair: the two subtractions as one sub.f32x2 (same results: x - hi is exact).
 __device__ __forceinline__ void split2(f32x2 x, uint32_t& hi, uint32_t& lo) {
   float x0, x1;
   f2un(x, x0, x1);
-  split2f(x0, x1, hi, lo);
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+  float l0, l1;
+  f2un(f2sub(x, f2pk(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u))), l0, l1);
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(l1), "f"(l0));
 }
 // 8 consecutive f32 -> hi and lo images of 8 bf16 (one 16-byte chunk each)
 __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
-  split2f(v[0], v[1], hi.x, lo.x);
-  split2f(v[2], v[3], hi.y, lo.y);
-  split2f(v[4], v[5], hi.z, lo.z);
-  split2f(v[6], v[7], hi.w, lo.w);
+  split2(f2pk(v[0], v[1]), hi.x, lo.x);
+  split2(f2pk(v[2], v[3]), hi.y, lo.y);
+  split2(f2pk(v[4], v[5]), hi.z, lo.z);
+  split2(f2pk(v[6], v[7]), hi.w, lo.w);
 }
 
 // Four consecutive input elements of one row as two f32 pairs, read with a
