@@ -265,26 +265,35 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
       float gl[4] = {off[0], off[1], off[2], off[3]};
       Raw4<TIN> nq, nk, nb, nv, nw, nv2, nw2;  // nv2, nw2: value channels 128 + ch (V = 256)
       float4 ng;
+      // this lane's elements of row r0 of each input, advanced by one row per fetch
+      const TIN* aq = static_cast<const TIN*>(vptr<TIN>(p.q, bb, kh, t0 + r0, ch));
+      const TIN* ak = static_cast<const TIN*>(vptr<TIN>(p.k, bb, kh, t0 + r0, ch));
+      const TIN* ab = static_cast<const TIN*>(vptr<TIN>(p.b, bb, kh, t0 + r0, ch));
+      const TIN* av = static_cast<const TIN*>(vptr<TIN>(p.v, bb, hv, t0 + r0, ch));
+      const TIN* aw = static_cast<const TIN*>(vptr<TIN>(p.w, bb, hv, t0 + r0, ch));
+      const float* ag = gbase + (int64_t)(t0 + r0) * p.g.s2;
       auto fetch = [&](int i) {
         const int r = r0 + i;
-        ng = g_row(i);
         nq.zero(); nk.zero(); nb.zero(); nv.zero(); nw.zero();
+        ng = make_float4(0.f, 0.f, 0.f, 0.f);
         if (V256) {
           nv2.zero(); nw2.zero();
         }
         if (r < cv) {
-          nq.load(vptr<TIN>(p.q, bb, kh, t0 + r, ch), pol_kin);
-          nk.load(vptr<TIN>(p.k, bb, kh, t0 + r, ch), pol_kin);
-          nb.load(vptr<TIN>(p.b, bb, kh, t0 + r, ch), pol_kin);
+          ng = ld_f4_nc_x3(ag, pol_kin);
+          nq.load(aq, pol_kin);
+          nk.load(ak, pol_kin);
+          nb.load(ab, pol_kin);
           if (ch < V) {
-            nv.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch), pol_in);
-            nw.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch), pol_in);
+            nv.load(av, pol_in);
+            nw.load(aw, pol_in);
           }
           if (V256) {
-            nv2.load(vptr<TIN>(p.v, bb, hv, t0 + r, ch + 128), pol_in);
-            nw2.load(vptr<TIN>(p.w, bb, hv, t0 + r, ch + 128), pol_in);
+            nv2.load(av + 128, pol_in);
+            nw2.load(aw + 128, pol_in);
           }
         }
+        aq += p.q.s2; ak += p.k.s2; ab += p.b.s2; av += p.v.s2; aw += p.w.s2; ag += p.g.s2;
       };
       fetch(0);
       #pragma unroll 1
