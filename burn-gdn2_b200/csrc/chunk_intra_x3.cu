@@ -38,13 +38,16 @@
 namespace gdn2 {
 
 namespace ix3 {
-// step 2, the operands of two row tiles pa < pb (tiles 0, 3 in shared memory; tiles 1, 2 in the scratch slot
-// with the same offsets): X_pa, X_pb K-major [32][128]; Ks_pa K-major [16(pa+1)][128], Ks_pb K-major
-// [16(pb+1)][128]; each a hi image followed by its lo image.  Tiles {0, 3}: Ks_0 4 + 4 KB, Ks_3 at 40960
-// (16 + 16 KB); tiles {1, 2}: Ks_1 8 + 8 KB, Ks_2 at 49152 (12 + 12 KB); both end at 73728.
-constexpr uint32_t XA = 0;               // X_pa hi 8 KB, lo at +8 KB
-constexpr uint32_t XB = 16384;           // X_pb hi, lo
-constexpr uint32_t KSA = 32768;          // Ks_pa hi, lo after it, then Ks_pb hi and lo
+// step 2, the operands of a pair of row tiles pa < pb (tiles 0, 3 in shared memory; tiles 1, 2 in the scratch
+// slot with the same offsets), each a hi image followed by its lo image, so that the pair's scores are one
+// M = 64, N = 80 product per k-step:
+//   X  K-major [64][128]: rows 0..31 = X_pa (its 16 q rows, then its 16 b k rows), rows 32..63 = X_pb;
+//   Ks K-major [80][128]: rows 0 .. 16(pa+1)-1 = Ks_pa (the keys of tiles 0..pa at tile pa's reference
+//      point), then the 16(pb+1) rows of Ks_pb;
+// D = X Ks^T: row i of X against every key row; the cross blocks (X_pa . Ks_pb, X_pb . Ks_pa) are not read.
+constexpr uint32_t XA = 0;               // X hi 16 KB, lo at +16 KB
+constexpr uint32_t KSA = 32768;          // Ks hi 20 KB, lo at +20 KB; ends at 73728
+constexpr int XS_R = 64, KS_R = 80;      // rows of the two stacked operands
 constexpr uint32_t R_END = 81920;
 // step 3 (the buffer reused once both score MMA passes completed)
 constexpr int SS = 68;                   // row stride (floats) of AKK and TINV
@@ -248,15 +251,16 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
             cks2[pp][m] = f2pk(__expf(Gb[pp][j0] - Gbp[j0]), __expf(Gb[pp][j1] - Gbp[j1]));
         }
       }
-      // X image of this row tile: tiles 0 / 3 at XA / XB of the shared buffer, tiles 1 / 2 at XA / XB of the slot
-      unsigned char* const xr = (tp == 0 || tp == 3 ? sm : slot) + ((tp == 0 || tp == 1) ? XA : XB) +
-                                kb * 32 * 128 + hh * 1024 + eb;
-      // Ks_pp images (hi, then lo after 4096 (pp + 1) bytes): Ks_0 at KSA, Ks_3 at KSA + 8192 (shared buffer);
-      // Ks_1 at KSA, Ks_2 at KSA + 16384 (slot)
+      // X rows of this row tile: tiles 0 / 3 in the shared buffer, 1 / 2 in the slot; the pair's first tile at
+      // stacked rows 0..31, its second at 32..63
+      unsigned char* const xr = (tp == 0 || tp == 3 ? sm : slot) + XA + kb * XS_R * 128 +
+                                ((tp == 0 || tp == 1) ? 0 : 4096) + hh * 1024 + eb;
+      // Ks_pp rows of this thread's key rows (16 tp + 8 hh + i): Ks_0 / Ks_1 from stacked row 0, Ks_3 from row 16,
+      // Ks_2 from row 32
       auto ks_row = [&](int pp) {
         unsigned char* const base = (pp == 0 || pp == 3) ? sm : slot;
-        const uint32_t o = pp == 0 ? KSA : pp == 3 ? KSA + 8192 : pp == 1 ? KSA : KSA + 16384;
-        return base + o + kb * 16 * (pp + 1) * 128 + rg * 1024 + eb;
+        const int row0 = pp == 3 ? 16 : pp == 2 ? 32 : 0;
+        return base + KSA + kb * KS_R * 128 + (row0 / 8 + rg) * 1024 + eb;
       };
       unsigned char* const wqr = rec + L.wq_hi + kb * 128 * 128 + (8 + rg) * 1024 + eb;
       unsigned char* const kdr = rec + L.kd_hi + kb * 64 * 128 + rg * 1024 + eb;
@@ -312,13 +316,13 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
           qs2[m] = f2mul(cq.pair(m), e2);
           bks2[m] = f2mul(f2mul(cb.pair(m), k2), e2);
         }
-        // X rows: q part at row 8 hh + i, b k part at 16 + 8 hh + i of the tile's [32][128] image
-        put_split4(xr + ro, 8192, qs2[0], qs2[1]);
-        put_split4(xr + 2048 + ro, 8192, bks2[0], bks2[1]);
+        // X rows: q part at row 8 hh + i, b k part at 16 + 8 hh + i of the tile's 32 rows
+        put_split4(xr + ro, 16384, qs2[0], qs2[1]);
+        put_split4(xr + 2048 + ro, 16384, bks2[0], bks2[1]);
         #pragma unroll
         for (int pp = 0; pp < 4; ++pp) {
           if (pp < tp) continue;
-          put_split4(ks_row(pp) + ro, 4096 * (pp + 1), f2mul(kinv2[0], cks2[pp][0]), f2mul(kinv2[1], cks2[pp][1]));
+          put_split4(ks_row(pp) + ro, KS_R * 256, f2mul(kinv2[0], cks2[pp][0]), f2mul(kinv2[1], cks2[pp][1]));
         }
         put_split4_g(wqr + ro, L.wq_lo - L.wq_hi, f2mul(qs2[0], eGbpS2[0]), f2mul(qs2[1], eGbpS2[1]), pol_rec);
         put_split4_g(kdr + ro, L.kd_lo - L.kd_hi, f2mul(kinv2[0], edk2[0]), f2mul(kinv2[1], edk2[1]), pol_rec);
@@ -339,35 +343,31 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     __syncthreads();
     umma::fence_after_sync();
 
-    // score MMAs D_p = Ks_hi X_hi + Ks_lo X_hi + Ks_hi X_lo: row tiles 0 and 3 from the buffer; then, once
-    // they have read it, tiles 1 and 2 after one bulk copy of the slot's image into the same buffer
+    // score MMAs of a tile pair, D = X_hi Ks_hi^T + X_hi Ks_lo^T + X_lo Ks_hi^T (M = 64, N = 80): tiles {0, 3}
+    // from the buffer into TMEM columns [0, 80); then, once they have read it, tiles {1, 2} after one bulk copy
+    // of the slot's images into the same buffer, into columns [128, 208)
     if (tid == 0) {
-      const uint32_t idesc = umma::idesc_bf16(64, 32, false, false);
+      const uint32_t idesc = umma::idesc_bf16(64, KS_R, false, false);
       const uint32_t sbase = smem_u32(sm);
-      auto score_mmas = [&](int pa, int pb) {
+      auto pair_mmas = [&](uint32_t dcol) {
         #pragma unroll 1
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int pp = q2 ? pb : pa;
-          const uint32_t ks = q2 ? KSA + 8192 * (pa + 1) : KSA, x = q2 ? XB : XA;
-          #pragma unroll 1
-          for (int ps = 0; ps < 3; ++ps) {
-            const uint64_t dks = umma::desc_kmaj_base(sbase + ks + (ps == 1 ? 4096 * (pp + 1) : 0));
-            const uint64_t dxs = umma::desc_kmaj_base(sbase + x + (ps == 2 ? 8192 : 0));
-            #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              umma::mma_bf16(tA + 32 * pp, umma::desc_kmaj_at(dks, 16 * (pp + 1), j),
-                             umma::desc_kmaj_at(dxs, 32, j), idesc, ps > 0 || j > 0);
-          }
+        for (int ps = 0; ps < 3; ++ps) {
+          const uint64_t dxs = umma::desc_kmaj_base(sbase + XA + (ps == 2 ? 16384 : 0));
+          const uint64_t dks = umma::desc_kmaj_base(sbase + KSA + (ps == 1 ? KS_R * 256 : 0));
+          #pragma unroll
+          for (int j = 0; j < 8; ++j)
+            umma::mma_bf16(tA + dcol, umma::desc_kmaj_at(dxs, XS_R, j), umma::desc_kmaj_at(dks, KS_R, j), idesc,
+                           ps > 0 || j > 0);
         }
       };
-      score_mmas(0, 3);
+      pair_mmas(0);
       umma::commit(&bars[0]);
       mbar_wait_bounded(&bars[0], par);
       umma::fence_after_sync();
       mbar_arrive_expect_tx(&bars[3], (unsigned)X3_SLOT_PASSB);
       bulk_g2s(sm, slot, (unsigned)X3_SLOT_PASSB, &bars[3]);
       mbar_wait_bounded(&bars[3], par);
-      score_mmas(1, 2);
+      pair_mmas(128);
       umma::commit(&bars[1]);
     }
     if (item + (int)gridDim.x < nitems) prefetch_rows_x3<TIN>(p, item + gridDim.x, r0, lane);
@@ -377,24 +377,53 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     float* sAkk = reinterpret_cast<float*>(sm + AKK);
     float* sTinv = reinterpret_cast<float*>(sm + TINV);
     {
-      const int sp = warp & 3, s = 16 * sp + lane;  // valid for lane < 16 (M = 64 TMEM layout)
-      #pragma unroll
-      for (int pq = 0; pq < 2; ++pq) {
-        const int pp = 2 * (warp >> 2) + pq;
-        float vq[16], vk[16];
-        umma::ld16(umma::taddr(tA, 32 * sp, 32 * pp), vq);
-        umma::ld16(umma::taddr(tA, 32 * sp, 32 * pp + 16), vk);
+      // warp w: pair w / 4 (TMEM columns from 128 (w / 4)), sub-partition w % 4 = D rows 16 (w % 4) + lane
+      // (lane < 16, the M = 64 layout): the q rows (even sub-partitions) or b k rows (odd) of the pair's first
+      // (sub-partitions 0, 1) or second tile, one query row per lane, against that tile's 16 (t + 1) keys
+      const int sp = warp & 3, pr = warp >> 2;
+      const int t = pr == 0 ? (sp < 2 ? 0 : 3) : (sp < 2 ? 1 : 2);
+      const int kc0 = (sp < 2) ? 0 : (pr == 0 ? 16 : 32);  // first key column of tile t in D
+      const int i = 16 * t + lane;                           // query row (lane < 16)
+      const bool qrow = (sp & 1) == 0;
+      for (int c16 = 0; c16 <= t; ++c16) {
+        float v[16];
+        umma::ld16(umma::taddr(tA, 32 * sp, 128 * pr + kc0 + 16 * c16), v);
         umma::wait_ld();
         if (lane < 16) {
-          #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int r = 16 * pp + j;
-            const float aq = (s <= r) ? vq[j] * p.scale : 0.f;
-            const __nv_bfloat16 ah = __float2bfloat16_rn(aq);
-            const uint32_t o = umma::kmaj_off(r, s, 64);
-            *reinterpret_cast<__nv_bfloat16*>(sm + AQK_HI + o) = ah;
-            *reinterpret_cast<__nv_bfloat16*>(sm + AQK_LO + o) = __float2bfloat16_rn(aq - __bfloat162float(ah));
-            sAkk[r * SS + s] = (s < r) ? vk[j] : 0.f;
+          const int j0 = 16 * c16;
+          if (qrow) {  // Aqk row i, keys j0 .. j0 + 15: scale (q . k decay) for j <= i
+            #pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = (j0 + j <= i) ? v[j] * p.scale : 0.f;
+            uint4 h0, l0, h1, l1;
+            split8(v, h0, l0);
+            split8(v + 8, h1, l1);
+            const uint32_t o0 = umma::kmaj_chunk(i, j0 / 8, 64), o1 = umma::kmaj_chunk(i, j0 / 8 + 1, 64);
+            *reinterpret_cast<uint4*>(sm + AQK_HI + o0) = h0;
+            *reinterpret_cast<uint4*>(sm + AQK_HI + o1) = h1;
+            *reinterpret_cast<uint4*>(sm + AQK_LO + o0) = l0;
+            *reinterpret_cast<uint4*>(sm + AQK_LO + o1) = l1;
+          } else {  // Akk row i: (b k . k decay) for j < i
+            float4* arow = reinterpret_cast<float4*>(sAkk + i * SS + j0);
+            #pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              arow[j / 4] = make_float4((j0 + j < i) ? v[j] : 0.f, (j0 + j + 1 < i) ? v[j + 1] : 0.f,
+                                        (j0 + j + 2 < i) ? v[j + 2] : 0.f, (j0 + j + 3 < i) ? v[j + 3] : 0.f);
+          }
+        }
+      }
+      if (lane < 16) {  // the keys after tile t: zero
+        for (int j0 = 16 * (t + 1); j0 < 64; j0 += 16) {
+          if (qrow) {
+            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t o0 = umma::kmaj_chunk(i, j0 / 8, 64), o1 = umma::kmaj_chunk(i, j0 / 8 + 1, 64);
+            *reinterpret_cast<uint4*>(sm + AQK_HI + o0) = z;
+            *reinterpret_cast<uint4*>(sm + AQK_HI + o1) = z;
+            *reinterpret_cast<uint4*>(sm + AQK_LO + o0) = z;
+            *reinterpret_cast<uint4*>(sm + AQK_LO + o1) = z;
+          } else {
+            float4* arow = reinterpret_cast<float4*>(sAkk + i * SS + j0);
+            #pragma unroll
+            for (int j = 0; j < 4; ++j) arow[j] = make_float4(0.f, 0.f, 0.f, 0.f);
           }
         }
       }
