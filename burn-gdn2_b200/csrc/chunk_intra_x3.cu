@@ -59,10 +59,12 @@ constexpr uint32_t AQK_LO = 57344;
 constexpr uint32_t TI_HI = 65536;        // bf16 K-major [64][64]: T = (I + Akk)^-1
 constexpr uint32_t TI_LO = 73728;
 // step 4 (the f32 tiles of step 3 are dead, the Aqk images copied out): the slot's rhs images, same offsets
-// at X3_SLOT_PASSB in the slot
+// at X3_SLOT_PASSB in the slot.  rhs_k and rhs_v side by side form one MN-major [64][128 + V] operand (hi,
+// then lo), so W and U are one MMA per k-step; at V = 256 the second rhs_v half follows at 65536 (hi) and
+// 81920 (lo) in the slot
 constexpr uint32_t RK_HI = 0;            // bf16 MN-major [64][128]
-constexpr uint32_t RK_LO = 16384;
-constexpr uint32_t RV_HI = 32768;        // bf16 MN-major [64][V]
+constexpr uint32_t RV_HI = 16384;        // bf16 MN-major [64][min(V, 128)], N groups 2, 3 of the operand
+constexpr uint32_t RK_LO = 32768;
 constexpr uint32_t RV_LO = 49152;
 // step 5 (after the W / U MMAs completed)
 constexpr uint32_t WST_HI = 0;           // W rows: K-major [64][128] (two 8 KB column blocks)
@@ -328,8 +330,8 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
         put_split4_g(kdr + ro, L.kd_lo - L.kd_hi, f2mul(kinv2[0], edk2[0]), f2mul(kinv2[1], edk2[1]), pol_rec);
         put_split4(rkr + ro, RK_LO - RK_HI, f2mul(bks2[0], eGbp2[0]), f2mul(bks2[1], eGbp2[1]));
         if (ch < V) put_split4(rvr + ro, RV_LO - RV_HI, f2mul(cw.pair(0), cvv.pair(0)), f2mul(cw.pair(1), cvv.pair(1)));
-        if (V256)  // the second rhs_v half, 32 KB after the first in the slot
-          put_split4(rvr + 32768 + ro, RV_LO - RV_HI, f2mul(cw2.pair(0), cv2.pair(0)), f2mul(cw2.pair(1), cv2.pair(1)));
+        if (V256)  // the second rhs_v half
+          put_split4(rvr + (65536 - RV_HI) + ro, 16384, f2mul(cw2.pair(0), cv2.pair(0)), f2mul(cw2.pair(1), cv2.pair(1)));
       }
     }
     if (warp == 0) {
@@ -546,19 +548,14 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
       bulk_g2s(sm + RK_HI, slot + X3_SLOT_PASSB, 65536u, &bars[4]);
       mbar_wait_bounded(&bars[4], par);
       const uint32_t sbase = smem_u32(sm);
-      const uint32_t iw = umma::idesc_bf16(64, 128, false, true);
-      const uint32_t iu = umma::idesc_bf16(64, VU, false, true);
+      const uint32_t iwu = umma::idesc_bf16(64, 128 + VU, false, true);  // [W | U] = T [rhs_k | rhs_v]
       #pragma unroll 1
       for (int ps = 0; ps < 3; ++ps) {
         const uint64_t dt = umma::desc_kmaj_base(sbase + (ps == 1 ? TI_LO : TI_HI));
-        const uint64_t drk = umma::desc_mnmaj_base(sbase + (ps == 2 ? RK_LO : RK_HI), 64);
-        const uint64_t drv = umma::desc_mnmaj_base(sbase + (ps == 2 ? RV_LO : RV_HI), 64);
+        const uint64_t drhs = umma::desc_mnmaj_base(sbase + (ps == 2 ? RK_LO : RK_HI), 64);
         #pragma unroll
         for (int j = 0; j < 4; ++j)
-          umma::mma_bf16(tA, umma::desc_kmaj_at(dt, 64, j), umma::desc_mnmaj_at(drk, j), iw, ps > 0 || j > 0);
-        #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          umma::mma_bf16(tA + 128, umma::desc_kmaj_at(dt, 64, j), umma::desc_mnmaj_at(drv, j), iu, ps > 0 || j > 0);
+          umma::mma_bf16(tA, umma::desc_kmaj_at(dt, 64, j), umma::desc_mnmaj_at(drhs, j), iwu, ps > 0 || j > 0);
       }
       umma::commit(&bars[2]);
     }
@@ -625,7 +622,8 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
         umma::fence_after_sync();  // the first U half is read out of TMEM
         bulk_wait_read_all();
         mbar_arrive_expect_tx(&bars[5], 32768u);
-        bulk_g2s(sm + RV_HI, slot + X3_SLOT_PASSB + 65536, 32768u, &bars[5]);
+        bulk_g2s(sm + RV_HI, slot + X3_SLOT_PASSB + 65536, 16384u, &bars[5]);
+        bulk_g2s(sm + RV_LO, slot + X3_SLOT_PASSB + 81920, 16384u, &bars[5]);
         mbar_wait_bounded(&bars[5], par);
         const uint32_t sbase = smem_u32(sm);
         const uint32_t iu = umma::idesc_bf16(64, 128, false, true);
