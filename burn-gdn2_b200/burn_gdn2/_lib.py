@@ -86,6 +86,7 @@ EXPORTS = (
     "gdn2_recurrent_fwd", "gdn2_short_conv", "gdn2_rms_norm_gate", "gdn2_config_validate",
     "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
     "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc", "gdn2_project_activations", "gdn2_selftest_wait",
+    "gdn2_set_reserved_sms",
 )
 
 
@@ -122,6 +123,8 @@ def _load():
     lib.gdn2_selftest_umma.restype = ctypes.c_int
     lib.gdn2_selftest_wait.argtypes = [ctypes.c_uint32, i32, ctypes.POINTER(ctypes.c_int32)]
     lib.gdn2_selftest_wait.restype = ctypes.c_int
+    lib.gdn2_set_reserved_sms.argtypes = [i32]
+    lib.gdn2_set_reserved_sms.restype = ctypes.c_int
     return lib
 
 

@@ -5,6 +5,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "chunk.cuh"
@@ -105,19 +106,21 @@ static size_t rec_bytes(const gdn2_dims& d, bool x3) {
   return x3 ? x3_record_layout(d.head_v_dim).bytes : tc_record_layout(d.head_v_dim).bytes;
 }
 
-// SMs of the current device (148 on a B200 if the query fails): sizes the scan segments.
-static int device_sms() {
+static std::atomic<int> g_reserved_sms{0};
+
+int usable_sms() {
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
       sms <= 0) {
     cudaGetLastError();
-    return 148;
+    sms = 148;
   }
-  return sms;
+  const int r = g_reserved_sms.load(std::memory_order_relaxed);
+  return sms - r >= sms / 2 ? sms - r : sms / 2;
 }
 
 static int scan_segments(const gdn2_dims& d, bool x3) {
-  return x3 ? x3_scan_segments(d.batch, d.num_v_heads, (d.seq_len + TC_C - 1) / TC_C, d.head_v_dim, device_sms())
+  return x3 ? x3_scan_segments(d.batch, d.num_v_heads, (d.seq_len + TC_C - 1) / TC_C, d.head_v_dim, usable_sms())
             : 1;
 }
 
@@ -340,6 +343,11 @@ int gdn2_selftest_umma(int32_t test, const float* a, const float* b, float* d, v
   if (test < 0 || test > 3) return set_error(GDN2_EINVAL, "gdn2_selftest_umma: test %d not in 0..3", test);
   if (!a || !b || !d) return set_error(GDN2_EINVAL, "gdn2_selftest_umma: null pointer");
   return selftest_umma(test, a, b, d, (cudaStream_t)stream);
+}
+
+int gdn2_set_reserved_sms(int32_t n) {
+  n = n < 0 ? 0 : n > 64 ? 64 : n;
+  return g_reserved_sms.exchange(n);
 }
 
 int gdn2_selftest_wait(uint32_t spins, int32_t arrive, int32_t* completed) {

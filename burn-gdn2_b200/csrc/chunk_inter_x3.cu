@@ -571,9 +571,7 @@ static TcParams inter_x3_split(const TcParams& p, int sms) {
 
 template <typename TIN>
 static int launch_inter_x3_t(const TcParams& p0, cudaStream_t st) {
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return check_cuda(cudaGetLastError(), "chunk inter (x3) device query");
+  const int sms = usable_sms();  // less the SMs the host reserved for its own work
   const size_t smem = nx3::TOTAL + 1024;
   for (void (*f)(const TcParams) : {k_inter_x3<TIN, true, false>, k_inter_x3<TIN, false, false>,
                                      k_inter_x3<TIN, false, true>}) {

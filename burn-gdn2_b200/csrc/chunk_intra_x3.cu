@@ -655,10 +655,7 @@ static int launch_intra_x3_t(const TcParams& p, cudaStream_t st) {
   void (*fn)(const TcParams, int) = p.V > 128 ? k_intra_x3<TIN, true> : k_intra_x3<TIN, false>;
   cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "chunk intra (x3) smem attribute");
-  int dev = 0, sms = 0;
-  e = cudaGetDevice(&dev);
-  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return check_cuda(e, "chunk intra (x3) SM count");
+  const int sms = usable_sms();  // less the SMs the host reserved for its own work
   const long long items = (long long)p.NC * p.HV * p.B;
   if (items > 0x7fffffffLL) return set_error(GDN2_EUNSUPPORTED, "chunk intra (x3): %lld chunk items", items);
   const long long slots = 2LL * sms;  // two CTAs per SM (87 KB of shared memory, 256 TMEM columns each)

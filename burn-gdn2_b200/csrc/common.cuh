@@ -74,4 +74,6 @@ __device__ __forceinline__ float block_sum(float x, float* red) {
 namespace gdn2 {
 int set_error(int code, const char* fmt, ...);
 int check_cuda(cudaError_t e, const char* where);
+// SMs of the current device less those reserved by gdn2_set_reserved_sms (148 on a B200 if the query fails)
+int usable_sms();
 }  // namespace gdn2

@@ -318,6 +318,18 @@ GDN2_API int gdn2_selftest_umma(int32_t test, const float* a, const float* b, fl
  * Synchronises the current device. */
 GDN2_API int gdn2_selftest_wait(uint32_t spins, int32_t arrive, int32_t* completed);
 
+/* SMs that the split-operand chunk kernels leave free (no counterpart in
+ * the reference; default 0).  Those kernels otherwise fill every SM for
+ * their duration (two CTAs per SM holding all registers, or one CTA per SM
+ * holding most of the shared memory), so a host that runs its own work
+ * beside a chunked forward on another stream -- for example the NCCL
+ * all-reduce of a head-sharded layer's previous token range -- reserves SMs
+ * for it here.  Process-wide, for every device; clamped to [0, 64]; returns
+ * the previous value.  The workspace size of a chunk call can depend on it
+ * (the chunk-parallel scan sizes its segments by the usable SMs): query the
+ * size after changing it. */
+GDN2_API int gdn2_set_reserved_sms(int32_t n);
+
 /* Error / version queries. */
 GDN2_API const char* gdn2_last_error(void);
 GDN2_API int gdn2_last_cuda_error(void);

@@ -180,6 +180,7 @@ extern "C" {
     pub fn gdn2_read_device_errors(flags: *mut u32) -> i32;
     pub fn gdn2_selftest_umma(test: i32, a: *const f32, b: *const f32, d: *mut f32, stream: *mut c_void) -> i32;
     pub fn gdn2_selftest_wait(spins: u32, arrive: i32, completed: *mut i32) -> i32;
+    pub fn gdn2_set_reserved_sms(n: i32) -> i32;
     pub fn gdn2_last_error() -> *const c_char;
     pub fn gdn2_last_cuda_error() -> i32;
     pub fn gdn2_abi_version() -> i32;

@@ -216,3 +216,18 @@ def test_config_mirror_validate():
         bg.Gdn2Config(num_v_heads=24).validate()
     with pytest.raises(ValueError, match="chunk_size must be > 0"):
         bg.Gdn2Config(chunk_size=0).validate()
+
+
+def test_set_reserved_sms_clamps_and_returns_previous():
+    """Host-only setting: the previous value comes back, the value is
+    clamped to [0, 64]; no device is touched."""
+    from burn_gdn2 import _lib
+
+    lib = _lib.LIB
+    prev = lib.gdn2_set_reserved_sms(16)
+    try:
+        assert lib.gdn2_set_reserved_sms(-5) == 16
+        assert lib.gdn2_set_reserved_sms(1000) == 0
+        assert lib.gdn2_set_reserved_sms(0) == 64
+    finally:
+        lib.gdn2_set_reserved_sms(prev)
