@@ -70,10 +70,16 @@ constexpr uint32_t RV_LO = 49152;
 constexpr uint32_t WST_HI = 0;           // W rows: K-major [64][128] (two 8 KB column blocks)
 constexpr uint32_t WST_LO = 16384;
 constexpr uint32_t UST = 32768;          // U f32 [64][V]
-constexpr uint32_t MISC = R_END;         // half-tile g sums [8][128] f32, sGlast [128] f32, barriers, tmem slot
-constexpr uint32_t TOTAL = MISC + 4096 + 512 + 64;
+constexpr uint32_t MISC = R_END;         // half-tile g sums [2][8][128] f32 and last-row cumsums [2][128] f32 (by
+                                         // chunk parity), sGlast [128] f32, barriers, tmem slot
+constexpr uint32_t TOTAL = MISC + 8192 + 1024 + 512 + 64;
 }  // namespace ix3
 
+__device__ __forceinline__ float4 ld_f4_nc_plain(const float* ptr) {
+  float4 r;
+  asm("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(ptr));
+  return r;
+}
 __device__ __forceinline__ float4 ld_f4_nc_x3(const float* ptr, uint64_t pol) {
   float4 r;
   asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
@@ -138,8 +144,9 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
   constexpr uint32_t TCOLS = 256;   // score D [0, 128), then W [0, 128) and U [128, 128 + V)
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char* sm = smraw + ((1024u - (smem_u32(smraw) & 1023u)) & 1023u);
-  float* sHalf = reinterpret_cast<float*>(sm + MISC);  // [8][128] g sums of each 8-row half tile
-  float* sGlast = sHalf + 8 * 128;
+  float* sHalfB = reinterpret_cast<float*>(sm + MISC);  // [2][8][128] g sums of each 8-row half tile
+  float* sGlrB = sHalfB + 2 * 8 * 128;                  // [2][128] half-local cumsum at the last valid row
+  float* sGlast = sGlrB + 2 * 128;
   // score MMAs of tiles 0 / 3, of tiles 1 / 2, W / U MMAs, the slot's score image, the slot's rhs images,
   // (V = 256) the slot's second rhs_v half, the second U MMA
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGlast + 128);
@@ -174,6 +181,28 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
   const uint64_t pol_rec = l2_policy_evict_first();
   const uint64_t pol_in = l2_policy_evict_first(), pol_kin = p.rep == 1 ? pol_in : l2_policy_evict_normal();
 
+  // step 1 of chunk item `itm` into buffer bf: the g sums of this warp's 8-row half tile, and the half-local
+  // cumsum at the chunk's last valid row (by the thread whose rows hold it).  For every chunk but a CTA's first
+  // this runs while the previous chunk's W / U MMAs do, on rows already prefetched to L2.
+  auto gsum_item = [&](int itm, int bf) {
+    const int c_ = itm % p.NC, hv_ = (itm / p.NC) % p.HV, bb_ = itm / (p.NC * p.HV);
+    const int t0_ = c_ * TC_C, cv_ = min(TC_C, p.T - t0_);
+    const float* gr = static_cast<const float*>(p.g.p) + bb_ * p.g.s0 + (hv_ / p.rep) * p.g.s1 + ch +
+                      (int64_t)(t0_ + r0) * p.g.s2;
+    float4 gv[8];
+    #pragma unroll
+    for (int i = 0; i < 8; ++i)
+      gv[i] = r0 + i < cv_ ? ld_f4_nc_plain(gr + (int64_t)i * p.g.s2) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float run[4] = {0.f, 0.f, 0.f, 0.f};
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      run[0] += gv[i].x; run[1] += gv[i].y; run[2] += gv[i].z; run[3] += gv[i].w;
+      if (r0 + i == cv_ - 1)
+        *reinterpret_cast<float4*>(sGlrB + bf * 128 + ch) = make_float4(run[0], run[1], run[2], run[3]);
+    }
+    *reinterpret_cast<float4*>(sHalfB + bf * 1024 + warp * 128 + ch) = make_float4(run[0], run[1], run[2], run[3]);
+  };
+
   int it = 0;
   for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++it) {
     const unsigned par = (unsigned)(it & 1);  // phase parity of every barrier (each completes once per chunk)
@@ -183,27 +212,10 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     const int cv = min(TC_C, p.T - t0);
     unsigned char* rec = p.rec + (size_t)item * p.rec_bytes;
     const float* gbase = static_cast<const float*>(p.g.p) + bb * p.g.s0 + kh * p.g.s1 + ch;
-    auto g_row = [&](int i) {
-      const int r = r0 + i;
-      return r < cv ? ld_f4_nc_x3(gbase + (int64_t)(t0 + r) * p.g.s2, pol_kin) : make_float4(0.f, 0.f, 0.f, 0.f);
-    };
 
-    // ---- 1. sums of g over each half tile ----
-    float glr[4] = {0.f, 0.f, 0.f, 0.f};  // half-local cumsum at the last valid row, if it is ours
-    {
-      float4 gv[8];
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) gv[i] = g_row(i);
-      float run[4] = {0.f, 0.f, 0.f, 0.f};
-      #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        run[0] += gv[i].x; run[1] += gv[i].y; run[2] += gv[i].z; run[3] += gv[i].w;
-        if (r0 + i == cv - 1) {
-          glr[0] = run[0]; glr[1] = run[1]; glr[2] = run[2]; glr[3] = run[3];
-        }
-      }
-      *reinterpret_cast<float4*>(sHalf + warp * 128 + ch) = make_float4(run[0], run[1], run[2], run[3]);
-    }
+    // ---- 1. sums of g over each half tile (computed during the previous chunk, except for the first) ----
+    if (it == 0) gsum_item(item, 0);
+    const float* sHalf = sHalfB + (it & 1) * 1024;
     if (tid == 0) bulk_wait_read_all();  // the previous chunk's record copies have read the staging tiles
     __syncthreads();
     float Gb[4][4];  // Gb[pp][j]: G at the end of tile pp - 1 (0 for pp = 0)
@@ -226,9 +238,11 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
         off[j] = hh ? hv0[j] : 0.f;
       }
     }
-    if (r0 <= cv - 1 && cv - 1 < r0 + 8)
-      *reinterpret_cast<float4*>(sGlast + ch) = make_float4(Gbp[0] + off[0] + glr[0], Gbp[1] + off[1] + glr[1],
-                                                            Gbp[2] + off[2] + glr[2], Gbp[3] + off[3] + glr[3]);
+    if (r0 <= cv - 1 && cv - 1 < r0 + 8) {
+      const float4 gl = *reinterpret_cast<const float4*>(sGlrB + (it & 1) * 128 + ch);
+      *reinterpret_cast<float4*>(sGlast + ch) = make_float4(Gbp[0] + off[0] + gl.x, Gbp[1] + off[1] + gl.y,
+                                                            Gbp[2] + off[2] + gl.z, Gbp[3] + off[3] + gl.w);
+    }
     __syncthreads();
     f32x2 eGbp2[2];
     #pragma unroll
@@ -559,6 +573,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
       }
       umma::commit(&bars[2]);
     }
+    if (item + (int)gridDim.x < nitems) gsum_item(item + (int)gridDim.x, (it + 1) & 1);
     mbar_wait_bounded(&bars[2], par);
     umma::fence_after_sync();
 
