@@ -39,8 +39,6 @@ def init_process_group(backend: str, timeout_s: float = 60.0, device=None):
 
         opts = ProcessGroupNCCL.Options()
         opts.config.blocking = 0
-        # collectives on a high-priority stream: their kernels take SMs ahead of the compute they overlap
-        opts.is_high_priority_stream = True
         kw["pg_options"] = opts
         if device is not None:
             kw["device_id"] = device

@@ -66,17 +66,16 @@ class ShardedGatedDeltaNet2:
     built from `shard_weights`; `forward_train` / `forward` return the full
     output after the all-reduce (sum) of the row-parallel o_proj partials.
 
-    `forward_train` in chunk mode overlaps that all-reduce with the rest of
-    the layer: it runs over `overlap_segments` consecutive token ranges
-    (whole chunks): each range's projections (the short-conv caches carried
-    from the previous range), its chunk core (the state carried: the same
-    recurrence as one call) and its o_proj GEMM, then that range's
-    all-reduce on a high-priority side stream while the next range computes.
-    The chunk kernels fill every SM for their duration, so `reserve_sms` SMs
-    are left to the collective meanwhile (gdn2_set_reserved_sms).  Only the
-    last range's all-reduce is exposed.  Under GVA in the reference's repeat
-    layout (which mixes tokens across the whole sequence) the projections run
-    once over the whole sequence instead.
+    `forward_train` in chunk mode overlaps that all-reduce with the
+    recurrence: after the projections of the whole sequence, the chunk core
+    runs over `overlap_segments` consecutive token ranges (whole chunks, the
+    state carried from one to the next, which is the same recurrence as one
+    call), and as each range completes, its o_proj GEMM and its all-reduce
+    run on a side stream while the core walks the next range.  Only the last
+    range's o_proj and all-reduce are exposed.  `reserve_sms` > 0 leaves that
+    many SMs to the side stream while the core runs (gdn2_set_reserved_sms);
+    with 2 and 4 B200s it made no measurable difference, so it is 0 by
+    default.
 
     Every all-reduce is bracketed by CUDA events on the stream it runs on and
     nothing waits on them here, so a timed loop of layer calls never stalls
@@ -86,7 +85,7 @@ class ShardedGatedDeltaNet2:
     """
 
     def __init__(self, cfg, weights: dict, group=None, device="cuda", dtype=None, overlap_segments: int = 4,
-                 reserve_sms: int = 16, **kw):
+                 reserve_sms: int = 0, **kw):
         import torch
         import torch.distributed as dist
 
@@ -116,7 +115,7 @@ class ShardedGatedDeltaNet2:
 
     def _forward_train_overlapped(self, x):
         """Chunk-mode forward_train with the o_proj all-reduce overlapped
-        with the rest of the layer (see the class docstring)."""
+        with the recurrence (see the class docstring)."""
         import dataclasses as dc
 
         import torch
@@ -129,33 +128,28 @@ class ShardedGatedDeltaNet2:
         h, hk, hv, vh = m._dims
         nch = (T + C - 1) // C
         seg = -(-nch // self.overlap_segments) * C  # tokens per range, whole chunks
-        per_range = not (hv > h and m.gva_mode == "reference")
-        p_all = None if per_range else m.project(x, None)[0]
+        p, _ = m.project(x, None)
         state = torch.zeros(B, hv, hk, vh, dtype=torch.float32, device=x.device)
         y = torch.empty(B, T, D, dtype=x.dtype, device=x.device)
         main = torch.cuda.current_stream(x.device)
         if self._side is None:
-            self._side = torch.cuda.Stream(device=x.device, priority=-1)
+            self._side = torch.cuda.Stream(device=x.device)
         side = self._side
-        side.wait_stream(main)  # y exists before the side stream writes it
+        side.wait_stream(main)  # y and the weights exist before the side stream writes or reads them
         evs = []
-        cache = None
-        prev = LIB.gdn2_set_reserved_sms(self.reserve_sms)
+        prev = LIB.gdn2_set_reserved_sms(self.reserve_sms) if self.reserve_sms else None
         try:
             for t0 in range(0, T, seg):
                 t1 = min(T, t0 + seg)
-                if per_range:
-                    ps, cache = m.project(x[:, t0:t1], cache)
-                else:
-                    ps = dc.replace(p_all, q=p_all.q[:, :, t0:t1], k=p_all.k[:, :, t0:t1], v=p_all.v[:, :, t0:t1],
-                                    g=p_all.g[:, :, t0:t1], b=p_all.b[:, :, t0:t1], w=p_all.w[:, :, t0:t1],
-                                    gate=p_all.gate[:, t0:t1])
-                part = m._out_proj(m._chunk_core(ps, state))  # [B, t1 - t0, D], contiguous
+                ps = dc.replace(p, q=p.q[:, :, t0:t1], k=p.k[:, :, t0:t1], v=p.v[:, :, t0:t1], g=p.g[:, :, t0:t1],
+                                b=p.b[:, :, t0:t1], w=p.w[:, :, t0:t1], gate=p.gate[:, t0:t1])
+                normed = m._chunk_core(ps, state)
                 done = torch.cuda.Event()
                 done.record(main)
                 with torch.cuda.stream(side):
                     side.wait_event(done)
-                    part.record_stream(side)
+                    normed.record_stream(side)
+                    part = m._out_proj(normed)  # [B, t1 - t0, D], contiguous
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record(side)
                     self.dist.all_reduce(part, op=self.dist.ReduceOp.SUM, group=self.group)
@@ -163,7 +157,8 @@ class ShardedGatedDeltaNet2:
                     evs.append((e0, e1))
                     y[:, t0:t1].copy_(part)
         finally:
-            LIB.gdn2_set_reserved_sms(prev)
+            if prev is not None:
+                LIB.gdn2_set_reserved_sms(prev)
         main.wait_stream(side)
         self._events.append(evs)
         return y
