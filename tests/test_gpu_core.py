@@ -277,15 +277,28 @@ def test_chunk_split_path_one_and_two_ctas_per_chain(dtype):
     assert bg._lib.read_device_errors() == 0
 
 
-@pytest.mark.parametrize("shape", [(1, 3, 1600, 128, 128), (1, 1, 2048, 128, 256)])
+@pytest.mark.parametrize("reserve", [0, 64])
+@pytest.mark.parametrize("shape", [(1, 3, 1600, 128, 128), (1, 1, 2048, 128, 256), (2, 12, 2048, 128, 128)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_chunk_state_scan_segments(shape, dtype):
+def test_chunk_state_scan_segments(shape, dtype, reserve):
     """Few long chains: the split-operand inter kernel cuts each chain into
     segments (3 of 9, 9 and 7 chunks for 3 chains at V = 128; 4 of 8 at
-    V = 256), computes every segment's end state from zero and its state
-    transition in parallel, chains the start states, then runs the segments
-    in parallel.  With the fused gated RMS norm and a random initial state,
-    vs the f64 oracle: gated output elementwise, final state."""
+    V = 256; 3 for 24 chains), computes every segment's end state from zero
+    and its state transition in parallel, chains the start states, then runs
+    the segments in parallel.  With the fused gated RMS norm and a random
+    initial state, vs the f64 oracle: gated output elementwise, final state;
+    also with 64 SMs reserved (gdn2_set_reserved_sms: a smaller intra grid,
+    and for the 24 chains no scan but 64-column cluster pairs)."""
+    import burn_gdn2 as bg
+
+    prev = bg.LIB.gdn2_set_reserved_sms(reserve)
+    try:
+        _scan_case(shape, dtype)
+    finally:
+        bg.LIB.gdn2_set_reserved_sms(prev)
+
+
+def _scan_case(shape, dtype):
     import burn_gdn2 as bg
 
     B, HV, T, K, V = shape
