@@ -496,7 +496,7 @@ def overlap_fields(ms, ar_ms, local_ms, segments):
 def sharded_parity(torch, bg, sharding, dev, world):
     """ShardedGatedDeltaNet2 (NCCL all-reduce, overlapped forward_train) vs the unsharded layer on rank 0, both
     on the CUDA path: a bf16 layer of 8 x 128 heads, hidden 1024, B = 2, T = 320 (five chunks over the ranges),
-    judged by the whole-layer criterion of the tests (relative Frobenius error <= 1e-2, max |d| <= 2.5e-2 of the
+    checked by the whole-layer criterion of the tests (relative Frobenius error <= 1e-2, max |d| <= 2.5e-2 of the
     reference's max magnitude: the ranks' o_proj partials are bf16 before their sum)."""
     import torch.distributed as dist
     cfg = bg.Gdn2Config(hidden_size=1024, num_heads=8, head_dim=128, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
