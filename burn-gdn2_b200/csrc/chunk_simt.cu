@@ -502,7 +502,12 @@ static int launch_inter_vt(const ChunkParams& p, cudaStream_t st) {
 // so the grid must fit in one wave: 64-column slices (256 CTAs for 128
 // chains of V = 128, two per SM) beat 32-column ones (512 CTAs, more than
 // the 444 that fit) and read each chain's W / Qg / Kd / Aqk half as often.
+// With few chains the narrowest slices that still fit two per SM cut the
+// per-chunk work on each chain's critical path instead.
 int launch_inter_simt(const ChunkParams& p, cudaStream_t st) {
+  const long long chains = (long long)p.B * p.HV, fit = 2LL * usable_sms();
+  if (p.V % 16 == 0 && chains * (p.V / 16) <= fit) return launch_inter_vt<16>(p, st);
+  if (p.V % 32 == 0 && chains * (p.V / 32) <= fit) return launch_inter_vt<32>(p, st);
   if (p.V <= 16) return launch_inter_vt<16>(p, st);
   if (p.V <= 64 && p.V % 32 != 0) return launch_inter_vt<16>(p, st);
   if (p.V % 64 == 0) return launch_inter_vt<64>(p, st);
