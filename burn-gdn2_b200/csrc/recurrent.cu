@@ -423,12 +423,16 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const RecParams p) {
   if ((int)blockIdx.x >= n_items) return;
 
   // async copy of this lane's part of step (item, sub) into buffer b
+  const uint64_t pol_st = l2_policy_evict_first();  // the state lines: read and written once per step
   auto issue = [&](int item, int sub, int b) {
     const int bb = item / p.Hq, kh = item % p.Hq;
     const int hv = kh * p.rep + sub / vsplit, vs = sub % vsplit;
     const float* src = p.state + ((int64_t)bb * p.HV + hv) * (int64_t)K * V + vs * DEC_VT + wc;
     float* dst = wbuf + b * K * 16 + cg * 4;
-    for (int kk = rg; kk < K; kk += 8) cp_async16(dst + kk * 16, src + (int64_t)kk * V);
+    for (int kk = rg; kk < K; kk += 8)  // read once per step: evict-first
+      asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + kk * 16)),
+                   "l"(src + (int64_t)kk * V), "l"(pol_st)
+                   : "memory");
     cp_async_commit();
   };
 
@@ -570,7 +574,11 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const RecParams p) {
           s.y = e * s.y + kq * vn.y;
           s.z = e * s.z + kq * vn.z;
           s.w = e * s.w + kq * vn.w;
-          *reinterpret_cast<float4*>(dst + (int64_t)kk * V) = s;
+          // written once per step and read again only by the next step, long after: evict-first
+          asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(
+                           dst + (int64_t)kk * V),
+                       "f"(s.x), "f"(s.y), "f"(s.z), "f"(s.w), "l"(pol_st)
+                       : "memory");
         }
         buf ^= 1;
       }
