@@ -390,6 +390,9 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     // ---- 3. scores back from TMEM (warp w: sub-partition w % 4, row tiles 2 (w / 4) .. +1), then T ----
     mbar_wait_bounded(&bars[1], par);  // both passes (the second commit covers every earlier MMA)
     umma::fence_after_sync();
+    // the slot's score images were read back (the second pass's MMAs, issued after that copy, are done):
+    // dropped from L2 instead of written back to HBM
+    for (int l = tid; l < (int)(X3_SLOT_PASSB / 128); l += 256) discard_l2_line(slot + (size_t)l * 128);
     float* sAkk = reinterpret_cast<float*>(sm + AKK);
     float* sTinv = reinterpret_cast<float*>(sm + TINV);
     {
@@ -576,6 +579,9 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     if (item + (int)gridDim.x < nitems) gsum_item(item + (int)gridDim.x, (it + 1) & 1);
     mbar_wait_bounded(&bars[2], par);
     umma::fence_after_sync();
+    // the slot's rhs images were read back (the W / U MMAs are done): dropped from L2 likewise (the second rhs_v
+    // half of V = 256 is read back later and stays)
+    for (int l = tid; l < 65536 / 128; l += 256) discard_l2_line(slot + X3_SLOT_PASSB + (size_t)l * 128);
 
     // ---- 5. W (hi / lo images) and U (f32, one 128-column slice at a time) staged in shared memory (warp w:
     // sub-partition w % 4, column half w / 4), then bulk copies into the record (they drain while the next

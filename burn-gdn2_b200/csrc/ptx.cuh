@@ -164,6 +164,11 @@ __device__ __forceinline__ void bulk_s2g_hint(void* gdst, const void* ssrc, unsi
                "r"(smem_u32(ssrc)), "r"(bytes), "l"(pol)
                : "memory");
 }
+// Drop the 128-byte L2 line at `p` (128-byte aligned) without writing it back: for scratch whose contents are
+// dead (read back already, rewritten before the next read).
+__device__ __forceinline__ void discard_l2_line(const void* p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
 // L2 eviction policies for the .L2::cache_hint forms.  Lines that are written or read once and not touched
 // again soon (the chunk records, inputs read by one CTA) are marked evict-first, so that L2 keeps the lines
 // that are re-read soon (rows prefetched for the next chunk, per-CTA scratch).
