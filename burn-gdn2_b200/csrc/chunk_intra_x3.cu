@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
     mbar_wait_bounded(&bars[2], par);
     umma::fence_after_sync();
     // the slot's rhs images were read back (the W / U MMAs are done): dropped from L2 likewise (the second rhs_v
-    // half of V = 256 is read back later and stays)
+    // half of V = 256 is read back later, and dropped then)
     for (int l = tid; l < 65536 / 128; l += 256) discard_l2_line(slot + X3_SLOT_PASSB + (size_t)l * 128);
 
     // ---- 5. W (hi / lo images) and U (f32, one 128-column slice at a time) staged in shared memory (warp w:
@@ -660,6 +660,8 @@ __global__ void __launch_bounds__(256, 2) k_intra_x3(const TcParams p, int nitem
       }
       mbar_wait_bounded(&bars[6], par);
       umma::fence_after_sync();
+      // the second rhs_v half was read back (its U MMA is done): dropped from L2 like the rest of the slot
+      for (int l = tid; l < 32768 / 128; l += 256) discard_l2_line(slot + X3_SLOT_PASSB + 65536 + (size_t)l * 128);
       stage_u(rec + L.u + 64 * 128 * 4);
     }
     umma::fence_after_sync();
