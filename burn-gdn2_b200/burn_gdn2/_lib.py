@@ -58,6 +58,15 @@ class RecurrentArgs(ctypes.Structure):
                 ("gate", View), ("o_norm_weight", ctypes.c_void_p), ("state", ctypes.c_void_p), ("out", View)]
 
 
+class RecurrentBwdArgs(ctypes.Structure):
+    _fields_ = [("dims", Dims), ("dtype", ctypes.c_int32), ("key_heads_grouped", ctypes.c_int32),
+                ("scale", ctypes.c_float),
+                ("q", View), ("k", View), ("v", View), ("g", View), ("b", View), ("w", View),
+                ("state_in", ctypes.c_void_p), ("d_out", View), ("d_state_out", ctypes.c_void_p),
+                ("dq", View), ("dk", View), ("dv", View), ("dg", View), ("db", View), ("dw", View),
+                ("d_state_in", ctypes.c_void_p)]
+
+
 class PrologueArgs(ctypes.Structure):
     _fields_ = [("dims", Dims), ("dtype", ctypes.c_int32), ("use_short_conv", ctypes.c_int32),
                 ("allow_neg_eigval", ctypes.c_int32), ("min_decay", ctypes.c_float),
@@ -86,7 +95,7 @@ EXPORTS = (
     "gdn2_recurrent_fwd", "gdn2_short_conv", "gdn2_rms_norm_gate", "gdn2_config_validate",
     "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
     "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc", "gdn2_project_activations", "gdn2_selftest_wait",
-    "gdn2_set_reserved_sms",
+    "gdn2_set_reserved_sms", "gdn2_recurrent_bwd_workspace_bytes", "gdn2_recurrent_bwd",
 )
 
 
@@ -107,6 +116,10 @@ def _load():
     lib.gdn2_chunk_fwd_noalloc.restype = ctypes.c_int
     lib.gdn2_recurrent_fwd.argtypes = [P(RecurrentArgs), vp]
     lib.gdn2_recurrent_fwd.restype = ctypes.c_int
+    lib.gdn2_recurrent_bwd_workspace_bytes.argtypes = [P(Dims)]
+    lib.gdn2_recurrent_bwd_workspace_bytes.restype = sz
+    lib.gdn2_recurrent_bwd.argtypes = [P(RecurrentBwdArgs), vp, sz, vp]
+    lib.gdn2_recurrent_bwd.restype = ctypes.c_int
     lib.gdn2_short_conv.argtypes = [i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     lib.gdn2_short_conv.restype = ctypes.c_int
     lib.gdn2_rms_norm_gate.argtypes = [P(Dims), i32, View, View, vp, f32, View, vp]

@@ -176,6 +176,82 @@ def fused_recurrent_forward(q, k, v, g, b, w, state, scale) -> Tuple[torch.Tenso
     return out, st
 
 
+def recurrent_backward(q, k, v, g, b, w, state, scale, d_out, d_state=None, *, num_heads=None):
+    """Backward of the core recurrence (gdn2_recurrent_bwd, exact f32).
+
+    q,k,g,b: [B,Hq,T,K] with Hq = HV, or Hq = num_heads key heads shared by
+    groups of HV / Hq value heads; v,w,d_out: [B,HV,T,V]; state: [B,HV,K,V]
+    initial state or None (zeros); d_state: dL/d(final state) or None.
+    Returns (dq, dk, dv, dg, db, dw, d_state_in), f32, the key-side ones
+    summed over each group back to [B,Hq,T,K].
+    """
+    _require_cuda(q, k, v, g, b, w, d_out)
+    dt = q.dtype if q.dtype in _DT else torch.float32
+    B, Hq, T, K = q.shape
+    HV, V = v.shape[1], v.shape[3]
+    grouped = Hq != HV
+    if grouped and HV % Hq:
+        raise ValueError(f"value heads {HV} not a multiple of key heads {Hq}")
+    q, k, v, w, d_out = (_last_contig(x, dt) for x in (q, k, v, w, d_out))
+    b = _last_contig(_expand_k(b, K), dt)
+    g = _last_contig(_expand_k(g, K), torch.float32)
+    st = None if state is None else state.to(torch.float32).contiguous()
+    dst = None if d_state is None else d_state.to(torch.float32).contiguous()
+    f32 = dict(dtype=torch.float32, device=q.device)
+    dq, dk, dg, db = (torch.empty(B, HV, T, K, **f32) for _ in range(4))
+    dv, dw = (torch.empty(B, HV, T, V, **f32) for _ in range(2))
+    dh0 = torch.empty(B, HV, K, V, **f32)
+    a = _lib.RecurrentBwdArgs()
+    a.dims = _lib.Dims(B, T, Hq if grouped else HV, HV, K, V)
+    a.dtype = dtype_code(dt)
+    a.key_heads_grouped = int(grouped)
+    a.scale = float(scale)
+    a.q, a.k, a.v, a.g, a.b, a.w = (view4(x) for x in (q, k, v, g, b, w))
+    a.state_in = None if st is None else st.data_ptr()
+    a.d_out = view4(d_out)
+    a.d_state_out = None if dst is None else dst.data_ptr()
+    a.dq, a.dk, a.dv, a.dg, a.db, a.dw = (view4(x) for x in (dq, dk, dv, dg, db, dw))
+    a.d_state_in = dh0.data_ptr()
+    nbytes = LIB.gdn2_recurrent_bwd_workspace_bytes(ctypes.byref(a.dims))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
+    check(LIB.gdn2_recurrent_bwd(ctypes.byref(a), ptr(ws), ws.numel(), stream_handle(q.device)))
+    if grouped:
+        dq, dk, dg, db = (x.view(B, Hq, HV // Hq, T, K).sum(2) for x in (dq, dk, dg, db))
+    return dq, dk, dv, dg, db, dw, dh0
+
+
+class GatedDeltaCore(torch.autograd.Function):
+    """Differentiable core: forward on the chunked kernels (1) + (2), f32-grade
+    (or the recurrent kernel (3) for T <= 64), backward on gdn2_recurrent_bwd.
+
+    apply(q, k, v, g, b, w, state, scale, chunk_size) -> (out [B,HV,T,V], new state f32).
+    q,k,g,b: [B,HV,T,K] (g, b last dim K); gradients flow to q, k, v, g, b, w
+    and the initial state; the new state's gradient is taken into account.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, b, w, state, scale, chunk_size):
+        s0 = state if state is not None else torch.zeros(q.shape[0], v.shape[1], q.shape[3], v.shape[3],
+                                                          dtype=torch.float32, device=q.device)
+        if q.shape[2] <= 64:
+            out, st = fused_recurrent_forward(q, k, v, g, b, w, s0, scale)
+        else:
+            out, st = chunk_wy_forward(q, k, v, g, b, w, s0, scale, chunk_size)
+        ctx.save_for_backward(q, k, v, g, b, w, state)
+        ctx.scale = scale
+        return out, st
+
+    @staticmethod
+    def backward(ctx, d_out, d_state):
+        q, k, v, g, b, w, state = ctx.saved_tensors
+        if d_out is None:
+            d_out = torch.zeros(v.shape, dtype=v.dtype, device=v.device)
+        dq, dk, dv, dg, db, dw, dh0 = recurrent_backward(q, k, v, g, b, w, state, ctx.scale, d_out, d_state)
+        cast = lambda gr, x: gr.to(x.dtype)
+        return (cast(dq, q), cast(dk, k), cast(dv, v), cast(dg, g), cast(db, b), cast(dw, w),
+                None if state is None else cast(dh0, state), None, None)
+
+
 def fused_recurrent_gdn2(q, k, v, g, b, w, state: Optional[torch.Tensor], scale, update_state: bool):
     """Dispatcher of src/kernel/fused_recurrent.rs:65-108.
 

@@ -33,6 +33,8 @@ int check_cuda(cudaError_t e, const char* where) {
 }
 
 int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream);
+int launch_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
+size_t recurrent_bwd_workspace_bytes(const gdn2_dims& d);
 unsigned read_device_errors_recurrent();
 unsigned read_device_errors_selftest();
 unsigned read_device_errors_intra_tc();
@@ -360,6 +362,13 @@ int gdn2_selftest_wait(uint32_t spins, int32_t arrive, int32_t* completed) {
 int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, void* stream) {
   if (!a) return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: null args");
   return launch_recurrent(a, (cudaStream_t)stream);
+}
+
+size_t gdn2_recurrent_bwd_workspace_bytes(const gdn2_dims* d) { return d ? recurrent_bwd_workspace_bytes(*d) : 0; }
+
+int gdn2_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!a) return set_error(GDN2_EINVAL, "gdn2_recurrent_bwd: null args");
+  return launch_recurrent_bwd(a, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 int gdn2_project_activations(const gdn2_prologue_args* a, void* stream) {

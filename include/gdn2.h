@@ -215,6 +215,43 @@ typedef struct gdn2_recurrent_args {
 GDN2_API int gdn2_recurrent_fwd(const gdn2_recurrent_args* args, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Backward of the core recurrence (exact f32): the reverse-mode adjoint of
+ * the per-token scan src/kernel/fused_recurrent.rs:11-56, which is what the
+ * crate's burn autodiff differentiates through its tensor path
+ * (src/forward.rs:44-278); the crate's own adjoint kernel sketch
+ * src/kernel/chunk_adjoint_cube.rs:22-378 is unwired.  For
+ *
+ *   o_t = scale S_t^T q_t,   S_t = e^{g_t} S_{t-1} + k_t u_t^T,
+ *   u_t = w_t v_t - (b_t k_t)^T (e^{g_t} S_{t-1}),   S_0 = state_in
+ *
+ * given d_out = dL/do and d_state_out = dL/dS_T (NULL = 0), it writes
+ * dL/d{q, k, v, g, b, w} and d_state_in = dL/dS_0 (NULL = not written).
+ * Inputs as gdn2_recurrent_fwd with prologue = 0 (q, k, g, b are the final,
+ * activated values; g is the log decay, f32).  Outputs are f32 views;
+ * dq, dk, dg, db are [B, HV, T, K] per VALUE head: with key_heads_grouped =
+ * 1 the caller sums each group of HV / H value heads for its key head.
+ * K a multiple of 32 up to 128, V a multiple of 16 up to 256.  The
+ * workspace (gdn2_recurrent_bwd_workspace_bytes, 8-byte aligned) holds the
+ * state at every 8th token: B x HV x ceil(T / 8) x K x V floats.
+ * ---------------------------------------------------------------------- */
+typedef struct gdn2_recurrent_bwd_args {
+  gdn2_dims dims;
+  int32_t dtype; /* of q, k, v, b, w and d_out */
+  int32_t key_heads_grouped;
+  float scale;
+  gdn2_view q, k, v, g, b, w;
+  const float* state_in;    /* [B,HV,K,V] f32 or NULL (zeros) */
+  gdn2_view d_out;          /* [B,HV,T,V] */
+  const float* d_state_out; /* [B,HV,K,V] f32 or NULL (zeros) */
+  gdn2_view dq, dk, dv, dg, db, dw;
+  float* d_state_in; /* [B,HV,K,V] f32 or NULL */
+} gdn2_recurrent_bwd_args;
+
+GDN2_API size_t gdn2_recurrent_bwd_workspace_bytes(const gdn2_dims* dims);
+GDN2_API int gdn2_recurrent_bwd(const gdn2_recurrent_bwd_args* args, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
+/* ------------------------------------------------------------------------
  * Projection activations: everything elementwise in GatedDeltaNet2::project
  * (src/module.rs:381-498) between the caller's projection GEMMs and the
  * core, in one launch.  Replaces short_conv_1d (src/short_conv.rs:22-65),

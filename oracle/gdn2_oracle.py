@@ -117,6 +117,52 @@ def fused_recurrent_forward(q, k, v, g, b, w, state, scale):
     return np.stack(outs, axis=2), S
 
 
+def fused_recurrent_backward(q, k, v, g, b, w, state, scale, d_out, d_state=None):
+    """Reverse-mode adjoint of fused_recurrent_forward (the recurrence of
+    src/kernel/fused_recurrent.rs:11-56, which the crate differentiates by
+    burn autodiff of src/forward.rs:44-278).  Stores every token's state,
+    then walks the tokens backwards.
+
+    Shapes as fused_recurrent_forward with g, b of last dim K; d_out
+    [B,H,T,V]; d_state dL/d(final state) or None.  Returns
+    (dq, dk, dv, dg, db, dw, d_state_in).
+    """
+    T = q.shape[2]
+    S = state.copy()
+    gam = np.exp(g)
+    pre = []  # the incoming state of every token
+    us = []
+    for t in range(T):
+        pre.append(S)
+        Sa = S * gam[:, :, t, :, None]
+        bk = b[:, :, t] * k[:, :, t]
+        u = w[:, :, t] * v[:, :, t] - (Sa * bk[..., None]).sum(axis=2)
+        S = Sa + k[:, :, t, :, None] * u[:, :, None, :]
+        us.append(u)
+    dS = np.zeros_like(S) if d_state is None else d_state.astype(S.dtype).copy()
+    dq, dk, dg, db = (np.zeros_like(q) for _ in range(4))
+    dv, dw = np.zeros_like(v), np.zeros_like(w)
+    for t in range(T - 1, -1, -1):
+        gt = gam[:, :, t, :, None]
+        kt, qt, bt = k[:, :, t], q[:, :, t], b[:, :, t]
+        Sa = pre[t] * gt
+        St = Sa + kt[..., None] * us[t][:, :, None, :]
+        dO = d_out[:, :, t]
+        dS = dS + scale * qt[..., None] * dO[:, :, None, :]  # o_t = scale S_t^T q_t
+        dq[:, :, t] = scale * (St * dO[:, :, None, :]).sum(axis=3)
+        du = (dS * kt[..., None]).sum(axis=2)  # S_t = Sa + k u^T
+        dk[:, :, t] = (dS * us[t][:, :, None, :]).sum(axis=3)
+        dv[:, :, t] = du * w[:, :, t]  # u = w v - e
+        dw[:, :, t] = du * v[:, :, t]
+        dSa = dS - (bt * kt)[..., None] * du[:, :, None, :]  # e = Sa^T (b k), de = -du
+        dbk = -(Sa * du[:, :, None, :]).sum(axis=3)
+        dk[:, :, t] += dbk * bt
+        db[:, :, t] = dbk * kt
+        dg[:, :, t] = (dSa * Sa).sum(axis=3)  # Sa = e^g S_{t-1}
+        dS = dSa * gt
+    return dq, dk, dv, dg, db, dw, dS
+
+
 # --------------------------------------------------------------------------
 # src/forward.rs:44-278
 # --------------------------------------------------------------------------

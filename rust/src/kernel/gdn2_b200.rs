@@ -104,6 +104,33 @@ pub struct Gdn2RecurrentArgs {
     pub out: Gdn2View,
 }
 
+/// Backward of the core recurrence (`gdn2_recurrent_bwd`): dq, dk, dg, db are
+/// per value head; with `key_heads_grouped` the caller sums each group.
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct Gdn2RecurrentBwdArgs {
+    pub dims: Gdn2Dims,
+    pub dtype: i32,
+    pub key_heads_grouped: i32,
+    pub scale: f32,
+    pub q: Gdn2View,
+    pub k: Gdn2View,
+    pub v: Gdn2View,
+    pub g: Gdn2View,
+    pub b: Gdn2View,
+    pub w: Gdn2View,
+    pub state_in: *const f32,
+    pub d_out: Gdn2View,
+    pub d_state_out: *const f32,
+    pub dq: Gdn2View,
+    pub dk: Gdn2View,
+    pub dv: Gdn2View,
+    pub dg: Gdn2View,
+    pub db: Gdn2View,
+    pub dw: Gdn2View,
+    pub d_state_in: *mut f32,
+}
+
 #[repr(C)]
 #[derive(Clone, Copy, Debug)]
 pub struct Gdn2PrologueArgs {
@@ -170,6 +197,9 @@ extern "C" {
         -> i32;
     pub fn gdn2_chunk_fwd_noalloc(args: *const Gdn2ChunkArgs, stream: *mut c_void) -> i32;
     pub fn gdn2_recurrent_fwd(args: *const Gdn2RecurrentArgs, stream: *mut c_void) -> i32;
+    pub fn gdn2_recurrent_bwd_workspace_bytes(dims: *const Gdn2Dims) -> usize;
+    pub fn gdn2_recurrent_bwd(args: *const Gdn2RecurrentBwdArgs, workspace: *mut c_void, workspace_bytes: usize,
+                              stream: *mut c_void) -> i32;
     pub fn gdn2_project_activations(args: *const Gdn2PrologueArgs, stream: *mut c_void) -> i32;
     pub fn gdn2_short_conv(batch: i32, seq_len: i32, channels: i32, dtype: i32, x: *const c_void,
                            weight: *const f32, cache_in: *const f32, cache_out: *mut f32, y: *mut c_void,

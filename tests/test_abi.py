@@ -39,8 +39,12 @@ def test_struct_layout_matches_header():
 #include "gdn2.h"
 #define P(T, F) printf(#T "." #F " %zu\n", offsetof(T, F));
 int main() {
-  printf("view %zu\ndims %zu\nchunk %zu\nrec %zu\ncfg %zu\npro %zu\n", sizeof(gdn2_view), sizeof(gdn2_dims),
-         sizeof(gdn2_chunk_args), sizeof(gdn2_recurrent_args), sizeof(gdn2_config), sizeof(gdn2_prologue_args));
+  printf("view %zu\ndims %zu\nchunk %zu\nrec %zu\ncfg %zu\npro %zu\nbwd %zu\n", sizeof(gdn2_view),
+         sizeof(gdn2_dims), sizeof(gdn2_chunk_args), sizeof(gdn2_recurrent_args), sizeof(gdn2_config),
+         sizeof(gdn2_prologue_args), sizeof(gdn2_recurrent_bwd_args));
+  P(gdn2_recurrent_bwd_args, scale) P(gdn2_recurrent_bwd_args, q) P(gdn2_recurrent_bwd_args, state_in)
+  P(gdn2_recurrent_bwd_args, d_out) P(gdn2_recurrent_bwd_args, d_state_out) P(gdn2_recurrent_bwd_args, dq)
+  P(gdn2_recurrent_bwd_args, dw) P(gdn2_recurrent_bwd_args, d_state_in)
   P(gdn2_prologue_args, min_decay) P(gdn2_prologue_args, q_raw) P(gdn2_prologue_args, ld_q)
   P(gdn2_prologue_args, ld_f) P(gdn2_prologue_args, conv_w_q) P(gdn2_prologue_args, conv_v_out)
   P(gdn2_prologue_args, a_log) P(gdn2_prologue_args, decay_factors) P(gdn2_prologue_args, q)
@@ -67,7 +71,9 @@ int main() {
     assert got["rec"] == ctypes.sizeof(_lib.RecurrentArgs)
     assert got["cfg"] == ctypes.sizeof(_lib.Config)
     assert got["pro"] == ctypes.sizeof(_lib.PrologueArgs)
+    assert got["bwd"] == ctypes.sizeof(_lib.RecurrentBwdArgs)
     names = {"gdn2_chunk_args": _lib.ChunkArgs, "gdn2_recurrent_args": _lib.RecurrentArgs,
+             "gdn2_recurrent_bwd_args": _lib.RecurrentBwdArgs,
              "gdn2_config": _lib.Config, "gdn2_prologue_args": _lib.PrologueArgs}
     for key, off in got.items():
         if "." in key:
@@ -231,3 +237,30 @@ def test_set_reserved_sms_clamps_and_returns_previous():
         assert lib.gdn2_set_reserved_sms(0) == 64
     finally:
         lib.gdn2_set_reserved_sms(prev)
+
+
+def test_recurrent_bwd_argument_errors():
+    from burn_gdn2 import LIB, _lib
+
+    a = _lib.RecurrentBwdArgs()
+    a.dims = _lib.Dims(1, 20, 1, 1, 128, 128)
+    assert LIB.gdn2_recurrent_bwd(None, None, 0, None) == _lib.GDN2_EINVAL
+    assert LIB.gdn2_recurrent_bwd(ctypes.byref(a), None, 0, None) == _lib.GDN2_EINVAL  # null tensors
+    # workspace: the state at every 8th token, ceil(20 / 8) = 3 of them
+    assert LIB.gdn2_recurrent_bwd_workspace_bytes(ctypes.byref(a.dims)) == 3 * 128 * 128 * 4
+    bad = _lib.Dims(1, 20, 1, -1, 128, 128)
+    assert LIB.gdn2_recurrent_bwd_workspace_bytes(ctypes.byref(bad)) == 0
+    fake = 1 << 20  # never dereferenced: validation fails first
+    for n in ("q", "k", "v", "g", "b", "w", "d_out", "dq", "dk", "dv", "dg", "db", "dw"):
+        setattr(a, n, _lib.View(fake, 0, 0, 0))
+    assert LIB.gdn2_recurrent_bwd(ctypes.byref(a), None, 0, None) == _lib.GDN2_EWORKSPACE
+    assert LIB.gdn2_recurrent_bwd(ctypes.byref(a), ctypes.c_void_p(fake), 1024, None) == _lib.GDN2_EWORKSPACE
+    for dims in [(1, 20, 1, 1, 100, 128), (1, 20, 1, 1, 256, 128), (1, 20, 1, 1, 128, 24), (1, 20, 1, 1, 128, 512)]:
+        a.dims = _lib.Dims(*dims)
+        assert LIB.gdn2_recurrent_bwd(ctypes.byref(a), ctypes.c_void_p(fake), 1 << 30, None) == \
+            _lib.GDN2_EUNSUPPORTED, dims
+    a.dims = _lib.Dims(1, 20, 2, 3, 128, 128)
+    assert LIB.gdn2_recurrent_bwd(ctypes.byref(a), ctypes.c_void_p(fake), 1 << 30, None) == _lib.GDN2_EINVAL
+    a.dims = _lib.Dims(1, 20, 1, 1, 128, 128)
+    a.dtype = 5
+    assert LIB.gdn2_recurrent_bwd(ctypes.byref(a), ctypes.c_void_p(fake), 1 << 30, None) == _lib.GDN2_EINVAL

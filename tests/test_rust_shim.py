@@ -15,7 +15,7 @@ HEADER = os.path.join(ROOT, "include", "gdn2.h")
 RUST = os.path.join(ROOT, "rust", "src", "kernel", "gdn2_b200.rs")
 NAMES = {"Gdn2View": "gdn2_view", "Gdn2Dims": "gdn2_dims", "Gdn2ChunkArgs": "gdn2_chunk_args",
          "Gdn2RecurrentArgs": "gdn2_recurrent_args", "Gdn2PrologueArgs": "gdn2_prologue_args",
-         "Gdn2Config": "gdn2_config"}
+         "Gdn2Config": "gdn2_config", "Gdn2RecurrentBwdArgs": "gdn2_recurrent_bwd_args"}
 PRIM = {"i32": 4, "u32": 4, "f32": 4, "i64": 8, "u64": 8, "f64": 8, "usize": 8}
 
 
