@@ -21,19 +21,27 @@
 // columns of one (batch, value head) chain, a warp owns 2 of them, and lane
 // l owns key rows l, l+32, l+64, l+96, so the two K-reductions per token
 // on the critical path (e and du) are warp shuffles.  The V-reductions are
-// outputs only: each warp adds its per-row partials into a shared buffer
-// (red.shared) and, every 8 tokens, the CTAs of a chain, which form one
-// thread-block cluster, sum each other's buffers through distributed shared
-// memory and write dq, dk, db, dg once.
+// outputs only: each warp stores its per-row partials of a token in its own
+// shared slot (plain stores; float atomics on shared memory serialise the
+// warps), one barrier later every thread sums two of the 4K values over the
+// warps into the sub-chunk buffer, and, every 8 tokens, the CTAs of a chain,
+// which form one thread-block cluster, sum each other's buffers through
+// distributed shared memory and write dq, dk, db, dg once.
 //
 // States for the reverse pass.  A forward pass over the sequence stores the
 // state at every 8th token boundary in the workspace (each thread its own
-// 2 x RPL values, in a private layout that makes every warp store 256
-// contiguous bytes).  The reverse pass walks the 8-token sub-chunks from the
-// last: it reloads the sub-chunk's start state, replays the 8 tokens keeping
-// each token's incoming state in registers, then runs the adjoint over
-// them.  Work per token is three forward steps and one adjoint step on the
-// slice; the workspace is B x HV x ceil(T/8) x K x V floats.
+// 2 x RPL values, contiguous, so a warp stores one contiguous block).  The
+// reverse pass walks the 8-token sub-chunks from the last: it reloads the
+// sub-chunk's start state, replays the 8 tokens keeping each token's
+// incoming state in registers, then runs the adjoint over them.  Work per
+// token is three forward steps and one adjoint step on the slice; the
+// workspace is B x HV x ceil(T/8) x K x V floats.
+//
+// Inputs.  When every view is 16-byte aligned, the raw rows of the next
+// sub-chunk (and, in the reverse pass, the thread's next checkpoint) are
+// fetched by cp.async into a staging buffer while the current sub-chunk
+// computes; one pass then converts them into the packed layout.  Other
+// views are read synchronously.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -64,21 +72,83 @@ __device__ __forceinline__ float warp_sum_bwd(float x) {
   return x;
 }
 
-__device__ __forceinline__ void red_shared_add(float* p, float x) {
-  asm volatile("red.shared.add.f32 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(p)), "f"(x) : "memory");
-}
-
-// Shared memory (floats): staged inputs of one sub-chunk, the per-column
-// outputs dv / dw, and two V-reduction buffers (by sub-chunk parity).
+// Shared memory: staged inputs of one sub-chunk, packed so that one 128-bit
+// load gives a row's or a column's values for a token, the per-column
+// outputs dv / dw, two V-reduction buffers (by sub-chunk parity) and the
+// warps' per-token partial slots (by token parity).
 struct BwdSmem {
-  float *q, *k, *b, *gm;  // [L][K]  (gm = e^g)
-  float *v, *w, *dO;      // [L][VT]
-  float *dv, *dw;         // [L][VT]
-  float* red;             // [2][L][4][K]: dq, dk (through S_t), dbk, dg partials
+  float4* kr;    // [L][K]: (e^g, b, k, scale q) of key row kk
+  float4* vc;    // [L][VT]: (w v, dO, w, v) of value column c
+  float *dv, *dw;  // [L][VT]
+  float4* red;   // [2][L][K]: (dq, dk through S_t, dbk, dg) of the CTA's columns
+  float4* slot;  // [2][NW][K]: the same of one warp's columns, one token
+  // cp.async staging (aligned views only): raw q, k, b [L][K], g [L][K] f32, v, w, dO [L][VT]; checkpoints
+  unsigned char *rq, *rk, *rb, *rv, *rw, *rdo;
+  float* rg;
+  float* ck;     // [threads][2 RPL]
 };
 
-__host__ __device__ inline size_t bwd_smem_floats(int K, int VT) {
-  return (size_t)4 * BWD_L * K + (size_t)5 * BWD_L * VT + (size_t)2 * BWD_L * 4 * K;
+__host__ __device__ inline size_t bwd_smem_bytes(int K, int VT, int NW, int RPL, int esz) {
+  return 16 * ((size_t)BWD_L * K + (size_t)BWD_L * VT + (size_t)2 * BWD_L * K + (size_t)2 * NW * K) +
+         8 * (size_t)BWD_L * VT + (size_t)BWD_L * (3 * (size_t)K * esz + 4 * (size_t)K + 3 * (size_t)VT * esz) +
+         (size_t)NW * 32 * RPL * 8;
+}
+
+// cp.async of sub-chunk tokens t0 .. t0+cv-1 of every input into the staging buffer (one commit group)
+template <typename TIN>
+__device__ __forceinline__ void bwd_issue(const BwdParams& p, const BwdSmem& s, int bb, int hv, int kh, int col0,
+                                          int t0, int cv, bool with_dout) {
+  const int nth = blockDim.x, tid = threadIdx.x, K = p.K, VT = p.VT;
+  constexpr int ES = (int)sizeof(TIN);
+  const int cr = K * ES / 16, cg4 = K * 4 / 16, cvv = VT * ES / 16;  // 16-byte chunks per row
+  const int nk = cv * cr;
+  for (int i = tid; i < 3 * nk; i += nth) {
+    const int which = i / nk, rem = i - which * nk, tt = rem / cr, c = rem - tt * cr;
+    const DView& v = which == 0 ? p.q : which == 1 ? p.k : p.b;
+    unsigned char* dst = which == 0 ? s.rq : which == 1 ? s.rk : s.rb;
+    const char* src = static_cast<const char*>(v.p) + ((int64_t)bb * v.s0 + (int64_t)kh * v.s1 + (int64_t)(t0 + tt) * v.s2) * ES;
+    cp_async16(dst + (tt * K) * ES + c * 16, src + c * 16);
+  }
+  for (int i = tid; i < cv * cg4; i += nth) {
+    const int tt = i / cg4, c = i - tt * cg4;
+    const char* src = static_cast<const char*>(p.g.p) +
+                      ((int64_t)bb * p.g.s0 + (int64_t)kh * p.g.s1 + (int64_t)(t0 + tt) * p.g.s2) * 4;
+    cp_async16(reinterpret_cast<unsigned char*>(s.rg) + tt * K * 4 + c * 16, src + c * 16);
+  }
+  const int nv = cv * cvv, nvt = with_dout ? 3 : 2;
+  for (int i = tid; i < nvt * nv; i += nth) {
+    const int which = i / nv, rem = i - which * nv, tt = rem / cvv, c = rem - tt * cvv;
+    const DView& v = which == 0 ? p.v : which == 1 ? p.w : p.dout;
+    unsigned char* dst = which == 0 ? s.rv : which == 1 ? s.rw : s.rdo;
+    const char* src = static_cast<const char*>(v.p) +
+                      ((int64_t)bb * v.s0 + (int64_t)hv * v.s1 + (int64_t)(t0 + tt) * v.s2 + col0) * ES;
+    cp_async16(dst + (tt * VT) * ES + c * 16, src + c * 16);
+  }
+}
+
+// staged raw rows -> the packed layout (tokens past cv: the identity step's values)
+template <typename TIN>
+__device__ __forceinline__ void bwd_convert(const BwdParams& p, const BwdSmem& s, int cv, bool with_dout) {
+  const int nth = blockDim.x, tid = threadIdx.x, K = p.K, VT = p.VT;
+  const TIN *q = reinterpret_cast<const TIN*>(s.rq), *k = reinterpret_cast<const TIN*>(s.rk),
+            *b = reinterpret_cast<const TIN*>(s.rb);
+  for (int i = tid; i < BWD_L * K; i += nth) {
+    float4 r = make_float4(1.f, 0.f, 0.f, 0.f);
+    if (i < cv * K) r = make_float4(expf(s.rg[i]), to_f32<TIN>(b[i]), to_f32<TIN>(k[i]), p.scale * to_f32<TIN>(q[i]));
+    s.kr[i] = r;
+  }
+  const TIN *v = reinterpret_cast<const TIN*>(s.rv), *w = reinterpret_cast<const TIN*>(s.rw),
+            *d = reinterpret_cast<const TIN*>(s.rdo);
+  for (int i = tid; i < BWD_L * VT; i += nth) {
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < cv * VT) {
+      r.z = to_f32<TIN>(w[i]);
+      r.w = to_f32<TIN>(v[i]);
+      r.x = r.z * r.w;
+      if (with_dout) r.y = to_f32<TIN>(d[i]);
+    }
+    s.vc[i] = r;
+  }
 }
 
 template <typename TIN>
@@ -87,29 +157,25 @@ __device__ __forceinline__ void bwd_stage(const BwdParams& p, const BwdSmem& s, 
   const int nth = blockDim.x, tid = threadIdx.x, K = p.K, VT = p.VT;
   for (int i = tid; i < BWD_L * K; i += nth) {
     const int tt = i / K, kk = i - tt * K;
-    float qv = 0.f, kv = 0.f, bv = 0.f, gv = 1.f;
+    float4 r = make_float4(1.f, 0.f, 0.f, 0.f);
     if (tt < cv) {
-      qv = vload<TIN>(p.q, bb, kh, t0 + tt, kk);
-      kv = vload<TIN>(p.k, bb, kh, t0 + tt, kk);
-      bv = vload<TIN>(p.b, bb, kh, t0 + tt, kk);
-      gv = expf(vload<float>(p.g, bb, kh, t0 + tt, kk));
+      r.x = expf(vload<float>(p.g, bb, kh, t0 + tt, kk));
+      r.y = vload<TIN>(p.b, bb, kh, t0 + tt, kk);
+      r.z = vload<TIN>(p.k, bb, kh, t0 + tt, kk);
+      r.w = p.scale * vload<TIN>(p.q, bb, kh, t0 + tt, kk);
     }
-    s.q[i] = qv;
-    s.k[i] = kv;
-    s.b[i] = bv;
-    s.gm[i] = gv;
+    s.kr[i] = r;
   }
   for (int i = tid; i < BWD_L * VT; i += nth) {
     const int tt = i / VT, c = i - tt * VT;
-    float vv = 0.f, wv = 0.f, dv = 0.f;
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
     if (tt < cv) {
-      vv = vload<TIN>(p.v, bb, hv, t0 + tt, col0 + c);
-      wv = vload<TIN>(p.w, bb, hv, t0 + tt, col0 + c);
-      if (with_dout) dv = vload<TIN>(p.dout, bb, hv, t0 + tt, col0 + c);
+      r.z = vload<TIN>(p.w, bb, hv, t0 + tt, col0 + c);
+      r.w = vload<TIN>(p.v, bb, hv, t0 + tt, col0 + c);
+      r.x = r.z * r.w;
+      if (with_dout) r.y = vload<TIN>(p.dout, bb, hv, t0 + tt, col0 + c);
     }
-    s.v[i] = vv;
-    s.w[i] = wv;
-    s.dO[i] = dv;
+    s.vc[i] = r;
   }
 }
 
@@ -117,44 +183,51 @@ __device__ __forceinline__ void bwd_stage(const BwdParams& p, const BwdSmem& s, 
 template <int RPL>
 __device__ __forceinline__ void bwd_fwd_step(const BwdSmem& s, int K, int VT, int tt, int lane, int cw,
                                              float (&S)[RPL][BWD_NC], float (&u)[BWD_NC]) {
-  float e[BWD_NC];
+  float e[BWD_NC], kr[RPL];
   #pragma unroll
   for (int c = 0; c < BWD_NC; ++c) e[c] = 0.f;
   #pragma unroll
   for (int r = 0; r < RPL; ++r) {
-    const int kk = lane + 32 * r;
-    const float gr = s.gm[tt * K + kk], bkr = s.b[tt * K + kk] * s.k[tt * K + kk];
+    const float4 x = s.kr[tt * K + lane + 32 * r];
+    const float bkr = x.y * x.z;
+    kr[r] = x.z;
     #pragma unroll
     for (int c = 0; c < BWD_NC; ++c) {
-      S[r][c] *= gr;
+      S[r][c] *= x.x;
       e[c] += bkr * S[r][c];
     }
   }
   #pragma unroll
-  for (int c = 0; c < BWD_NC; ++c) u[c] = s.w[tt * VT + cw + c] * s.v[tt * VT + cw + c] - warp_sum_bwd(e[c]);
+  for (int c = 0; c < BWD_NC; ++c) u[c] = s.vc[tt * VT + cw + c].x - warp_sum_bwd(e[c]);
   #pragma unroll
-  for (int r = 0; r < RPL; ++r) {
-    const float kr = s.k[tt * K + lane + 32 * r];
+  for (int r = 0; r < RPL; ++r)
     #pragma unroll
-    for (int c = 0; c < BWD_NC; ++c) S[r][c] += kr * u[c];
-  }
+    for (int c = 0; c < BWD_NC; ++c) S[r][c] += kr[r] * u[c];
 }
 
-template <typename TIN, int RPL>
+template <typename TIN, int RPL, bool ASYNC>
 __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
-  extern __shared__ __align__(16) float smf[];
+  extern __shared__ __align__(16) float4 smf4[];
   const int K = p.K, VT = p.VT, NCL = p.NCL;
   BwdSmem s;
-  s.q = smf;
-  s.k = s.q + BWD_L * K;
-  s.b = s.k + BWD_L * K;
-  s.gm = s.b + BWD_L * K;
-  s.v = s.gm + BWD_L * K;
-  s.w = s.v + BWD_L * VT;
-  s.dO = s.w + BWD_L * VT;
-  s.dv = s.dO + BWD_L * VT;
+  s.kr = smf4;
+  s.vc = s.kr + BWD_L * K;
+  s.red = s.vc + BWD_L * VT;
+  s.slot = s.red + 2 * BWD_L * K;
+  s.dv = reinterpret_cast<float*>(s.slot + 2 * p.NW * K);
   s.dw = s.dv + BWD_L * VT;
-  s.red = s.dw + BWD_L * VT;
+  {
+    constexpr int ES = (int)sizeof(TIN);
+    unsigned char* raw = reinterpret_cast<unsigned char*>(s.dw + BWD_L * VT);  // 16-byte aligned: L VT = 8 VT floats
+    s.rg = reinterpret_cast<float*>(raw);
+    s.rq = raw + BWD_L * K * 4;
+    s.rk = s.rq + BWD_L * K * ES;
+    s.rb = s.rk + BWD_L * K * ES;
+    s.rv = s.rb + BWD_L * K * ES;
+    s.rw = s.rv + BWD_L * VT * ES;
+    s.rdo = s.rw + BWD_L * VT * ES;
+    s.ck = reinterpret_cast<float*>(s.rdo + BWD_L * VT * ES);
+  }
 
   cg::cluster_group cl = cg::this_cluster();
   const int rank = (int)cl.block_rank();
@@ -165,10 +238,10 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
   const int64_t chain = (int64_t)bb * p.HV + hv;
   const int64_t KV = (int64_t)K * p.V;
 
-  // this thread's checkpoint slot of sub-chunk n: 256 contiguous bytes per warp and row group
-  auto ck = [&](int n, int r) -> float2* {
-    const int64_t base = (((chain * p.NS + n) * NCL + rank) * p.NW + warp) * (int64_t)RPL + r;
-    return reinterpret_cast<float2*>(p.ckpt + (base * 32 + lane) * BWD_NC);
+  // this thread's checkpoint of sub-chunk n: RPL float2, contiguous
+  auto ck = [&](int n) -> float2* {
+    const int64_t base = ((chain * p.NS + n) * NCL + rank) * (int64_t)nth + tid;
+    return reinterpret_cast<float2*>(p.ckpt + base * (RPL * BWD_NC));
   };
 
   // ---- forward pass: the state at every sub-chunk start into the workspace ----
@@ -178,19 +251,34 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
     #pragma unroll
     for (int c = 0; c < BWD_NC; ++c)
       S[r][c] = p.h0 ? p.h0[chain * KV + (int64_t)(lane + 32 * r) * p.V + col0 + cw + c] : 0.f;
+  if (ASYNC && p.NS > 1) {
+    bwd_issue<TIN>(p, s, bb, hv, kh, col0, 0, BWD_L, false);
+    cp_async_commit();
+  }
   for (int n = 0; n < p.NS; ++n) {
     const int t0 = n * BWD_L, cv = min(BWD_L, p.T - t0);
     #pragma unroll
-    for (int r = 0; r < RPL; ++r) *ck(n, r) = make_float2(S[r][0], S[r][1]);
+    for (int r = 0; r < RPL; ++r) ck(n)[r] = make_float2(S[r][0], S[r][1]);
     if (n == p.NS - 1) break;  // the last sub-chunk is replayed from its checkpoint
-    bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, cv, false);
-    __syncthreads();
+    if (ASYNC) {
+      cp_async_wait<0>();
+      __syncthreads();  // every thread's copies landed; the previous sub-chunk's steps are done
+      bwd_convert<TIN>(p, s, cv, false);
+      __syncthreads();
+      if (n + 1 < p.NS - 1) {
+        bwd_issue<TIN>(p, s, bb, hv, kh, col0, t0 + BWD_L, BWD_L, false);
+        cp_async_commit();
+      }
+    } else {
+      bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, cv, false);
+      __syncthreads();
+    }
     #pragma unroll
     for (int tt = 0; tt < BWD_L; ++tt) {
       float u[BWD_NC];
       bwd_fwd_step<RPL>(s, K, VT, tt, lane, cw, S, u);
     }
-    __syncthreads();
+    if (!ASYNC) __syncthreads();
   }
 
   // ---- reverse pass ----
@@ -200,21 +288,49 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
     #pragma unroll
     for (int c = 0; c < BWD_NC; ++c)
       dS[r][c] = p.dht ? p.dht[chain * KV + (int64_t)(lane + 32 * r) * p.V + col0 + cw + c] : 0.f;
-  for (int i = tid; i < 2 * BWD_L * 4 * K; i += nth) s.red[i] = 0.f;
 
+  // this thread's checkpoint and the inputs of sub-chunk n into the staging buffer
+  auto issue_rev = [&](int n, bool with_ck) {
+    if (with_ck) {
+      const float2* src = ck(n);
+      #pragma unroll
+      for (int r = 0; r < RPL; ++r) cp_async8(s.ck + (tid * RPL + r) * BWD_NC, src + r);
+    }
+    bwd_issue<TIN>(p, s, bb, hv, kh, col0, n * BWD_L, min(BWD_L, p.T - n * BWD_L), true);
+    cp_async_commit();
+  };
+  if (ASYNC) {
+    __syncthreads();  // the forward pass's last conversion is read
+    issue_rev(p.NS - 1, false);  // the last sub-chunk's start state is still in registers
+  }
   for (int it = 0; it < p.NS; ++it) {
     const int n = p.NS - 1 - it, par = it & 1;
     const int t0 = n * BWD_L, cv = min(BWD_L, p.T - t0);
-    float* red = s.red + par * BWD_L * 4 * K;
-    #pragma unroll
-    for (int r = 0; r < RPL; ++r) {
-      const float2 v = *ck(n, r);
-      S[r][0] = v.x;
-      S[r][1] = v.y;
+    float4* red = s.red + par * BWD_L * K;
+    if (ASYNC) {
+      cp_async_wait<0>();
+      if (it > 0) {
+        #pragma unroll
+        for (int r = 0; r < RPL; ++r) {
+          S[r][0] = s.ck[(tid * RPL + r) * BWD_NC];
+          S[r][1] = s.ck[(tid * RPL + r) * BWD_NC + 1];
+        }
+      }
+      __syncthreads();  // every thread's copies landed; the previous reduction read the packed rows and dv / dw
+      bwd_convert<TIN>(p, s, cv, true);
+      __syncthreads();
+      if (n > 0) issue_rev(n - 1, true);
+    } else {
+      #pragma unroll
+      for (int r = 0; r < RPL; ++r) {
+        const float2 v = ck(n)[r];
+        S[r][0] = v.x;
+        S[r][1] = v.y;
+      }
+      __syncthreads();  // the previous reduction read the staged rows and dv / dw
+      bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, cv, true);
+      __syncthreads();
     }
-    __syncthreads();  // the previous reduction read the staged k / b / dv / dw
-    bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, cv, true);
-    __syncthreads();
 
     // replay: each token's incoming state and u, in registers
     float H[BWD_L][RPL][BWD_NC], U[BWD_L][BWD_NC];
@@ -230,24 +346,26 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
     // adjoint, last token first (tokens past the end have dO = 0, k = b = 0, gamma = 1: identity steps)
     #pragma unroll
     for (int tt = BWD_L - 1; tt >= 0; --tt) {
-      float dO[BWD_NC], du[BWD_NC];
+      float4 col[BWD_NC];
+      float du[BWD_NC];
       #pragma unroll
       for (int c = 0; c < BWD_NC; ++c) {
-        dO[c] = s.dO[tt * VT + cw + c];
+        col[c] = s.vc[tt * VT + cw + c];
         du[c] = 0.f;
       }
+      float4 row[RPL];
       float pq[RPL], pk[RPL];
       #pragma unroll
       for (int r = 0; r < RPL; ++r) {
-        const int kk = lane + 32 * r;
-        const float gr = s.gm[tt * K + kk], kr = s.k[tt * K + kk], qs = p.scale * s.q[tt * K + kk];
+        row[r] = s.kr[tt * K + lane + 32 * r];
+        const float gr = row[r].x, kr = row[r].z, qs = row[r].w;
         pq[r] = 0.f;
         pk[r] = 0.f;
         #pragma unroll
         for (int c = 0; c < BWD_NC; ++c) {
           const float st = gr * H[tt][r][c] + kr * U[tt][c];
-          dS[r][c] += qs * dO[c];
-          pq[r] += st * dO[c];
+          dS[r][c] += qs * col[c].y;
+          pq[r] += st * col[c].y;
           du[c] += dS[r][c] * kr;
           pk[r] += dS[r][c] * U[tt][c];
         }
@@ -256,8 +374,7 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
       for (int c = 0; c < BWD_NC; ++c) du[c] = warp_sum_bwd(du[c]);
       #pragma unroll
       for (int r = 0; r < RPL; ++r) {
-        const int kk = lane + 32 * r;
-        const float gr = s.gm[tt * K + kk], bkr = s.b[tt * K + kk] * s.k[tt * K + kk];
+        const float gr = row[r].x, bkr = row[r].y * row[r].z;
         float pb = 0.f, pg = 0.f;
         #pragma unroll
         for (int c = 0; c < BWD_NC; ++c) {
@@ -267,40 +384,49 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
           pg += dsa * sa;
           dS[r][c] = gr * dsa;
         }
-        float* rt = red + tt * 4 * K + kk;
-        red_shared_add(rt, p.scale * pq[r]);
-        red_shared_add(rt + K, pk[r]);
-        red_shared_add(rt + 2 * K, pb);
-        red_shared_add(rt + 3 * K, pg);
+        s.slot[((tt & 1) * p.NW + warp) * K + lane + 32 * r] = make_float4(p.scale * pq[r], pk[r], pb, pg);
       }
       if (lane == 0) {
         #pragma unroll
         for (int c = 0; c < BWD_NC; ++c) {
-          s.dv[tt * VT + cw + c] = du[c] * s.w[tt * VT + cw + c];
-          s.dw[tt * VT + cw + c] = du[c] * s.v[tt * VT + cw + c];
+          s.dv[tt * VT + cw + c] = du[c] * col[c].z;
+          s.dw[tt * VT + cw + c] = du[c] * col[c].w;
         }
+      }
+      // the warps' partials of this token summed into the sub-chunk buffer (the slot of this token parity is
+      // rewritten two tokens later, after the next token's barrier, by which time every thread has read it)
+      __syncthreads();
+      const float4* sl = s.slot + (tt & 1) * p.NW * K;
+      for (int i = tid; i < K; i += nth) {
+        float4 acc = sl[i];
+        for (int x = 1; x < p.NW; ++x) {
+          const float4 y = sl[x * K + i];
+          acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
+        }
+        red[tt * K + i] = acc;
       }
     }
 
-    // every CTA of the chain has added its partials for this sub-chunk (and finished reading the other buffer)
+    // every CTA of the chain has written its buffer for this sub-chunk (and finished reading the other one,
+    // which the next sub-chunk rewrites)
     __syncthreads();
     cl.sync();
-    float* other = s.red + (par ^ 1) * BWD_L * 4 * K;
-    for (int i = tid; i < BWD_L * 4 * K; i += nth) other[i] = 0.f;
-    for (int i = rank * nth + tid; i < BWD_L * K; i += NCL * nth) {
+    const int per = (cv * K + NCL - 1) / NCL;
+    for (int i = rank * per + tid; i < min((rank + 1) * per, cv * K); i += nth) {
       const int tt = i / K, kk = i - tt * K;
-      if (tt >= cv) continue;
-      float a[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int x = 0; x < NCL; ++x) {
-        const float* pr = cl.map_shared_rank(red, x) + tt * 4 * K + kk;
-        #pragma unroll
-        for (int j = 0; j < 4; ++j) a[j] += pr[j * K];
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      #pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        if (x < NCL) {
+          const float4 y = cl.map_shared_rank(red, x)[i];
+          a.x += y.x; a.y += y.y; a.z += y.z; a.w += y.w;
+        }
       }
-      const float bv = s.b[tt * K + kk], kv = s.k[tt * K + kk];
-      vstore<float>(p.dq, bb, hv, t0 + tt, kk, a[0]);
-      vstore<float>(p.dk, bb, hv, t0 + tt, kk, a[1] + a[2] * bv);
-      vstore<float>(p.db, bb, hv, t0 + tt, kk, a[2] * kv);
-      vstore<float>(p.dg, bb, hv, t0 + tt, kk, a[3]);
+      const float4 rw = s.kr[i];
+      vstore<float>(p.dq, bb, hv, t0 + tt, kk, a.x);
+      vstore<float>(p.dk, bb, hv, t0 + tt, kk, a.y + a.z * rw.y);
+      vstore<float>(p.db, bb, hv, t0 + tt, kk, a.z * rw.z);
+      vstore<float>(p.dg, bb, hv, t0 + tt, kk, a.w);
     }
     for (int i = tid; i < cv * VT; i += nth) {
       const int tt = i / VT, c = i - tt * VT;
@@ -367,15 +493,30 @@ int launch_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* ws, size_t ws_b
   p.h0 = a->state_in; p.dht = a->d_state_out; p.dh0 = a->d_state_in;
   p.ckpt = static_cast<float*>(ws);
 
-  void (*fn)(const BwdParams) = nullptr;
   const bool bf = a->dtype == GDN2_DTYPE_BF16;
-  switch (K / 32) {
-    case 1: fn = bf ? k_recurrent_bwd<__nv_bfloat16, 1> : k_recurrent_bwd<float, 1>; break;
-    case 2: fn = bf ? k_recurrent_bwd<__nv_bfloat16, 2> : k_recurrent_bwd<float, 2>; break;
-    case 3: fn = bf ? k_recurrent_bwd<__nv_bfloat16, 3> : k_recurrent_bwd<float, 3>; break;
-    default: fn = bf ? k_recurrent_bwd<__nv_bfloat16, 4> : k_recurrent_bwd<float, 4>; break;
-  }
-  const size_t smem = bwd_smem_floats(K, p.VT) * sizeof(float);
+  const int esz = bf ? 2 : 4;
+  // cp.async staging needs every input row (and the slice's first column) on a 16-byte boundary
+  auto al = [](const gdn2_view& v, int es) {
+    return ((uintptr_t)v.data % 16) == 0 && (v.stride0 * es) % 16 == 0 && (v.stride1 * es) % 16 == 0 &&
+           (v.stride2 * es) % 16 == 0;
+  };
+  const bool async = al(a->q, esz) && al(a->k, esz) && al(a->b, esz) && al(a->g, 4) && al(a->v, esz) &&
+                     al(a->w, esz) && al(a->d_out, esz) && (p.VT * esz) % 16 == 0;
+  void (*fn)(const BwdParams) = nullptr;
+  auto pick = [&](auto tin) {
+    using TIN = decltype(tin);
+    switch (K / 32) {
+      case 1: fn = async ? k_recurrent_bwd<TIN, 1, true> : k_recurrent_bwd<TIN, 1, false>; break;
+      case 2: fn = async ? k_recurrent_bwd<TIN, 2, true> : k_recurrent_bwd<TIN, 2, false>; break;
+      case 3: fn = async ? k_recurrent_bwd<TIN, 3, true> : k_recurrent_bwd<TIN, 3, false>; break;
+      default: fn = async ? k_recurrent_bwd<TIN, 4, true> : k_recurrent_bwd<TIN, 4, false>; break;
+    }
+  };
+  if (bf)
+    pick(__nv_bfloat16());
+  else
+    pick(0.f);
+  const size_t smem = bwd_smem_bytes(K, p.VT, p.NW, K / 32, esz);
   cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_bwd: smem attribute");
   cudaLaunchConfig_t cfg = {};

@@ -128,3 +128,24 @@ def test_gated_delta_core_autograd(T):
     order = ["dq", "dk", "dv", "dg", "db", "dw", "dh0"]
     for name, x, r in zip(order, got, ref):
         _check(x.cpu().numpy(), r, torch.float32, f"{name} T={T}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_recurrent_backward_unaligned_views(dtype):
+    """Inputs that are column slices at an odd element offset (not on a 16-byte
+    boundary): the kernel reads them synchronously instead of by cp.async."""
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V = 1, 2, 45, 64, 32
+    dev, dout, h0, dst = _case(B, HV, HV, T, K, V, dtype, seed=17)
+    wide = {}
+    for n, t in dev.items():
+        w = torch.zeros(*t.shape[:3], t.shape[3] + 3, dtype=t.dtype, device=DEV)
+        w[..., 1:1 + t.shape[3]] = t
+        wide[n] = w[..., 1:1 + t.shape[3]]
+    assert wide["q"].data_ptr() % 16 != 0
+    got = bg.recurrent_backward(wide["q"], wide["k"], wide["v"], wide["g"], wide["b"], wide["w"], h0, 0.125, dout,
+                                dst)
+    ref = _oracle(dev, dout, h0, dst, 0.125, HV)
+    for name, x, r in zip(NAMES, got, ref):
+        _check(x.cpu().numpy(), r, dtype, f"{name} unaligned")
