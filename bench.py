@@ -16,7 +16,8 @@ Printed (rank 0, one JSON line): tokens/s of the device-resident core
 the roofline of the dominant kernel, the decode step of BASELINE config 3
 (B = 256, one token, state [256,16,128,128] f32) as `decode`, the config-2
 layer (`layer`: projections + core + o_proj, against the tensor-core peak),
-the config-2 core in f32 (`f32`), BASELINE configs 4 and 5 (`other_configs`:
+the config-2 core in f32 (`f32`), the core's backward over a config-2 batch
+(`backward`), BASELINE configs 4 and 5 (`other_configs`:
 their chunk cores, and config 5 as its head-sharded layer over the N ranks),
 the CPU baseline (numpy restatement of the crate's tensor path on the host
 cores) and SM clocks sampled during the timed region.
@@ -325,6 +326,7 @@ def run_ours(args):
     decode = run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world)
     # ---- whole layer forward_train (projections on cuBLAS + the core) ----
     layer = run_layer(torch, bg, dev, stream, args, max_over_ranks, world) if not args.core_only else None
+    backward = run_backward(torch, bg, dev, max_over_ranks, rank) if not args.core_only else None
     layer_fast = (run_layer(torch, bg, dev, stream, args, max_over_ranks, world, precision="bf16")
                   if not args.core_only else None)
     # ---- N > 1: one config-2 layer split by heads, o_proj all-reduce timed apart ----
@@ -381,6 +383,7 @@ def run_ours(args):
             "layer": layer,
             "layer_bf16_intermediates": layer_fast,
             "layer_head_sharded": layer_tp,
+            "backward": backward,
             "other_configs": others,
             "gpu_launches": 2 * args.steps,
             "clocks": head["clocks"],
@@ -633,6 +636,44 @@ def run_core_cfg(torch, bg, ops, dev, stream, c, name, max_over_ranks, world, se
             "path": path,
             "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": alg / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}}
+
+
+def run_backward(torch, bg, dev, max_over_ranks, rank):
+    """The core's backward (gdn2_recurrent_bwd) over one config-2 batch per rank: B = 8, HV = 16, T = 4096,
+    K = V = 128, bf16 inputs and output gradient, an initial state, f32 gradients of q, k, v, g, b, w and the
+    state.  Arithmetic: per token and head the kernel runs two forward steps (5 K V flops each: decay, erase
+    product, rank-1 update) and one adjoint step (19 K V flops), 29 K V in all, on the f32 CUDA cores."""
+    c = CFG2
+    B, HV, T, K, V = c["B"], c["HV"], c["T"], c["K"], c["V"]
+    gen = torch.Generator(device=dev).manual_seed(6000 + rank)
+    rn = lambda *s: torch.randn(*s, generator=gen, device=dev)
+    ru = lambda *s: torch.rand(*s, generator=gen, device=dev)
+    bf = torch.bfloat16
+    q = torch.nn.functional.normalize(rn(B, HV, T, K), dim=-1).to(bf)
+    k = torch.nn.functional.normalize(rn(B, HV, T, K), dim=-1).to(bf)
+    v, w, b = rn(B, HV, T, V).to(bf), ru(B, HV, T, V).to(bf), ru(B, HV, T, K).to(bf)
+    g = -0.14 * ru(B, HV, T, K) - 0.01
+    dout, h0 = rn(B, HV, T, V).to(bf), 0.1 * rn(B, HV, K, V)
+    run = lambda: bg.recurrent_backward(q, k, v, g, b, w, h0, K ** -0.5, dout, None)
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 3
+    e0.record(st)
+    for _ in range(n):
+        run()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    flops = 29.0 * K * V * B * HV * T
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    peak = sms * 128 * 2 * 1.965e9 / 1e12  # f32 FMA lanes x 2 flops x max SM clock (nominal, not measured)
+    return {"workload": f"core backward, config 2 per rank: B={B}, HV={HV}, T={T}, K=V={K}, bf16 inputs, "
+                        "f32 gradients", "ms": round(ms, 3), "tokens_per_s": B * T / (ms / 1e3),
+            "tflops_f32": round(flops / (ms / 1e3) / 1e12, 2), "f32_simt_peak_tflops_nominal": round(peak, 1),
+            "frac_of_nominal_f32": round(flops / (ms / 1e3) / 1e12 / peak, 3)}
 
 
 def run_decode(torch, bg, ops, dev, stream, args, rank, max_over_ranks, world):
