@@ -28,10 +28,11 @@
 // which form one thread-block cluster, sum each other's buffers through
 // distributed shared memory and write dq, dk, db, dg once.
 //
-// States for the reverse pass.  A forward pass over the sequence stores the
-// state at every 8th token boundary in the workspace (each thread its own
-// 2 x RPL values, contiguous, so a warp stores one contiguous block).  The
-// reverse pass walks the 8-token sub-chunks from the last: it reloads the
+// States for the reverse pass.  A forward pass over the sequence (its own
+// launch, k_recurrent_bwd_ckpt, at twice the occupancy) stores the state at
+// every 8th token boundary in the workspace (each thread its own 2 x RPL
+// values, contiguous, so a warp stores one contiguous block).  The reverse
+// pass walks the 8-token sub-chunks from the last: it reloads the
 // sub-chunk's start state, replays the 8 tokens keeping each token's
 // incoming state in registers, then runs the adjoint over them.  Work per
 // token is three forward steps and one adjoint step on the slice; the
@@ -205,6 +206,83 @@ __device__ __forceinline__ void bwd_fwd_step(const BwdSmem& s, int K, int VT, in
     for (int c = 0; c < BWD_NC; ++c) S[r][c] += kr[r] * u[c];
 }
 
+// this thread's checkpoint of sub-chunk n (RPL float2, contiguous; the same thread of the same CTA position in
+// both kernels)
+template <int RPL>
+__device__ __forceinline__ float2* bwd_ckpt_ptr(const BwdParams& p, int64_t chain, int n, int rank) {
+  const int64_t base = ((chain * p.NS + n) * p.NCL + rank) * (int64_t)blockDim.x + threadIdx.x;
+  return reinterpret_cast<float2*>(p.ckpt + base * (RPL * BWD_NC));
+}
+
+// The forward pass: the state at every sub-chunk start into the workspace.  Its own launch (no register
+// history, no cluster), so that more CTAs share an SM than the reverse pass allows.
+template <typename TIN, int RPL, bool ASYNC>
+__global__ void __launch_bounds__(512, 2) k_recurrent_bwd_ckpt(const BwdParams p) {
+  extern __shared__ __align__(16) float4 smf4[];
+  const int K = p.K, VT = p.VT;
+  BwdSmem s;
+  s.kr = smf4;
+  s.vc = s.kr + BWD_L * K;
+  {
+    constexpr int ES = (int)sizeof(TIN);
+    unsigned char* raw = reinterpret_cast<unsigned char*>(s.vc + BWD_L * VT);
+    s.rg = reinterpret_cast<float*>(raw);
+    s.rq = raw + BWD_L * K * 4;
+    s.rk = s.rq + BWD_L * K * ES;
+    s.rb = s.rk + BWD_L * K * ES;
+    s.rv = s.rb + BWD_L * K * ES;
+    s.rw = s.rv + BWD_L * VT * ES;
+    s.rdo = s.rw + BWD_L * VT * ES;
+  }
+  const int rank = blockIdx.x, hv = blockIdx.y, bb = blockIdx.z, kh = hv / p.rep;
+  const int col0 = rank * VT;
+  const int lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) * BWD_NC;
+  const int64_t chain = (int64_t)bb * p.HV + hv;
+  const int64_t KV = (int64_t)K * p.V;
+
+  float S[RPL][BWD_NC];
+  #pragma unroll
+  for (int r = 0; r < RPL; ++r)
+    #pragma unroll
+    for (int c = 0; c < BWD_NC; ++c)
+      S[r][c] = p.h0 ? p.h0[chain * KV + (int64_t)(lane + 32 * r) * p.V + col0 + cw + c] : 0.f;
+  if (ASYNC && p.NS > 1) {
+    bwd_issue<TIN>(p, s, bb, hv, kh, col0, 0, BWD_L, false);
+    cp_async_commit();
+  }
+  for (int n = 0; n < p.NS; ++n) {
+    const int t0 = n * BWD_L;
+    float2* ck = bwd_ckpt_ptr<RPL>(p, chain, n, rank);
+    #pragma unroll
+    for (int r = 0; r < RPL; ++r) ck[r] = make_float2(S[r][0], S[r][1]);
+    if (n == p.NS - 1) break;  // the last sub-chunk's steps are not needed: it is replayed from its start
+    if (ASYNC) {
+      cp_async_wait<0>();
+      __syncthreads();  // every thread's copies landed; the previous sub-chunk's steps are done
+      bwd_convert<TIN>(p, s, BWD_L, false);
+      __syncthreads();
+      if (n + 1 < p.NS - 1) {
+        bwd_issue<TIN>(p, s, bb, hv, kh, col0, t0 + BWD_L, BWD_L, false);
+        cp_async_commit();
+      }
+    } else {
+      bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, BWD_L, false);
+      __syncthreads();
+    }
+    #pragma unroll
+    for (int tt = 0; tt < BWD_L; ++tt) {
+      float u[BWD_NC];
+      bwd_fwd_step<RPL>(s, K, VT, tt, lane, cw, S, u);
+    }
+    if (!ASYNC) __syncthreads();
+  }
+}
+
+__host__ __device__ inline size_t bwd_ckpt_smem_bytes(int K, int VT, int esz) {
+  return 16 * ((size_t)BWD_L * K + (size_t)BWD_L * VT) +
+         (size_t)BWD_L * (3 * (size_t)K * esz + 4 * (size_t)K + 3 * (size_t)VT * esz);
+}
+
 template <typename TIN, int RPL, bool ASYNC>
 __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
   extern __shared__ __align__(16) float4 smf4[];
@@ -238,49 +316,10 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
   const int64_t chain = (int64_t)bb * p.HV + hv;
   const int64_t KV = (int64_t)K * p.V;
 
-  // this thread's checkpoint of sub-chunk n: RPL float2, contiguous
-  auto ck = [&](int n) -> float2* {
-    const int64_t base = ((chain * p.NS + n) * NCL + rank) * (int64_t)nth + tid;
-    return reinterpret_cast<float2*>(p.ckpt + base * (RPL * BWD_NC));
-  };
+  // this thread's checkpoint of sub-chunk n, written by k_recurrent_bwd_ckpt
+  auto ck = [&](int n) -> float2* { return bwd_ckpt_ptr<RPL>(p, chain, n, rank); };
 
-  // ---- forward pass: the state at every sub-chunk start into the workspace ----
   float S[RPL][BWD_NC];
-  #pragma unroll
-  for (int r = 0; r < RPL; ++r)
-    #pragma unroll
-    for (int c = 0; c < BWD_NC; ++c)
-      S[r][c] = p.h0 ? p.h0[chain * KV + (int64_t)(lane + 32 * r) * p.V + col0 + cw + c] : 0.f;
-  if (ASYNC && p.NS > 1) {
-    bwd_issue<TIN>(p, s, bb, hv, kh, col0, 0, BWD_L, false);
-    cp_async_commit();
-  }
-  for (int n = 0; n < p.NS; ++n) {
-    const int t0 = n * BWD_L, cv = min(BWD_L, p.T - t0);
-    #pragma unroll
-    for (int r = 0; r < RPL; ++r) ck(n)[r] = make_float2(S[r][0], S[r][1]);
-    if (n == p.NS - 1) break;  // the last sub-chunk is replayed from its checkpoint
-    if (ASYNC) {
-      cp_async_wait<0>();
-      __syncthreads();  // every thread's copies landed; the previous sub-chunk's steps are done
-      bwd_convert<TIN>(p, s, cv, false);
-      __syncthreads();
-      if (n + 1 < p.NS - 1) {
-        bwd_issue<TIN>(p, s, bb, hv, kh, col0, t0 + BWD_L, BWD_L, false);
-        cp_async_commit();
-      }
-    } else {
-      bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, cv, false);
-      __syncthreads();
-    }
-    #pragma unroll
-    for (int tt = 0; tt < BWD_L; ++tt) {
-      float u[BWD_NC];
-      bwd_fwd_step<RPL>(s, K, VT, tt, lane, cw, S, u);
-    }
-    if (!ASYNC) __syncthreads();
-  }
-
   // ---- reverse pass ----
   float dS[RPL][BWD_NC];
   #pragma unroll
@@ -299,22 +338,17 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
     bwd_issue<TIN>(p, s, bb, hv, kh, col0, n * BWD_L, min(BWD_L, p.T - n * BWD_L), true);
     cp_async_commit();
   };
-  if (ASYNC) {
-    __syncthreads();  // the forward pass's last conversion is read
-    issue_rev(p.NS - 1, false);  // the last sub-chunk's start state is still in registers
-  }
+  if (ASYNC) issue_rev(p.NS - 1, true);
   for (int it = 0; it < p.NS; ++it) {
     const int n = p.NS - 1 - it, par = it & 1;
     const int t0 = n * BWD_L, cv = min(BWD_L, p.T - t0);
     float4* red = s.red + par * BWD_L * K;
     if (ASYNC) {
       cp_async_wait<0>();
-      if (it > 0) {
-        #pragma unroll
-        for (int r = 0; r < RPL; ++r) {
-          S[r][0] = s.ck[(tid * RPL + r) * BWD_NC];
-          S[r][1] = s.ck[(tid * RPL + r) * BWD_NC + 1];
-        }
+      #pragma unroll
+      for (int r = 0; r < RPL; ++r) {
+        S[r][0] = s.ck[(tid * RPL + r) * BWD_NC];
+        S[r][1] = s.ck[(tid * RPL + r) * BWD_NC + 1];
       }
       __syncthreads();  // every thread's copies landed; the previous reduction read the packed rows and dv / dw
       bwd_convert<TIN>(p, s, cv, true);
@@ -503,21 +537,32 @@ int launch_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* ws, size_t ws_b
   const bool async = al(a->q, esz) && al(a->k, esz) && al(a->b, esz) && al(a->g, 4) && al(a->v, esz) &&
                      al(a->w, esz) && al(a->d_out, esz) && (p.VT * esz) % 16 == 0;
   void (*fn)(const BwdParams) = nullptr;
+  void (*fck)(const BwdParams) = nullptr;
   auto pick = [&](auto tin) {
     using TIN = decltype(tin);
     switch (K / 32) {
-      case 1: fn = async ? k_recurrent_bwd<TIN, 1, true> : k_recurrent_bwd<TIN, 1, false>; break;
-      case 2: fn = async ? k_recurrent_bwd<TIN, 2, true> : k_recurrent_bwd<TIN, 2, false>; break;
-      case 3: fn = async ? k_recurrent_bwd<TIN, 3, true> : k_recurrent_bwd<TIN, 3, false>; break;
-      default: fn = async ? k_recurrent_bwd<TIN, 4, true> : k_recurrent_bwd<TIN, 4, false>; break;
+      case 1: fn = async ? k_recurrent_bwd<TIN, 1, true> : k_recurrent_bwd<TIN, 1, false>;
+              fck = async ? k_recurrent_bwd_ckpt<TIN, 1, true> : k_recurrent_bwd_ckpt<TIN, 1, false>; break;
+      case 2: fn = async ? k_recurrent_bwd<TIN, 2, true> : k_recurrent_bwd<TIN, 2, false>;
+              fck = async ? k_recurrent_bwd_ckpt<TIN, 2, true> : k_recurrent_bwd_ckpt<TIN, 2, false>; break;
+      case 3: fn = async ? k_recurrent_bwd<TIN, 3, true> : k_recurrent_bwd<TIN, 3, false>;
+              fck = async ? k_recurrent_bwd_ckpt<TIN, 3, true> : k_recurrent_bwd_ckpt<TIN, 3, false>; break;
+      default: fn = async ? k_recurrent_bwd<TIN, 4, true> : k_recurrent_bwd<TIN, 4, false>;
+               fck = async ? k_recurrent_bwd_ckpt<TIN, 4, true> : k_recurrent_bwd_ckpt<TIN, 4, false>; break;
     }
   };
   if (bf)
     pick(__nv_bfloat16());
   else
     pick(0.f);
+  const size_t smem_ck = bwd_ckpt_smem_bytes(K, p.VT, esz);
+  cudaError_t e = cudaFuncSetAttribute((const void*)fck, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_ck);
+  if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_bwd: smem attribute");
+  fck<<<dim3(p.NCL, d.num_v_heads, d.batch), p.NW * 32, smem_ck, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_bwd checkpoint launch");
   const size_t smem = bwd_smem_bytes(K, p.VT, p.NW, K / 32, esz);
-  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "gdn2_recurrent_bwd: smem attribute");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.NCL, d.num_v_heads, d.batch);
