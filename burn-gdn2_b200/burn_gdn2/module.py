@@ -165,6 +165,36 @@ class GatedDeltaNet2:
             W["decay_factors"] = f(self.decay_factors)
         return W
 
+    # -- training (torch autograd; src/module.rs:326-375 under burn autodiff) --
+    def parameters(self) -> dict:
+        """The layer's live weight tensors by constructor name (projections
+        [in, out]); set ``requires_grad`` on them (``requires_grad_``) and call
+        ``forward_train_autograd`` to train."""
+        P = {n: getattr(self, n).weight for n in
+             ("q_proj", "k_proj", "v_proj", "f_proj_0", "f_proj_1", "b_proj", "w_proj", "g_proj_0", "o_proj")}
+        P["g_proj_1_w"], P["g_proj_1_b"] = self.g_proj_1.weight, self.g_proj_1.bias
+        for n, a in (("A_log", "a_log"), ("dt_bias", "dt_bias"), ("o_norm_w", "o_norm_weight"),
+                     ("q_conv_w", "q_conv_w"), ("k_conv_w", "k_conv_w"), ("v_conv_w", "v_conv_w")):
+            P[n] = getattr(self, a)
+        if self.decay_factors is not None:
+            P["decay_factors"] = self.decay_factors
+        return P
+
+    def requires_grad_(self, flag: bool = True):
+        for t in self.parameters().values():
+            t.requires_grad_(flag)
+        return self
+
+    def forward_train_autograd(self, hidden_states):
+        """forward_train as a torch autograd graph (burn_gdn2.training): the
+        same output as ``forward_train``, with gradients for every weight
+        whose ``requires_grad`` is set and for the input.  The recurrence runs
+        on the chunked kernels forward and gdn2_recurrent_bwd backward."""
+        from .training import layer_forward
+
+        self._validate_input(hidden_states)
+        return layer_forward(self.parameters(), self.config, hidden_states.to(self.dtype), self.gva_mode)
+
     # -- helpers -------------------------------------------------------------
     @property
     def _dims(self):
