@@ -17,7 +17,7 @@ the roofline of the dominant kernel, the decode step of BASELINE config 3
 (B = 256, one token, state [256,16,128,128] f32) as `decode`, the config-2
 layer (`layer`: projections + core + o_proj, against the tensor-core peak),
 the config-2 core in f32 (`f32`), the core's backward over a config-2 batch
-(`backward`), BASELINE configs 4 and 5 (`other_configs`:
+(`backward`) and one training step of the config-2 layer (`layer_train_step`), BASELINE configs 4 and 5 (`other_configs`:
 their chunk cores, and config 5 as its head-sharded layer over the N ranks),
 the CPU baseline (numpy restatement of the crate's tensor path on the host
 cores) and SM clocks sampled during the timed region.
@@ -327,6 +327,7 @@ def run_ours(args):
     # ---- whole layer forward_train (projections on cuBLAS + the core) ----
     layer = run_layer(torch, bg, dev, stream, args, max_over_ranks, world) if not args.core_only else None
     backward = run_backward(torch, bg, dev, max_over_ranks, rank) if not args.core_only else None
+    layer_train = run_layer_train(torch, bg, dev, max_over_ranks) if not args.core_only else None
     layer_fast = (run_layer(torch, bg, dev, stream, args, max_over_ranks, world, precision="bf16")
                   if not args.core_only else None)
     # ---- N > 1: one config-2 layer split by heads, o_proj all-reduce timed apart ----
@@ -384,6 +385,7 @@ def run_ours(args):
             "layer_bf16_intermediates": layer_fast,
             "layer_head_sharded": layer_tp,
             "backward": backward,
+            "layer_train_step": layer_train,
             "other_configs": others,
             "gpu_launches": 2 * args.steps,
             "clocks": head["clocks"],
@@ -438,6 +440,40 @@ def run_layer(torch, bg, dev, stream, args, max_over_ranks, world, precision="f3
             "workload": f"GatedDeltaNet2.forward_train, BASELINE config 2 (D=2048, 16x128 heads, B={c['B']}, T=4096, bf16)",
             "tflops": flops / (ms / 1e3) / 1e12, "tc_frac": flops / (ms / 1e3) / (peaks["bf16_tflops"] * 1e12),
             "flops_per_step": flops}
+
+
+def run_layer_train(torch, bg, dev, max_over_ranks):
+    """One training step of the config-2 layer (hidden 2048, 16 x 128 heads, bf16, B = 8, T = 4096):
+    GatedDeltaNet2.forward_train_autograd, a mean-square loss, backward to every weight and the input
+    (torch autograd; the recurrence on the chunked forward and gdn2_recurrent_bwd kernels)."""
+    c = CFG2
+    cfg = bg.Gdn2Config(hidden_size=2048, num_heads=16, head_dim=128, mode=bg.Gdn2Mode.Chunk, chunk_size=64)
+    m = bg.GatedDeltaNet2.new(cfg, device=dev, dtype=torch.bfloat16, seed=0)
+    m.requires_grad_(True)
+    g = torch.Generator(device=dev).manual_seed(12)
+    x = torch.randn(c["B"], c["T"], 2048, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+
+    def step():
+        for t in m.parameters().values():
+            t.grad = None
+        x.grad = None
+        m.forward_train_autograd(x).float().square().mean().backward()
+
+    step()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 2
+    e0.record(st)
+    for _ in range(n):
+        step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / n)
+    m.requires_grad_(False)
+    return {"workload": f"GatedDeltaNet2 training step (forward_train_autograd + backward), BASELINE config 2 "
+                        f"(D=2048, 16x128 heads, B={c['B']}, T=4096, bf16)",
+            "ms_per_step": round(ms, 3), "tokens_per_s": c["B"] * c["T"] / (ms / 1e3)}
 
 
 def run_layer_sharded(torch, bg, dev, stream, max_over_ranks, world):
