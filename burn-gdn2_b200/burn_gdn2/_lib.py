@@ -96,6 +96,7 @@ EXPORTS = (
     "gdn2_last_error", "gdn2_last_cuda_error", "gdn2_abi_version", "gdn2_read_device_errors",
     "gdn2_selftest_umma", "gdn2_chunk_fwd_noalloc", "gdn2_project_activations", "gdn2_selftest_wait",
     "gdn2_set_reserved_sms", "gdn2_recurrent_bwd_workspace_bytes", "gdn2_recurrent_bwd",
+    "gdn2_chunk_trajectory",
 )
 
 
@@ -120,6 +121,8 @@ def _load():
     lib.gdn2_recurrent_bwd_workspace_bytes.restype = sz
     lib.gdn2_recurrent_bwd.argtypes = [P(RecurrentBwdArgs), vp, sz, vp]
     lib.gdn2_recurrent_bwd.restype = ctypes.c_int
+    lib.gdn2_chunk_trajectory.argtypes = [P(RecurrentArgs), i32, vp, View, vp]
+    lib.gdn2_chunk_trajectory.restype = ctypes.c_int
     lib.gdn2_short_conv.argtypes = [i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]
     lib.gdn2_short_conv.restype = ctypes.c_int
     lib.gdn2_rms_norm_gate.argtypes = [P(Dims), i32, View, View, vp, f32, View, vp]

@@ -220,6 +220,31 @@ def recurrent_backward(q, k, v, g, b, w, state, scale, d_out, d_state=None, *, n
     return dq, dk, dv, dg, db, dw, dh0
 
 
+def chunk_trajectory(q, k, v, g, b, w, state, chunk_size, with_v_new=True):
+    """Trajectory export (gdn2_chunk_trajectory; the crate's
+    gdn2_chunk_trajectory_export_kernel, src/kernel/chunk_cube.rs:613-734):
+    the state entering every chunk [B,HV,ceil(T/C),K,V] f32 and v_new per
+    token [B,HV,T,V] f32 (None unless with_v_new), exact f32.  Shapes as
+    fused_recurrent_forward; state None = zeros (not modified)."""
+    _require_cuda(q, k, v, g, b, w)
+    dt = q.dtype if q.dtype in _DT else torch.float32
+    K = q.shape[3]
+    q, k, v, w = (_last_contig(x, dt) for x in (q, k, v, w))
+    b = _last_contig(_expand_k(b, K), dt)
+    g = _last_contig(_expand_k(g, K), torch.float32)
+    B, HV, T, _ = q.shape
+    V = v.shape[3]
+    st = None if state is None else state.to(torch.float32).contiguous()
+    states = torch.empty(B, HV, (T + chunk_size - 1) // chunk_size, K, V, dtype=torch.float32, device=q.device)
+    vnew = torch.empty(B, HV, T, V, dtype=torch.float32, device=q.device) if with_v_new else None
+    a = recurrent_args(q, k, v, g, b, w, st if st is not None else states, vnew, 1.0)
+    a.state = None if st is None else st.data_ptr()
+    a.out = _lib.View()
+    check(LIB.gdn2_chunk_trajectory(ctypes.byref(a), int(chunk_size), ptr(states), view4(vnew),
+                                    stream_handle(q.device)))
+    return states, vnew
+
+
 class GatedDeltaCore(torch.autograd.Function):
     """Differentiable core: forward on the chunked kernels (1) + (2), f32-grade
     (or the recurrent kernel (3) for T <= 64), backward on gdn2_recurrent_bwd.

@@ -35,6 +35,8 @@ int check_cuda(cudaError_t e, const char* where) {
 int launch_recurrent(const gdn2_recurrent_args* a, cudaStream_t stream);
 int launch_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* ws, size_t ws_bytes, cudaStream_t stream);
 size_t recurrent_bwd_workspace_bytes(const gdn2_dims& d);
+int launch_chunk_trajectory(const gdn2_recurrent_args* a, int chunk_size, float* states_out, const gdn2_view& vnew,
+                            cudaStream_t stream);
 unsigned read_device_errors_recurrent();
 unsigned read_device_errors_selftest();
 unsigned read_device_errors_intra_tc();
@@ -362,6 +364,12 @@ int gdn2_selftest_wait(uint32_t spins, int32_t arrive, int32_t* completed) {
 int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, void* stream) {
   if (!a) return set_error(GDN2_EINVAL, "gdn2_recurrent_fwd: null args");
   return launch_recurrent(a, (cudaStream_t)stream);
+}
+
+int gdn2_chunk_trajectory(const gdn2_recurrent_args* a, int32_t chunk_size, float* states_out, gdn2_view v_new_out,
+                          void* stream) {
+  if (!a) return set_error(GDN2_EINVAL, "gdn2_chunk_trajectory: null args");
+  return launch_chunk_trajectory(a, chunk_size, states_out, v_new_out, (cudaStream_t)stream);
 }
 
 size_t gdn2_recurrent_bwd_workspace_bytes(const gdn2_dims* d) { return d ? recurrent_bwd_workspace_bytes(*d) : 0; }

@@ -65,6 +65,11 @@ struct BwdParams {
   const float* dht;              // [B,HV,K,V] or null
   float* dh0;                    // [B,HV,K,V] or null
   float* ckpt;                   // workspace
+  // trajectory export (k_recurrent_bwd_ckpt with EXPORT): the state entering every chunk of `chunk` tokens,
+  // [B,HV,ceil(T/chunk),K,V] f32, and v_new per token (f32 view, p = null: not written)
+  int chunk;
+  float* states_out;
+  DView vnew;
 };
 
 __device__ __forceinline__ float warp_sum_bwd(float x) {
@@ -215,8 +220,10 @@ __device__ __forceinline__ float2* bwd_ckpt_ptr(const BwdParams& p, int64_t chai
 }
 
 // The forward pass: the state at every sub-chunk start into the workspace.  Its own launch (no register
-// history, no cluster), so that more CTAs share an SM than the reverse pass allows.
-template <typename TIN, int RPL, bool ASYNC>
+// history, no cluster), so that more CTAs share an SM than the reverse pass allows.  With EXPORT it is the
+// trajectory export instead: every token is stepped, the state entering each chunk goes to p.states_out in
+// the public [B,HV,NT,K,V] layout and v_new = w v - (b k)^T (e^g S) of every token to p.vnew.
+template <typename TIN, int RPL, bool ASYNC, bool EXPORT>
 __global__ void __launch_bounds__(512, 2) k_recurrent_bwd_ckpt(const BwdParams p) {
   extern __shared__ __align__(16) float4 smf4[];
   const int K = p.K, VT = p.VT;
@@ -246,33 +253,47 @@ __global__ void __launch_bounds__(512, 2) k_recurrent_bwd_ckpt(const BwdParams p
     #pragma unroll
     for (int c = 0; c < BWD_NC; ++c)
       S[r][c] = p.h0 ? p.h0[chain * KV + (int64_t)(lane + 32 * r) * p.V + col0 + cw + c] : 0.f;
-  if (ASYNC && p.NS > 1) {
-    bwd_issue<TIN>(p, s, bb, hv, kh, col0, 0, BWD_L, false);
+  // sub-chunks stepped: all of them for the export, all but the last for the checkpoints (the last is
+  // replayed from its start by the reverse pass)
+  const int nsteps = EXPORT ? p.NS : p.NS - 1;
+  if (ASYNC && nsteps > 0) {
+    bwd_issue<TIN>(p, s, bb, hv, kh, col0, 0, min(BWD_L, p.T), false);
     cp_async_commit();
   }
   for (int n = 0; n < p.NS; ++n) {
-    const int t0 = n * BWD_L;
-    float2* ck = bwd_ckpt_ptr<RPL>(p, chain, n, rank);
-    #pragma unroll
-    for (int r = 0; r < RPL; ++r) ck[r] = make_float2(S[r][0], S[r][1]);
-    if (n == p.NS - 1) break;  // the last sub-chunk's steps are not needed: it is replayed from its start
+    const int t0 = n * BWD_L, cv = min(BWD_L, p.T - t0);
+    if (EXPORT) {
+      if (t0 % p.chunk == 0) {
+        float* so = p.states_out + (chain * ((p.T + p.chunk - 1) / p.chunk) + t0 / p.chunk) * KV + col0 + cw;
+        #pragma unroll
+        for (int r = 0; r < RPL; ++r)
+          *reinterpret_cast<float2*>(so + (int64_t)(lane + 32 * r) * p.V) = make_float2(S[r][0], S[r][1]);
+      }
+    } else {
+      float2* ck = bwd_ckpt_ptr<RPL>(p, chain, n, rank);
+      #pragma unroll
+      for (int r = 0; r < RPL; ++r) ck[r] = make_float2(S[r][0], S[r][1]);
+    }
+    if (n >= nsteps) break;
     if (ASYNC) {
       cp_async_wait<0>();
       __syncthreads();  // every thread's copies landed; the previous sub-chunk's steps are done
-      bwd_convert<TIN>(p, s, BWD_L, false);
+      bwd_convert<TIN>(p, s, cv, false);
       __syncthreads();
-      if (n + 1 < p.NS - 1) {
-        bwd_issue<TIN>(p, s, bb, hv, kh, col0, t0 + BWD_L, BWD_L, false);
+      if (n + 1 < nsteps) {
+        bwd_issue<TIN>(p, s, bb, hv, kh, col0, t0 + BWD_L, min(BWD_L, p.T - t0 - BWD_L), false);
         cp_async_commit();
       }
     } else {
-      bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, BWD_L, false);
+      bwd_stage<TIN>(p, s, bb, hv, kh, col0, t0, cv, false);
       __syncthreads();
     }
     #pragma unroll
     for (int tt = 0; tt < BWD_L; ++tt) {
       float u[BWD_NC];
-      bwd_fwd_step<RPL>(s, K, VT, tt, lane, cw, S, u);
+      bwd_fwd_step<RPL>(s, K, VT, tt, lane, cw, S, u);  // tokens past the end: identity steps
+      if (EXPORT && p.vnew.p && lane < BWD_NC && tt < cv)
+        vstore<float>(p.vnew, bb, hv, t0 + tt, col0 + cw + lane, lane == 0 ? u[0] : u[1]);
     }
     if (!ASYNC) __syncthreads();
   }
@@ -477,6 +498,17 @@ __global__ void __launch_bounds__(512, 1) k_recurrent_bwd(const BwdParams p) {
   cl.sync();  // no CTA leaves while a peer may still read its buffers
 }
 
+// cp.async staging needs every input row (and the slice's first column) on a 16-byte boundary
+static bool view_aligned16(const gdn2_view& v, int es) {
+  return ((uintptr_t)v.data % 16) == 0 && (v.stride0 * es) % 16 == 0 && (v.stride1 * es) % 16 == 0 &&
+         (v.stride2 * es) % 16 == 0;
+}
+static bool bwd_inputs_aligned(const gdn2_view& q, const gdn2_view& k, const gdn2_view& v, const gdn2_view& g,
+                               const gdn2_view& b, const gdn2_view& w, int es, int vt) {
+  return view_aligned16(q, es) && view_aligned16(k, es) && view_aligned16(b, es) && view_aligned16(g, 4) &&
+         view_aligned16(v, es) && view_aligned16(w, es) && (vt * es) % 16 == 0;
+}
+
 static void bwd_shape(int V, int& ncl, int& vt, int& nw) {
   ncl = V / 16 < 8 ? V / 16 : 8;
   vt = V / ncl;
@@ -513,7 +545,7 @@ int launch_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* ws, size_t ws_b
                      ws ? ws_bytes : (size_t)0);
   if ((uintptr_t)ws & 7) return set_error(GDN2_EINVAL, "gdn2_recurrent_bwd: workspace must be 8-byte aligned");
 
-  BwdParams p;
+  BwdParams p = {};
   p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.K = K; p.V = V;
   p.rep = a->key_heads_grouped ? d.num_v_heads / d.num_heads : 1;
   bwd_shape(V, p.NCL, p.VT, p.NW);
@@ -529,26 +561,20 @@ int launch_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* ws, size_t ws_b
 
   const bool bf = a->dtype == GDN2_DTYPE_BF16;
   const int esz = bf ? 2 : 4;
-  // cp.async staging needs every input row (and the slice's first column) on a 16-byte boundary
-  auto al = [](const gdn2_view& v, int es) {
-    return ((uintptr_t)v.data % 16) == 0 && (v.stride0 * es) % 16 == 0 && (v.stride1 * es) % 16 == 0 &&
-           (v.stride2 * es) % 16 == 0;
-  };
-  const bool async = al(a->q, esz) && al(a->k, esz) && al(a->b, esz) && al(a->g, 4) && al(a->v, esz) &&
-                     al(a->w, esz) && al(a->d_out, esz) && (p.VT * esz) % 16 == 0;
+  const bool async = bwd_inputs_aligned(a->q, a->k, a->v, a->g, a->b, a->w, esz, p.VT) && view_aligned16(a->d_out, esz);
   void (*fn)(const BwdParams) = nullptr;
   void (*fck)(const BwdParams) = nullptr;
   auto pick = [&](auto tin) {
     using TIN = decltype(tin);
     switch (K / 32) {
       case 1: fn = async ? k_recurrent_bwd<TIN, 1, true> : k_recurrent_bwd<TIN, 1, false>;
-              fck = async ? k_recurrent_bwd_ckpt<TIN, 1, true> : k_recurrent_bwd_ckpt<TIN, 1, false>; break;
+              fck = async ? k_recurrent_bwd_ckpt<TIN, 1, true, false> : k_recurrent_bwd_ckpt<TIN, 1, false, false>; break;
       case 2: fn = async ? k_recurrent_bwd<TIN, 2, true> : k_recurrent_bwd<TIN, 2, false>;
-              fck = async ? k_recurrent_bwd_ckpt<TIN, 2, true> : k_recurrent_bwd_ckpt<TIN, 2, false>; break;
+              fck = async ? k_recurrent_bwd_ckpt<TIN, 2, true, false> : k_recurrent_bwd_ckpt<TIN, 2, false, false>; break;
       case 3: fn = async ? k_recurrent_bwd<TIN, 3, true> : k_recurrent_bwd<TIN, 3, false>;
-              fck = async ? k_recurrent_bwd_ckpt<TIN, 3, true> : k_recurrent_bwd_ckpt<TIN, 3, false>; break;
+              fck = async ? k_recurrent_bwd_ckpt<TIN, 3, true, false> : k_recurrent_bwd_ckpt<TIN, 3, false, false>; break;
       default: fn = async ? k_recurrent_bwd<TIN, 4, true> : k_recurrent_bwd<TIN, 4, false>;
-               fck = async ? k_recurrent_bwd_ckpt<TIN, 4, true> : k_recurrent_bwd_ckpt<TIN, 4, false>; break;
+               fck = async ? k_recurrent_bwd_ckpt<TIN, 4, true, false> : k_recurrent_bwd_ckpt<TIN, 4, false, false>; break;
     }
   };
   if (bf)
@@ -577,6 +603,64 @@ int launch_recurrent_bwd(const gdn2_recurrent_bwd_args* a, void* ws, size_t ws_b
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return check_cuda(cudaLaunchKernelEx(&cfg, fn, p), "gdn2_recurrent_bwd launch");
+}
+
+int launch_chunk_trajectory(const gdn2_recurrent_args* a, int chunk_size, float* states_out, const gdn2_view& vnew,
+                            cudaStream_t stream) {
+  const gdn2_dims& d = a->dims;
+  if (d.batch <= 0 || d.seq_len <= 0 || d.num_heads <= 0 || d.num_v_heads <= 0 || d.head_k_dim <= 0 ||
+      d.head_v_dim <= 0)
+    return set_error(GDN2_EINVAL, "gdn2_chunk_trajectory: all dims must be > 0");
+  if (d.num_v_heads % d.num_heads)
+    return set_error(GDN2_EINVAL, "gdn2_chunk_trajectory: num_v_heads %d not a multiple of num_heads %d",
+                     d.num_v_heads, d.num_heads);
+  if (a->dtype != GDN2_DTYPE_F32 && a->dtype != GDN2_DTYPE_BF16)
+    return set_error(GDN2_EINVAL, "gdn2_chunk_trajectory: unknown dtype %d", a->dtype);
+  if (a->prologue != 0) return set_error(GDN2_EINVAL, "gdn2_chunk_trajectory: prologue must be 0");
+  if (!a->q.data || !a->k.data || !a->v.data || !a->g.data || !a->b.data || !a->w.data || !states_out)
+    return set_error(GDN2_EINVAL, "gdn2_chunk_trajectory: null tensor pointer");
+  if (chunk_size < BWD_L || chunk_size % BWD_L)
+    return set_error(GDN2_EUNSUPPORTED, "gdn2_chunk_trajectory: chunk_size %d (needs a multiple of %d)", chunk_size,
+                     BWD_L);
+  if ((uintptr_t)states_out % 8) return set_error(GDN2_EINVAL, "gdn2_chunk_trajectory: states_out not 8-byte aligned");
+  const int K = d.head_k_dim, V = d.head_v_dim;
+  if (K % 32 || K > 128)
+    return set_error(GDN2_EUNSUPPORTED, "gdn2_chunk_trajectory: head_k_dim %d (needs a multiple of 32, <= 128)", K);
+  if (V % 16 || V > 256)
+    return set_error(GDN2_EUNSUPPORTED, "gdn2_chunk_trajectory: head_v_dim %d (needs a multiple of 16, <= 256)", V);
+  BwdParams p = {};
+  p.B = d.batch; p.T = d.seq_len; p.HV = d.num_v_heads; p.K = K; p.V = V;
+  p.rep = a->key_heads_grouped ? d.num_v_heads / d.num_heads : 1;
+  bwd_shape(V, p.NCL, p.VT, p.NW);
+  p.NS = (d.seq_len + BWD_L - 1) / BWD_L;
+  p.q = make_dview(a->q); p.k = make_dview(a->k); p.v = make_dview(a->v);
+  p.g = make_dview(a->g); p.b = make_dview(a->b); p.w = make_dview(a->w);
+  p.h0 = a->state;
+  p.chunk = chunk_size;
+  p.states_out = states_out;
+  p.vnew = make_dview(vnew);
+  const bool bf = a->dtype == GDN2_DTYPE_BF16;
+  const int esz = bf ? 2 : 4;
+  const bool async = bwd_inputs_aligned(a->q, a->k, a->v, a->g, a->b, a->w, esz, p.VT);
+  void (*fn)(const BwdParams) = nullptr;
+  auto pick = [&](auto tin) {
+    using TIN = decltype(tin);
+    switch (K / 32) {
+      case 1: fn = async ? k_recurrent_bwd_ckpt<TIN, 1, true, true> : k_recurrent_bwd_ckpt<TIN, 1, false, true>; break;
+      case 2: fn = async ? k_recurrent_bwd_ckpt<TIN, 2, true, true> : k_recurrent_bwd_ckpt<TIN, 2, false, true>; break;
+      case 3: fn = async ? k_recurrent_bwd_ckpt<TIN, 3, true, true> : k_recurrent_bwd_ckpt<TIN, 3, false, true>; break;
+      default: fn = async ? k_recurrent_bwd_ckpt<TIN, 4, true, true> : k_recurrent_bwd_ckpt<TIN, 4, false, true>; break;
+    }
+  };
+  if (bf)
+    pick(__nv_bfloat16());
+  else
+    pick(0.f);
+  const size_t smem = bwd_ckpt_smem_bytes(K, p.VT, esz);
+  cudaError_t e = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return check_cuda(e, "gdn2_chunk_trajectory: smem attribute");
+  fn<<<dim3(p.NCL, d.num_v_heads, d.batch), p.NW * 32, smem, stream>>>(p);
+  return check_cuda(cudaGetLastError(), "gdn2_chunk_trajectory launch");
 }
 
 }  // namespace gdn2

@@ -247,6 +247,17 @@ typedef struct gdn2_recurrent_bwd_args {
   float* d_state_in; /* [B,HV,K,V] f32 or NULL */
 } gdn2_recurrent_bwd_args;
 
+/* Trajectory export for a backward (replaces gdn2_chunk_trajectory_export_kernel,
+ * src/kernel/chunk_cube.rs:613-734): from args->state (the initial state,
+ * NULL = zeros; not modified) the state entering every chunk of chunk_size
+ * tokens, states_out [B, HV, ceil(T / chunk_size), K, V] f32 contiguous,
+ * and v_new = w v - (b k)^T (e^g S) of every token into v_new_out
+ * ([B, HV, T, V] f32 view; data NULL = not written).  Exact f32.  args as
+ * gdn2_recurrent_fwd with prologue = 0 (gate, out, conv and epilogue fields
+ * unused); chunk_size a multiple of 8; K and V as gdn2_recurrent_bwd. */
+GDN2_API int gdn2_chunk_trajectory(const gdn2_recurrent_args* args, int32_t chunk_size, float* states_out,
+                                   gdn2_view v_new_out, void* stream);
+
 GDN2_API size_t gdn2_recurrent_bwd_workspace_bytes(const gdn2_dims* dims);
 GDN2_API int gdn2_recurrent_bwd(const gdn2_recurrent_bwd_args* args, void* workspace, size_t workspace_bytes,
                                 void* stream);

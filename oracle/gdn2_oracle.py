@@ -117,6 +117,27 @@ def fused_recurrent_forward(q, k, v, g, b, w, state, scale):
     return np.stack(outs, axis=2), S
 
 
+def fused_recurrent_trajectory(q, k, v, g, b, w, state, chunk):
+    """What gdn2_chunk_trajectory_export_kernel (src/kernel/chunk_cube.rs:613-734)
+    exports for a backward: the state entering every chunk of `chunk` tokens
+    [B,H,ceil(T/chunk),K,V] and v_new [B,H,T,V].  The crate forms v_new of a
+    chunk as u - w S (its WY factors); per token that is w v - (b k)^T (e^g S),
+    the recurrence of src/kernel/fused_recurrent.rs:36-44, stepped here."""
+    B, H, T, K = q.shape
+    S = state.copy()
+    gam = np.exp(g)
+    states, vnew = [], np.zeros(v.shape, dtype=S.dtype)
+    for t in range(T):
+        if t % chunk == 0:
+            states.append(S.copy())
+        Sa = S * gam[:, :, t, :, None]
+        bk = b[:, :, t] * k[:, :, t]
+        u = w[:, :, t] * v[:, :, t] - (Sa * bk[..., None]).sum(axis=2)
+        vnew[:, :, t] = u
+        S = Sa + k[:, :, t, :, None] * u[:, :, None, :]
+    return np.stack(states, axis=2), vnew
+
+
 def fused_recurrent_backward(q, k, v, g, b, w, state, scale, d_out, d_state=None):
     """Reverse-mode adjoint of fused_recurrent_forward (the recurrence of
     src/kernel/fused_recurrent.rs:11-56, which the crate differentiates by

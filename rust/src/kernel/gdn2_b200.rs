@@ -197,6 +197,8 @@ extern "C" {
         -> i32;
     pub fn gdn2_chunk_fwd_noalloc(args: *const Gdn2ChunkArgs, stream: *mut c_void) -> i32;
     pub fn gdn2_recurrent_fwd(args: *const Gdn2RecurrentArgs, stream: *mut c_void) -> i32;
+    pub fn gdn2_chunk_trajectory(args: *const Gdn2RecurrentArgs, chunk_size: i32, states_out: *mut f32,
+                                 v_new_out: Gdn2View, stream: *mut c_void) -> i32;
     pub fn gdn2_recurrent_bwd_workspace_bytes(dims: *const Gdn2Dims) -> usize;
     pub fn gdn2_recurrent_bwd(args: *const Gdn2RecurrentBwdArgs, workspace: *mut c_void, workspace_bytes: usize,
                               stream: *mut c_void) -> i32;

@@ -264,3 +264,22 @@ def test_recurrent_bwd_argument_errors():
     a.dims = _lib.Dims(1, 20, 1, 1, 128, 128)
     a.dtype = 5
     assert LIB.gdn2_recurrent_bwd(ctypes.byref(a), ctypes.c_void_p(fake), 1 << 30, None) == _lib.GDN2_EINVAL
+
+
+def test_chunk_trajectory_argument_errors():
+    from burn_gdn2 import LIB, _lib
+
+    a = _lib.RecurrentArgs()
+    a.dims = _lib.Dims(1, 20, 1, 1, 128, 128)
+    fake = ctypes.c_void_p(1 << 20)
+    assert LIB.gdn2_chunk_trajectory(None, 64, fake, _lib.View(), None) == _lib.GDN2_EINVAL
+    assert LIB.gdn2_chunk_trajectory(ctypes.byref(a), 64, fake, _lib.View(), None) == _lib.GDN2_EINVAL  # nulls
+    for n in ("q", "k", "v", "g", "b", "w"):
+        setattr(a, n, _lib.View(1 << 20, 0, 0, 0))
+    assert LIB.gdn2_chunk_trajectory(ctypes.byref(a), 64, None, _lib.View(), None) == _lib.GDN2_EINVAL
+    assert LIB.gdn2_chunk_trajectory(ctypes.byref(a), 12, fake, _lib.View(), None) == _lib.GDN2_EUNSUPPORTED
+    a.prologue = 1
+    assert LIB.gdn2_chunk_trajectory(ctypes.byref(a), 64, fake, _lib.View(), None) == _lib.GDN2_EINVAL
+    a.prologue = 0
+    a.dims = _lib.Dims(1, 20, 1, 1, 128, 40)
+    assert LIB.gdn2_chunk_trajectory(ctypes.byref(a), 64, fake, _lib.View(), None) == _lib.GDN2_EUNSUPPORTED

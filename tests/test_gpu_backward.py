@@ -149,3 +149,31 @@ def test_recurrent_backward_unaligned_views(dtype):
     ref = _oracle(dev, dout, h0, dst, 0.125, HV)
     for name, x, r in zip(NAMES, got, ref):
         _check(x.cpu().numpy(), r, dtype, f"{name} unaligned")
+
+
+TRAJ_SHAPES = [
+    # B, HV, T, K, V, chunk
+    (1, 2, 200, 128, 128, 64),   # partial last chunk
+    (2, 1, 37, 64, 48, 16),      # partial last sub-chunk, 3-CTA slices
+    (1, 2, 5, 128, 256, 64),     # shorter than one sub-chunk
+]
+
+
+@pytest.mark.parametrize("shape", TRAJ_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_chunk_trajectory_matches_oracle(shape, dtype):
+    """gdn2_chunk_trajectory: the state entering every chunk and v_new per token
+    against the oracle's restatement of the crate's trajectory export."""
+    import burn_gdn2 as bg
+
+    B, HV, T, K, V, C = shape
+    dev, _, h0, _ = _case(B, HV, HV, T, K, V, dtype, seed=9)
+    states, vnew = bg.chunk_trajectory(dev["q"], dev["k"], dev["v"], dev["g"], dev["b"], dev["w"], h0, C)
+    f = lambda t: t.detach().float().cpu().numpy().astype(np.float64)
+    want_s, want_v = O.fused_recurrent_trajectory(*(f(dev[n]) for n in "qkvgbw"), f(h0), C)
+    assert states.shape == want_s.shape
+    _check(states.cpu().numpy(), want_s, dtype, f"states {shape}")
+    _check(vnew.cpu().numpy(), want_v, dtype, f"v_new {shape}")
+    s2, none = bg.chunk_trajectory(dev["q"], dev["k"], dev["v"], dev["g"], dev["b"], dev["w"], None, C,
+                                   with_v_new=False)
+    assert none is None and float(s2[:, :, 0].abs().max()) == 0.0  # zero initial state

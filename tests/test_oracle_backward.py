@@ -77,3 +77,23 @@ def test_oracle_backward_matches_finite_differences():
             minus[i][idx] -= eps
             fd = (loss(plus) - loss(minus)) / (2 * eps)
             assert abs(fd - grads[i][idx]) <= 1e-6 * max(1.0, abs(fd)), (i, idx, fd, grads[i][idx])
+
+
+def test_oracle_trajectory_matches_forward_prefixes():
+    """The exported chunk-start states are the forward's final states of the
+    prefixes, and v_new reproduces the output: o_t = scale q_t^T S_t with
+    S_t = e^{g_t} S_{t-1} + k_t v_new_t^T."""
+    q, k, v, g, b, w, h0, _, _ = _inputs(7, T=21)
+    C = 8
+    states, vnew = O.fused_recurrent_trajectory(q, k, v, g, b, w, h0, C)
+    assert states.shape[2] == 3
+    assert np.abs(states[:, :, 0] - h0).max() == 0.0
+    for i in range(1, 3):
+        _, S = O.fused_recurrent_forward(q[:, :, :i * C], k[:, :, :i * C], v[:, :, :i * C], g[:, :, :i * C],
+                                         b[:, :, :i * C], w[:, :, :i * C], h0, 1.0)
+        assert np.abs(states[:, :, i] - S).max() <= 1e-12
+    o, _ = O.fused_recurrent_forward(q, k, v, g, b, w, h0, 0.5)
+    S = h0.copy()
+    for t in range(q.shape[2]):
+        S = S * np.exp(g[:, :, t])[..., None] + k[:, :, t, :, None] * vnew[:, :, t, None, :]
+        assert np.abs(0.5 * (S * q[:, :, t, :, None]).sum(2) - o[:, :, t]).max() <= 1e-12
