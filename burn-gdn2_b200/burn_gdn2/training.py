@@ -35,18 +35,19 @@ PARAM_NAMES = ("q_proj", "k_proj", "v_proj", "f_proj_0", "f_proj_1", "b_proj", "
 def short_conv_silu(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """Causal depthwise conv (kernel 4) + SiLU from a zero state: the sequence
     start padded by replicating token 0 three times (src/short_conv.rs:22-65).
-    x [B,T,C]; weight [C,4]."""
-    T = x.shape[1]
-    xp = torch.cat([x[:, :1].expand(-1, SHORT_CONV_CACHE, -1), x], dim=1)
-    out = xp[:, 0:T] * weight[:, 0]
-    for i in range(1, SHORT_CONV_KERNEL):
-        out = out + xp[:, i:i + T] * weight[:, i]
-    return F.silu(out)
+    x [B,T,C]; weight [C,4].  One depthwise conv1d over the replicate-padded
+    [B,C,T+3] sequence (cross-correlation: out[t] = sum_i w[c,i] x_pad[t+i])
+    instead of four shifted products, so forward and backward are a few
+    kernels, not a few dozen."""
+    C = x.shape[2]
+    xp = F.pad(x.transpose(1, 2), (SHORT_CONV_CACHE, 0), mode="replicate")
+    out = F.conv1d(xp, weight.reshape(C, 1, SHORT_CONV_KERNEL), groups=C)
+    return F.silu(out.transpose(1, 2).contiguous())
 
 
 def l2_normalize(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     """x / sqrt(sum x^2 + eps) over the last dim (src/l2norm.rs:13-16)."""
-    return x / torch.sqrt((x * x).sum(-1, keepdim=True) + eps)
+    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
 
 
 def gva_repeat(x: torch.Tensor, rep: int, gva_mode: str) -> torch.Tensor:
